@@ -1,0 +1,428 @@
+#!/usr/bin/env python
+"""Benchmark of the FP8 MoE decode path ("config 2").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode step of one MoE layer for a batch of B tokens (default 1):
+router GEMV, softmax top-8, grouping by expert, fused gate/up+SiLU, down and
+the slot-order combine, with hidden 2048, 128 experts, top-8, expert
+intermediate 768, FP8 e4m3 weights with one fp32 scale per 128x128 block,
+bf16 activations in and out, fp32 accumulation.  Weights are random-init
+N(0, 0.02) quantized on the device; activations N(0, 1) (synthetic data).
+
+L2: each step reads a different one of 8 layer replicas (8 x 604 MB of
+experts), so every step streams its weights from HBM.
+
+value   tokens/s over all ranks, device-timed (CUDA events around a CUDA graph of
+        exactly K steps, inputs resident in HBM).
+e2e     the same through the public C ABI with host buffers: every step copies
+        its input from pinned host memory and its output back, inside the
+        timed region.
+roofline  the dominant kernel (gate/up+SiLU), timed in its own loop of
+        back-to-back launches with CUDA events, against the measured HBM copy
+        bandwidth of MEASURED_PEAKS.json.
+cpu_baseline  the reference's host expert path restated in C++ with AVX-512
+        (oracle/cpu_baseline.cpp) on this box's host cores, rank 0, N=1 only.
+
+With N > 1 (torchrun) every rank runs its own replica of the workload
+(weak scaling, no collective on the data path) and rank 0 prints one line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FP8 expert GEMV HBM GB/s vs B200 peak; MoE decode tokens/s at 1/2/4/8 GPU"
+H, E, K_TOP, I = 2048, 128, 8, 768
+LAYERS = 8
+WORKLOAD = "config2: MoE expert decode, hidden 2048, 128 experts top-8, intermediate 768, FP8 e4m3 128x128 block scales"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="CPU work of the cpu_baseline / reference sample")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    return ap.parse_args()
+
+
+def config_dict(batch):
+    return {"workload": WORKLOAD, "hidden": H, "experts": E, "top_k": K_TOP, "inter": I,
+            "batch_per_gpu": batch, "scale_blocks": "128x128", "layers_rotated": LAYERS,
+            "l2": "inputs larger than L2: each step reads a different layer's experts (8 x 604 MB)"}
+
+
+def load_peaks():
+    for p in (os.path.join(ROOT, "MEASURED_PEAKS.json"),):
+        if os.path.exists(p):
+            d = json.load(open(p))
+            return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """DRAM traffic per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:
+            return None
+    return None
+
+
+# ---- clocks --------------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.result = None
+        if not self.proc:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if sm:
+            self.result = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                           "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- the reference arm (CPU) ---------------------------------------------------------------
+
+def cpu_layer(seed=1):
+    """One config-2 layer in host memory: bf16 router and 128 FP8 records.
+
+    The CPU kernels' time does not depend on the weight values, so the records
+    hold random finite e4m3 codes (bit 3 cleared: never the NaN codes 0x7f /
+    0xff) and block scales of the size N(0, 0.02) weights give (amax / 448).
+    """
+    import numpy as np
+
+    import oracle as O
+    from homelab_b200.records import record_layout
+    geo, stride = record_layout(H, I, 1)
+    rng = np.random.default_rng(seed)
+    recs = (rng.integers(0, 256, size=(E, stride), dtype=np.uint8) & 0xF7).astype(np.uint8)
+    for e in range(E):
+        for (so, n, k) in ((geo.gate_scale, I, H), (geo.up_scale, I, H), (geo.down_scale, H, I)):
+            ns = O.scale_count(n, k, O.SCALE_128X128)
+            recs[e, so:so + 4 * ns] = np.full(ns, 0.08 / 448, dtype=np.float32).view(np.uint8)
+    router = O.bf16_from_f32(rng.standard_normal(E * H, dtype=np.float32) * 0.02).reshape(E, H)
+    ptrs = (C.c_void_p * E)(*[recs[e].ctypes.data for e in range(E)])
+    g = O.Fp8Record()
+    for f, _ in O.Fp8Record._fields_:
+        setattr(g, f, getattr(geo, f))
+    return recs, router, ptrs, g
+
+
+def time_cpu(batch, seconds, threads=None):
+    """Best-of-5 per-step time of the CPU baseline (expert_bench.rs:58-80 method)."""
+    import numpy as np
+
+    import oracle as O
+    recs, router, ptrs, geo = cpu_layer()
+    pool = O.CpuPool(threads or os.cpu_count() or 1)
+    xs = [O.bf16_to_f32(O.normal_bf16(900 + i, batch * H)).reshape(batch, H) for i in range(16)]
+    pool.moe_layer(xs[0], router, K_TOP, ptrs, geo)  # warm-up
+    t0 = time.perf_counter()
+    pool.moe_layer(xs[1], router, K_TOP, ptrs, geo)
+    one = max(time.perf_counter() - t0, 1e-6)
+    reps = max(1, int(seconds / 5 / one))
+    best = float("inf")
+    for r in range(5):
+        t0 = time.perf_counter()
+        for i in range(reps):
+            pool.moe_layer(xs[(r * reps + i) % len(xs)], router, K_TOP, ptrs, geo)
+        best = min(best, (time.perf_counter() - t0) / reps)
+    threads_used = pool.threads
+    pool.close()
+    sample = f"{5 * reps} steps of the config-2 layer at batch {batch} (best of 5 rounds of {reps})"
+    return best, threads_used, sample, 5 * reps
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    steps = args.steps
+    per, threads, sample, n = time_cpu(args.batch, args.cpu_seconds)
+    tok_s = args.batch / per
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args.batch),
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample + "; the reference's host expert path (oominf-cpu) restated in "
+                                             "C++ with AVX-512, FP8 decode, whole layer on the CPU"},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm -------------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    import homelab_b200 as hb
+    from homelab_b200.backend import Gpu
+    from homelab_b200.records import ExpertBank, weight_bytes
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    gpu = Gpu(local_rank)
+    B = args.batch
+
+    # ---- weights: 8 layer replicas ----
+    layers = []
+    gen = torch.Generator(device=dev)
+    for li in range(LAYERS):
+        bank = ExpertBank(E, H, I, hb.SCALE_128X128, dev)
+        bank.fill_random(gpu, seed=1000 * (rank + 1) + li)
+        gen.manual_seed(77 + li)
+        router = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        L = hb.MoeLayer(hidden=H, experts=E, top_k=K_TOP, router_w=router.data_ptr(), recs=bank.addrs.data_ptr())
+        L.geo = bank.geo
+        layers.append((bank, router, L))
+    NX = 64
+    gen.manual_seed(5 + rank)
+    xs = (torch.randn((NX, B, H), generator=gen, device=dev)).to(torch.bfloat16)
+    out = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    ws = gpu.moe_decode_workspace(layers[0][2], B)
+    torch.cuda.synchronize()
+
+    def step(i, x=None, o=None):
+        gpu.moe_decode(layers[i % LAYERS][2], xs[i % NX] if x is None else x, B, out if o is None else o, ws)
+
+    # ---- warm-up (eager) ----
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    assert gpu.device_error() == 0
+
+    K = args.steps
+    G = min(K, 2000)  # steps per captured graph
+    reps, rem = divmod(K, G)
+    s = torch.cuda.Stream(dev)
+
+    def capture(n, e2e=False, xh=None, oh=None, xdev=None):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
+                if e2e:
+                    xdev.copy_(xh[i % NX], non_blocking=True)
+                    step(i, xdev, out)
+                    oh[i % NX].copy_(out, non_blocking=True)
+                else:
+                    step(i)
+        return g
+
+    def timed(graphs_and_counts, sampler_index):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            ev0.record(s)
+            for g, c in graphs_and_counts:
+                for _ in range(c):
+                    g.replay()
+            ev1.record(s)
+        ev1.synchronize()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if dist:
+            tt = torch.tensor([ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        return ms
+
+    g_main = capture(G)
+    g_rem = capture(rem) if rem else None
+    plan = [(g_main, reps)] + ([(g_rem, 1)] if g_rem else [])
+    # untimed graph warm-up, then the timed region under the clock sampler
+    for g, _ in plan:
+        g.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as cs:
+        # keep the GPU busy ~0.5 s before the timed region so the sampler sees load
+        t_end = time.time() + 0.5
+        while time.time() < t_end:
+            g_main.replay()
+            torch.cuda.synchronize()
+        ms = timed(plan, local_rank)
+    clocks = cs.result
+    assert gpu.device_error() == 0
+    tok_s = world * B * K / (ms / 1e3)
+
+    # ---- e2e: host buffers, copies inside the timed region ----
+    xh = xs.cpu().pin_memory()
+    oh = torch.empty((NX, B, H), dtype=torch.bfloat16).pin_memory()
+    xdev = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    ge_main = capture(G, True, xh, oh, xdev)
+    ge_rem = capture(rem, True, xh, oh, xdev) if rem else None
+    eplan = [(ge_main, reps)] + ([(ge_rem, 1)] if ge_rem else [])
+    for g, _ in eplan:
+        g.replay()
+    torch.cuda.synchronize()
+    ms_e2e = timed(eplan, local_rank)
+    e2e = world * B * K / (ms_e2e / 1e3)
+    del ge_main, ge_rem
+
+    # ---- roofline of the dominant kernel: gate/up+SiLU over the 8 experts of a step ----
+    roof = measure_gate_up(gpu, layers, dev, s, B)
+    peak, peak_kind = load_peaks()
+    traffic = load_traffic()
+    step_bytes = E * H * 2 + 8 * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
+
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(config_dict(B), parallelism=f"replicas{world}" if world > 1 else "single"),
+            "roofline": {"bound": "hbm", "achieved": roof["gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": roof["gbs"] / peak, "peak_kind": peak_kind,
+                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                         "kernel": "moe_fp8_kernel<2> (gate/up+SiLU, 8 experts)",
+                         "algorithmic_bytes_per_launch": roof["bytes"], "launch_us": roof["us"]},
+            "step_hbm_gbs": step_bytes * K / (ms / 1e3) / 1e9 / 1.0 if world == 1 else None,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
+                    "d2h_bytes_per_step": B * H * 2},
+            "gpu_launches": 4 * K,
+            "clocks": clocks,
+        }
+    return result, roof
+
+
+def measure_gate_up(gpu, layers, dev, s, B, launches=400):
+    """Average duration of back-to-back gate/up launches over 8 fixed experts per launch."""
+    import numpy as np
+    import torch
+
+    from homelab_b200.records import scale_bytes
+    rng = np.random.default_rng(3)
+    tables = []
+    for li in range(LAYERS):
+        bank = layers[li][0]
+        ids = np.sort(rng.choice(E, 8 * B if 8 * B <= E else E, replace=False)).astype(np.int32)
+        recs = bank.addrs[torch.from_numpy(ids).long().to(dev)].contiguous()
+        off = torch.arange(0, len(ids) + 1, dtype=torch.int32, device=dev)
+        tok = torch.zeros(len(ids), dtype=torch.int32, device=dev)
+        tables.append((recs, off, tok, len(ids)))
+    x = torch.randn((B, H), device=dev).to(torch.bfloat16)
+    h = torch.empty((8 * B, I), dtype=torch.float32, device=dev)
+    geo = layers[0][0].geo
+
+    def one(i):
+        recs, off, tok, n = tables[i % LAYERS]
+        gpu.moe_gate_up(recs, off, tok, n, x, h, geo)
+
+    for i in range(16):
+        one(i)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(launches):
+            one(i)
+    g.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = float("inf")
+    for _ in range(3):
+        with torch.cuda.stream(s):
+            ev0.record(s)
+            g.replay()
+            ev1.record(s)
+        ev1.synchronize()
+        best = min(best, ev0.elapsed_time(ev1) / launches)
+    n_e = tables[0][3]
+    nbytes = n_e * (2 * I * H + 2 * scale_bytes(I, H, geo.layout)) + n_e * H * 2 + n_e * I * 4
+    us = best * 1e3
+    return {"gbs": nbytes / (us * 1e-6) / 1e9, "bytes": nbytes, "us": us}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    result, _ = run_ours(args, rank, world, local_rank)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        per, threads, sample, _ = time_cpu(args.batch, args.cpu_seconds)
+        result["cpu_baseline"] = {"value": args.batch / per, "unit": "tokens/s", "cores": threads,
+                                  "kind": "port",
+                                  "sample": sample + "; oominf-cpu host expert path restated in C++/AVX-512"}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,99 @@
+"""Loads liboomb.so (the sm_100a kernels behind include/oomb.h) and declares its C ABI.
+
+The library is required: there is no CPU fallback.  Importing the package
+without a built library raises, and every entry point fails with
+OOMB_E_DEVICE when no sm_100 GPU is present.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboomb.so")
+
+OK = 0
+E_SHAPE = -1
+E_ALIGN = -2
+E_LAUNCH = -3
+E_TIMEOUT = -4
+E_ARG = -5
+E_DEVICE = -6
+E_WORKSPACE = -7
+
+F32 = 0
+BF16 = 1
+SCALE_1X128 = 0
+SCALE_128X128 = 1
+
+
+class Fp8Record(C.Structure):
+    """oomb_fp8_record: byte offsets of the parts of an FP8 expert record."""
+
+    _fields_ = [
+        ("hidden", C.c_int64), ("inter", C.c_int64),
+        ("gate_weight", C.c_int64), ("gate_scale", C.c_int64),
+        ("up_weight", C.c_int64), ("up_scale", C.c_int64),
+        ("down_weight", C.c_int64), ("down_scale", C.c_int64),
+        ("layout", C.c_int32), ("pad_", C.c_int32),
+    ]
+
+
+class MoeLayer(C.Structure):
+    """oomb_moe_layer: a resident MoE layer for the fused decode path."""
+
+    _fields_ = [
+        ("hidden", C.c_int32), ("experts", C.c_int32), ("top_k", C.c_int32), ("pad_", C.c_int32),
+        ("router_w", C.c_void_p), ("recs", C.c_void_p),
+        ("geo", Fp8Record),
+    ]
+
+
+# (name, restype, argtypes) of every entry point in include/oomb.h
+P, I, Z, S = C.c_void_p, C.c_int, C.c_size_t, C.c_void_p
+SIGNATURES = [
+    ("oomb_version", C.c_char_p, []),
+    ("oomb_status_string", C.c_char_p, [I]),
+    ("oomb_device_error", I, [C.POINTER(C.c_int), I]),
+    ("oomb_gemm_fp8", I, [P, I, P, P, I, P, I, I, I, I, P, Z, S]),
+    ("oomb_router_logits", I, [P, I, P, P, I, I, I, S]),
+    ("oomb_router_topk", I, [P, P, P, I, I, I, S]),
+    ("oomb_moe_gate_up_fp8", I, [P, P, P, I, P, I, P, C.POINTER(Fp8Record), S]),
+    ("oomb_moe_down_fp8", I, [P, P, I, P, P, C.POINTER(Fp8Record), S]),
+    ("oomb_moe_combine_slots", I, [P, P, P, P, I, I, I, I, S]),
+    ("oomb_moe_combine", I, [P, P, P, P, I, I, S]),
+    ("oomb_moe_decode_workspace_bytes", Z, [I, C.POINTER(MoeLayer)]),
+    ("oomb_moe_decode_fp8", I, [C.POINTER(MoeLayer), P, I, I, P, I, P, P, P, Z, S]),
+    ("oomb_workspace_clear", I, [P, Z, S]),
+    ("oomb_quantize_fp8", I, [P, I, I, I, P, P, S]),
+]
+
+_LIB = None
+
+
+def lib() -> C.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m homelab_b200.build` "
+                "(the FP8 path has no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+class OombError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        msg = lib().oomb_status_string(status).decode()
+        super().__init__(f"{what}: {msg} (status {status})" if what else msg)
+
+
+def check(status: int, what: str = "") -> None:
+    if status != OK:
+        raise OombError(status, what)

@@ -1,0 +1,118 @@
+"""The B200 backend's Linear / Experts methods, named and shaped as the engine's traits.
+
+Mirrors crates/oominf-core/src/backend.rs (projects/oom-inference): each method
+takes device buffers (torch CUDA tensors here, plain device addresses at the C
+ABI) and the same dimensions, and raises where the Rust method returns an
+`Err` (shape or alignment checks before launch, `Gpu::check`,
+crates/oominf-cuda/src/lib.rs:157-160).  All work is stream-ordered on the
+current torch stream; nothing synchronises the host.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F32, SCALE_128X128, SCALE_1X128, Fp8Record, MoeLayer, check
+
+__all__ = ["Gpu", "Fp8Record", "MoeLayer", "SCALE_1X128", "SCALE_128X128", "F32", "BF16"]
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise TypeError(f"activations must be float32 or bfloat16, got {t.dtype}")
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    if not t.is_cuda:
+        raise ValueError("buffers must live on the GPU")
+    return t.data_ptr()
+
+
+class Gpu:
+    """One device's backend (the counterpart of `oominf_cuda::Gpu`)."""
+
+    def __init__(self, device: int = 0):
+        self.device = torch.device("cuda", device)
+        self.L = _lib.lib()
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    # ---- Linear -------------------------------------------------------------------------
+    def gemm_fp8(self, x, q, scale, y, t: int, n: int, k: int, layout: int = SCALE_128X128):
+        """y[t, n] = x[t, k] @ w[n, k]^T for FP8 w (Linear::gemm_fp8, backend.rs:199-209)."""
+        check(self.L.oomb_gemm_fp8(_ptr(x), _dtype_code(x), _ptr(q), _ptr(scale), layout, _ptr(y),
+                                   _dtype_code(y), t, n, k, None, 0, self._stream()), "gemm_fp8")
+
+    def router_logits(self, x, w_bf16, logits, t: int, e: int, hidden: int):
+        """logits = x . W^T for the bf16 router (moe.rs:289-298), canonical order."""
+        check(self.L.oomb_router_logits(_ptr(x), _dtype_code(x), _ptr(w_bf16), _ptr(logits), t, e,
+                                        hidden, self._stream()), "router_logits")
+
+    # ---- Experts ------------------------------------------------------------------------
+    def router_topk(self, logits, ids, weights, t: int, e: int, k: int):
+        """Softmax top-k with renormalised weights (Experts::router_topk, backend.rs:816-824)."""
+        check(self.L.oomb_router_topk(_ptr(logits), _ptr(ids), _ptr(weights), t, e, k,
+                                      self._stream()), "router_topk")
+
+    def moe_gate_up(self, recs, off, assign_tok, n_experts: int, x, h, geo: Fp8Record):
+        """h[a] = silu(x[tok(a)] . Wg) * (x[tok(a)] . Wu) (Experts::moe_gate_up, backend.rs:827-836)."""
+        check(self.L.oomb_moe_gate_up_fp8(_ptr(recs), _ptr(off), _ptr(assign_tok), n_experts, _ptr(x),
+                                          _dtype_code(x), _ptr(h), C.byref(geo), self._stream()),
+              "moe_gate_up")
+
+    def moe_down(self, recs, off, n_experts: int, h, y, geo: Fp8Record):
+        """y[a] = h[a] . Wd^T (Experts::moe_down, backend.rs:860-868)."""
+        check(self.L.oomb_moe_down_fp8(_ptr(recs), _ptr(off), n_experts, _ptr(h), _ptr(y), C.byref(geo),
+                                       self._stream()), "moe_down")
+
+    def moe_combine_slots(self, y, slot_assign, w, out, t: int, h: int, k: int):
+        """out[t] = sum_s w[t, s] * y[slot_assign[t, s]] in slot order (backend.rs:898-907)."""
+        check(self.L.oomb_moe_combine_slots(_ptr(y), _ptr(slot_assign), _ptr(w), _ptr(out), _dtype_code(out),
+                                            t, h, k, self._stream()), "moe_combine_slots")
+
+    def moe_combine(self, routed, shared, gate_logit, out, t: int, h: int):
+        """out = routed + sigmoid(gate_logit[t]) * shared (backend.rs:909-917)."""
+        check(self.L.oomb_moe_combine(_ptr(routed), _ptr(shared), _ptr(gate_logit), _ptr(out), t, h,
+                                      self._stream()), "moe_combine")
+
+    # ---- fused decode step --------------------------------------------------------------
+    def moe_decode_workspace(self, layer: MoeLayer, t: int) -> torch.Tensor:
+        n = int(self.L.oomb_moe_decode_workspace_bytes(t, C.byref(layer)))
+        if n == 0:
+            raise ValueError("unsupported MoE layer shape")
+        ws = torch.empty(n, dtype=torch.uint8, device=self.device)
+        check(self.L.oomb_workspace_clear(_ptr(ws), n, self._stream()), "workspace_clear")
+        return ws
+
+    def moe_decode(self, layer: MoeLayer, x, t: int, out, workspace, ids=None, weights=None):
+        """One resident MoE layer step: route, group, gate/up, down, combine."""
+        check(self.L.oomb_moe_decode_fp8(C.byref(layer), _ptr(x), _dtype_code(x), t, _ptr(out),
+                                         _dtype_code(out), _ptr(ids), _ptr(weights), _ptr(workspace),
+                                         workspace.numel(), self._stream()), "moe_decode")
+
+    # ---- weights ------------------------------------------------------------------------
+    def quantize_fp8(self, w_bf16, n: int, k: int, layout: int, q=None, scale=None):
+        """FP8 block quantization on the device (fp8::quantize_blocks, fp8.rs:52-88)."""
+        if q is None:
+            q = torch.empty((n, k), dtype=torch.uint8, device=self.device)
+        if scale is None:
+            rows = (n + 127) // 128 if layout == SCALE_128X128 else n
+            scale = torch.empty((rows, (k + 127) // 128), dtype=torch.float32, device=self.device)
+        check(self.L.oomb_quantize_fp8(_ptr(w_bf16), n, k, layout, _ptr(q), _ptr(scale), self._stream()),
+              "quantize_fp8")
+        return q, scale
+
+    def device_error(self, clear: bool = True) -> int:
+        code = C.c_int(0)
+        self.L.oomb_device_error(C.byref(code), int(clear))
+        return code.value

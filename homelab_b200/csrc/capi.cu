@@ -1,0 +1,520 @@
+// capi.cu - the extern "C" entry points of liboomb.so (declared in include/oomb.h).
+//
+// Shape and alignment checks run on the host before any launch (as Gpu::check,
+// crates/oominf-cuda/src/lib.rs:157-160).  Every kernel is launched with
+// programmatic stream serialization so a kernel's weight stream can start while
+// the previous kernel in the stream drains; each kernel waits
+// (griddepcontrol.wait) before it reads anything its predecessor writes.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/oomb.h"
+#include "gemv_fp8.cuh"
+#include "moe_fp8.cuh"
+#include "quant.cuh"
+#include "route.cuh"
+
+namespace oomb {
+namespace {
+
+// Device error word: bounded waits that run out record a code here.
+__device__ unsigned g_device_error;
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+    bool init = false;
+    bool ok = false;
+    int sms = 0;
+    unsigned* err = nullptr;
+};
+
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+// Per-device state: SM count, error-word address, sm_100 check.
+const DeviceState* device_state() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DeviceState& d = g_dev[dev];
+    if (!d.init) {
+        d.init = true;
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess && prop.major == 10) {
+            d.sms = prop.multiProcessorCount;
+            void* p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess) {
+                d.err = static_cast<unsigned*>(p);
+                d.ok = true;
+            }
+        }
+    }
+    return d.ok ? &d : nullptr;
+}
+
+// Opts a kernel into more than 48 KB of dynamic shared memory, once per
+// (kernel, device): calls made later (for instance during CUDA graph capture)
+// find it done and touch nothing but the stream.
+std::mutex g_attr_mu;
+std::unordered_map<const void*, size_t> g_attr_done[kMaxDevices];
+
+template <typename Kernel>
+bool set_smem(Kernel k, size_t bytes) {
+    if (bytes <= 48 * 1024) return true;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+    const void* key = reinterpret_cast<const void*>(k);
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    auto it = g_attr_done[dev].find(key);
+    if (it != g_attr_done[dev].end() && it->second >= bytes) return true;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) !=
+        cudaSuccess)
+        return false;
+    g_attr_done[dev][key] = bytes;
+    return true;
+}
+
+template <typename Kernel, typename... Args>
+int launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+    if (!set_smem(kernel, smem)) return OOMB_E_LAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- GEMV -------------------------------------------------------------------
+
+template <int T, bool XB>
+int gemv_launch_t(const GemvPlan& pl, GemvParams& gp, cudaStream_t s) {
+    const size_t smem = gemv_smem_bytes(pl.maxg, T);
+    if (pl.maxg == 1)
+        return launch(gemv_fp8_kernel<T, XB, 1>, dim3(pl.grid), dim3(kGemvThreads), smem, s, gp);
+    if constexpr (T == 4)
+        return launch(gemv_fp8_kernel<T, XB, 2>, dim3(pl.grid), dim3(kGemvThreads), smem, s, gp);
+    else
+        return launch(gemv_fp8_kernel<T, XB, 4>, dim3(pl.grid), dim3(kGemvThreads), smem, s, gp);
+}
+
+template <bool XB>
+int gemv_launch(int tpad, const GemvPlan& pl, GemvParams& gp, cudaStream_t s) {
+    switch (tpad) {
+        case 1: return gemv_launch_t<1, XB>(pl, gp, s);
+        case 2: return gemv_launch_t<2, XB>(pl, gp, s);
+        default: return gemv_launch_t<4, XB>(pl, gp, s);
+    }
+}
+
+template <int PARTS, bool XB, bool EARLY>
+int moe_launch(int tb, int grid, const MoeParams& p, cudaStream_t s) {
+    if (tb == 1)
+        return launch(moe_fp8_kernel<PARTS, XB, EARLY, 1>, dim3(grid), dim3(kGemvThreads), moe_smem_bytes(), s, p);
+    return launch(moe_fp8_kernel<PARTS, XB, EARLY, kMoeTB>, dim3(grid), dim3(kGemvThreads), moe_smem_bytes(), s, p);
+}
+
+int moe_grid(const DeviceState* d, int units) {
+    return units < d->sms ? (units > 0 ? units : 1) : d->sms;
+}
+
+}  // namespace
+}  // namespace oomb
+
+using namespace oomb;
+
+extern "C" {
+
+const char* oomb_version(void) { return "oomb 0.1 (sm_100a)"; }
+
+const char* oomb_status_string(int status) {
+    switch (status) {
+        case OOMB_OK: return "ok";
+        case OOMB_E_SHAPE: return "buffer too small or shape unsupported";
+        case OOMB_E_ALIGN: return "pointer or stride not 16-byte aligned";
+        case OOMB_E_LAUNCH: return "CUDA launch failed";
+        case OOMB_E_TIMEOUT: return "a bounded device wait ran out";
+        case OOMB_E_ARG: return "null pointer or bad enum";
+        case OOMB_E_DEVICE: return "no usable sm_100 device";
+        case OOMB_E_WORKSPACE: return "workspace too small";
+        default: return "unknown status";
+    }
+}
+
+int oomb_device_error(int* code, int clear) {
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    unsigned v = 0;
+    if (cudaMemcpy(&v, d->err, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return OOMB_E_LAUNCH;
+    if (code) *code = static_cast<int>(v);
+    if (clear && v) {
+        const unsigned z = 0;
+        if (cudaMemcpy(d->err, &z, sizeof(z), cudaMemcpyHostToDevice) != cudaSuccess) return OOMB_E_LAUNCH;
+    }
+    return v ? OOMB_E_TIMEOUT : OOMB_OK;
+}
+
+int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* scale,
+                  int scale_layout, void* y, int y_dtype, int t, int n, int k, void* workspace,
+                  size_t workspace_bytes, oomb_stream stream) {
+    (void)workspace;
+    (void)workspace_bytes;
+    if (!x || !q || !scale || !y) return OOMB_E_ARG;
+    if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) || (y_dtype != OOMB_F32 && y_dtype != OOMB_BF16) ||
+        (scale_layout != OOMB_SCALE_1X128 && scale_layout != OOMB_SCALE_128X128))
+        return OOMB_E_ARG;
+    if (t < 0 || n <= 0 || k <= 0 || k % 16 != 0) return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(q) || !aligned16(scale) || !aligned16(y)) return OOMB_E_ALIGN;
+    if (t == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    const size_t xs = x_dtype == OOMB_BF16 ? 2 : 4, ys = y_dtype == OOMB_BF16 ? 2 : 4;
+    for (int t0 = 0; t0 < t; t0 += kGemvMaxTokens) {
+        const int tc = t - t0 < kGemvMaxTokens ? t - t0 : kGemvMaxTokens;
+        const int tpad = gemv_tpad(tc);
+        const GemvPlan pl = gemv_plan(n, k, tpad, d->sms);
+        GemvParams gp{};
+        gp.x = static_cast<const uint8_t*>(x) + static_cast<size_t>(t0) * k * xs;
+        gp.q = q;
+        gp.scale = scale;
+        gp.y = static_cast<uint8_t*>(y) + static_cast<size_t>(t0) * n * ys;
+        gp.n = n;
+        gp.k = k;
+        gp.t = tc;
+        gp.layout = scale_layout;
+        gp.y_bf16 = y_dtype == OOMB_BF16;
+        gp.rg = pl.rg;
+        gp.kc = pl.kc;
+        gp.ks = pl.ks;
+        gp.nsl = pl.nsl;
+        gp.groups = pl.groups;
+        gp.err = d->err;
+        const int rc = x_dtype == OOMB_BF16 ? gemv_launch<true>(tpad, pl, gp, stream)
+                                            : gemv_launch<false>(tpad, pl, gp, stream);
+        if (rc) return rc;
+    }
+    return OOMB_OK;
+}
+
+int oomb_router_logits(const void* x, int x_dtype, const uint16_t* w, float* logits, int t, int e,
+                       int hidden, oomb_stream stream) {
+    if (!x || !w || !logits) return OOMB_E_ARG;
+    if (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (t < 0 || e <= 0 || hidden <= 0 || hidden % 8 != 0) return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(w)) return OOMB_E_ALIGN;
+    if (t == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    RouteParams p{};
+    p.x = x;
+    p.x_bf16 = x_dtype == OOMB_BF16;
+    p.w = w;
+    p.logits = logits;
+    p.T = t;
+    p.H = hidden;
+    p.E = e;
+    p.do_logits = 1;
+    p.err = d->err;
+    const int tasks = e * ((t + kRouteTT - 1) / kRouteTT);
+    int grid = (tasks + 7) / 8;
+    if (grid > 4 * d->sms) grid = 4 * d->sms;
+    return p.x_bf16 ? launch(route_kernel<true>, dim3(grid), dim3(kRouteThreads), 0, stream, p)
+                    : launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), 0, stream, p);
+}
+
+int oomb_router_topk(const float* logits, int32_t* ids, float* weights, int t, int e, int k,
+                     oomb_stream stream) {
+    if (!logits || !ids || !weights) return OOMB_E_ARG;
+    if (t < 0 || k <= 0 || k > 32 || e > 8192 || k > e) return OOMB_E_SHAPE;
+    if (t == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    RouteParams p{};
+    p.logits = const_cast<float*>(logits);
+    p.T = t;
+    p.E = e;
+    p.K = k;
+    p.ids = ids;
+    p.weights = weights;
+    p.do_topk = 1;
+    p.err = d->err;
+    const int grid = (t + 7) / 8;
+    return launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), 0, stream, p);
+}
+
+int oomb_moe_gate_up_fp8(const uint64_t* recs, const int32_t* off, const int32_t* assign_tok,
+                         int n_experts, const void* x, int x_dtype, float* h,
+                         const oomb_fp8_record* geo, oomb_stream stream) {
+    if (!recs || !off || !assign_tok || !x || !h || !geo) return OOMB_E_ARG;
+    if (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (geo->layout != OOMB_SCALE_1X128 && geo->layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (n_experts < 0 || geo->hidden <= 0 || geo->inter <= 0 || geo->hidden % 16 || geo->inter % 16 ||
+        geo->hidden > 4096)
+        return OOMB_E_SHAPE;
+    if ((geo->gate_weight | geo->up_weight | geo->gate_scale | geo->up_scale) & 15) return OOMB_E_ALIGN;
+    if (!aligned16(x)) return OOMB_E_ALIGN;
+    if (n_experts == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    MoeParams p{};
+    p.recs = recs;
+    p.off = off;
+    p.assign_tok = assign_tok;
+    p.n_e_host = n_experts;
+    p.x = x;
+    p.out = h;
+    p.kdim = static_cast<int>(geo->hidden);
+    p.nrows = static_cast<int>(geo->inter);
+    p.w_off[0] = geo->gate_weight;
+    p.w_off[1] = geo->up_weight;
+    p.s_off[0] = geo->gate_scale;
+    p.s_off[1] = geo->up_scale;
+    p.layout = geo->layout;
+    moe_plan(p.kdim, 2, &p.rgp, &p.nsl);
+    p.gpe = (p.nrows + p.rgp - 1) / p.rgp;
+    p.err = d->err;
+    const int grid = moe_grid(d, n_experts * p.gpe);
+    return x_dtype == OOMB_BF16 ? moe_launch<2, true, false>(kMoeTB, grid, p, stream)
+                                : moe_launch<2, false, false>(kMoeTB, grid, p, stream);
+}
+
+int oomb_moe_down_fp8(const uint64_t* recs, const int32_t* off, int n_experts, const float* h,
+                      float* y, const oomb_fp8_record* geo, oomb_stream stream) {
+    if (!recs || !off || !h || !y || !geo) return OOMB_E_ARG;
+    if (geo->layout != OOMB_SCALE_1X128 && geo->layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (n_experts < 0 || geo->hidden <= 0 || geo->inter <= 0 || geo->hidden % 16 || geo->inter % 16 ||
+        geo->inter > 4096)
+        return OOMB_E_SHAPE;
+    if ((geo->down_weight | geo->down_scale) & 15) return OOMB_E_ALIGN;
+    if (!aligned16(h)) return OOMB_E_ALIGN;
+    if (n_experts == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    MoeParams p{};
+    p.recs = recs;
+    p.off = off;
+    p.n_e_host = n_experts;
+    p.x = h;
+    p.out = y;
+    p.kdim = static_cast<int>(geo->inter);
+    p.nrows = static_cast<int>(geo->hidden);
+    p.w_off[0] = p.w_off[1] = geo->down_weight;
+    p.s_off[0] = p.s_off[1] = geo->down_scale;
+    p.layout = geo->layout;
+    moe_plan(p.kdim, 1, &p.rgp, &p.nsl);
+    p.gpe = (p.nrows + p.rgp - 1) / p.rgp;
+    p.err = d->err;
+    const int grid = moe_grid(d, n_experts * p.gpe);
+    return moe_launch<1, false, false>(kMoeTB, grid, p, stream);
+}
+
+int oomb_moe_combine_slots(const float* y, const int32_t* slot_assign, const float* w, void* out,
+                           int out_dtype, int t, int h, int k, oomb_stream stream) {
+    if (!y || !slot_assign || !w || !out) return OOMB_E_ARG;
+    if (out_dtype != OOMB_F32 && out_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (t < 0 || h <= 0 || k <= 0 || h % 4) return OOMB_E_SHAPE;
+    if (!aligned16(y) || !aligned16(out)) return OOMB_E_ALIGN;
+    if (t == 0) return OOMB_OK;
+    if (!device_state()) return OOMB_E_DEVICE;
+    const int64_t quads = static_cast<int64_t>(t) * h / 4;
+    const dim3 grid(static_cast<unsigned>((quads + 255) / 256));
+    return out_dtype == OOMB_BF16
+               ? launch(combine_slots_kernel<true>, grid, dim3(256), 0, stream, y, slot_assign, w, out, t, h, k)
+               : launch(combine_slots_kernel<false>, grid, dim3(256), 0, stream, y, slot_assign, w, out, t, h, k);
+}
+
+int oomb_moe_combine(const float* routed, const float* shared, const float* gate_logit, float* out,
+                     int t, int h, oomb_stream stream) {
+    if (!routed || !shared || !gate_logit || !out) return OOMB_E_ARG;
+    if (t < 0 || h <= 0) return OOMB_E_SHAPE;
+    if (t == 0) return OOMB_OK;
+    if (!device_state()) return OOMB_E_DEVICE;
+    const int64_t n = static_cast<int64_t>(t) * h;
+    return launch(moe_combine_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream,
+                  routed, shared, gate_logit, out, t, h);
+}
+
+// ---- fused decode ------------------------------------------------------------
+
+namespace {
+struct DecodeLayout {
+    size_t ticket, logits, ids, weights, n_active, active, off, assign_tok, slot_assign, recs_active,
+        h, y, total;
+};
+
+size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+DecodeLayout decode_layout(int t, const oomb_moe_layer* L) {
+    DecodeLayout d{};
+    const size_t T = t, E = L->experts, K = L->top_k, A = T * K;
+    const size_t H = L->geo.hidden, I = L->geo.inter;
+    size_t o = 0;
+    d.ticket = o; o += 256;
+    d.logits = o; o = up256(o + T * E * 4);
+    d.ids = o; o = up256(o + A * 4);
+    d.weights = o; o = up256(o + A * 4);
+    d.n_active = o; o += 256;
+    d.active = o; o = up256(o + E * 4);
+    d.off = o; o = up256(o + (E + 1) * 4);
+    d.assign_tok = o; o = up256(o + A * 4);
+    d.slot_assign = o; o = up256(o + A * 4);
+    d.recs_active = o; o = up256(o + E * 8);
+    d.h = o; o = up256(o + A * I * 4);
+    d.y = o; o = up256(o + A * H * 4);
+    d.total = o;
+    return d;
+}
+
+int check_layer(const oomb_moe_layer* L) {
+    if (!L || !L->router_w || !L->recs) return OOMB_E_ARG;
+    const oomb_fp8_record& g = L->geo;
+    if (g.layout != OOMB_SCALE_1X128 && g.layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (L->hidden != g.hidden || L->experts <= 0 || L->experts > 8192 || L->top_k <= 0 ||
+        L->top_k > 32 || L->top_k > L->experts)
+        return OOMB_E_SHAPE;
+    if (g.hidden <= 0 || g.inter <= 0 || g.hidden % 16 || g.inter % 16 || g.hidden > 4096 || g.inter > 4096)
+        return OOMB_E_SHAPE;
+    if ((g.gate_weight | g.up_weight | g.down_weight | g.gate_scale | g.up_scale | g.down_scale) & 15)
+        return OOMB_E_ALIGN;
+    return OOMB_OK;
+}
+}  // namespace
+
+size_t oomb_moe_decode_workspace_bytes(int t, const oomb_moe_layer* layer) {
+    if (t <= 0 || check_layer(layer) != OOMB_OK) return 0;
+    return decode_layout(t, layer).total;
+}
+
+int oomb_workspace_clear(void* workspace, size_t bytes, oomb_stream stream) {
+    if (!workspace) return OOMB_E_ARG;
+    return cudaMemsetAsync(workspace, 0, bytes, stream) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int t, void* out,
+                        int out_dtype, int32_t* ids, float* weights, void* workspace,
+                        size_t workspace_bytes, oomb_stream stream) {
+    int rc = check_layer(L);
+    if (rc) return rc;
+    if (!x || !out || !workspace) return OOMB_E_ARG;
+    if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) || (out_dtype != OOMB_F32 && out_dtype != OOMB_BF16))
+        return OOMB_E_ARG;
+    if (t < 0) return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(out) || !aligned16(workspace) || !aligned16(L->router_w))
+        return OOMB_E_ALIGN;
+    if (t == 0) return OOMB_OK;
+    const DecodeLayout lay = decode_layout(t, L);
+    if (workspace_bytes < lay.total) return OOMB_E_WORKSPACE;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const int E = L->experts, K = L->top_k, H = L->hidden;
+    const int I = static_cast<int>(L->geo.inter);
+    const int A = t * K;
+
+    // 1. router logits + top-k + grouping (one launch; the last CTA groups)
+    RouteParams rp{};
+    rp.x = x;
+    rp.x_bf16 = x_dtype == OOMB_BF16;
+    rp.w = L->router_w;
+    rp.logits = reinterpret_cast<float*>(ws + lay.logits);
+    rp.T = t;
+    rp.H = H;
+    rp.E = E;
+    rp.K = K;
+    rp.ids = ids ? ids : reinterpret_cast<int32_t*>(ws + lay.ids);
+    rp.weights = weights ? weights : reinterpret_cast<float*>(ws + lay.weights);
+    rp.recs_all = L->recs;
+    rp.n_active = reinterpret_cast<int32_t*>(ws + lay.n_active);
+    rp.active = reinterpret_cast<int32_t*>(ws + lay.active);
+    rp.off = reinterpret_cast<int32_t*>(ws + lay.off);
+    rp.assign_tok = reinterpret_cast<int32_t*>(ws + lay.assign_tok);
+    rp.slot_assign = reinterpret_cast<int32_t*>(ws + lay.slot_assign);
+    rp.recs_active = reinterpret_cast<uint64_t*>(ws + lay.recs_active);
+    rp.ticket = reinterpret_cast<unsigned*>(ws + lay.ticket);
+    rp.do_logits = rp.do_topk = rp.do_group = 1;
+    rp.err = d->err;
+    {
+        const int tasks = E * ((t + kRouteTT - 1) / kRouteTT);
+        int grid = (tasks + 7) / 8;
+        if (grid > d->sms) grid = d->sms;
+        const size_t smem = (static_cast<size_t>(A) + 2 * static_cast<size_t>(E)) * 4;
+        if (smem > 200 * 1024) return OOMB_E_SHAPE;
+        rc = rp.x_bf16 ? launch(route_kernel<true>, dim3(grid), dim3(kRouteThreads), smem, stream, rp)
+                       : launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), smem, stream, rp);
+        if (rc) return rc;
+    }
+    // 2. gate/up + SiLU over the active experts
+    MoeParams gu{};
+    gu.recs = rp.recs_active;
+    gu.off = rp.off;
+    gu.assign_tok = rp.assign_tok;
+    gu.n_e_dev = rp.n_active;
+    gu.x = x;
+    gu.out = reinterpret_cast<float*>(ws + lay.h);
+    gu.kdim = H;
+    gu.nrows = I;
+    gu.w_off[0] = L->geo.gate_weight;
+    gu.w_off[1] = L->geo.up_weight;
+    gu.s_off[0] = L->geo.gate_scale;
+    gu.s_off[1] = L->geo.up_scale;
+    gu.layout = L->geo.layout;
+    moe_plan(H, 2, &gu.rgp, &gu.nsl);
+    gu.gpe = (I + gu.rgp - 1) / gu.rgp;
+    gu.err = d->err;
+    const int max_e = A < E ? A : E;
+    const int tb = moe_tb(t);
+    rc = rp.x_bf16 ? moe_launch<2, true, false>(tb, moe_grid(d, max_e * gu.gpe), gu, stream)
+                   : moe_launch<2, false, false>(tb, moe_grid(d, max_e * gu.gpe), gu, stream);
+    if (rc) return rc;
+    // 3. down (its producer starts streaming weights while gate/up finishes)
+    MoeParams dn{};
+    dn.recs = rp.recs_active;
+    dn.off = rp.off;
+    dn.n_e_dev = rp.n_active;
+    dn.x = gu.out;
+    dn.out = reinterpret_cast<float*>(ws + lay.y);
+    dn.kdim = I;
+    dn.nrows = H;
+    dn.w_off[0] = dn.w_off[1] = L->geo.down_weight;
+    dn.s_off[0] = dn.s_off[1] = L->geo.down_scale;
+    dn.layout = L->geo.layout;
+    moe_plan(I, 1, &dn.rgp, &dn.nsl);
+    dn.gpe = (H + dn.rgp - 1) / dn.rgp;
+    dn.err = d->err;
+    rc = moe_launch<1, false, true>(tb, moe_grid(d, max_e * dn.gpe), dn, stream);
+    if (rc) return rc;
+    // 4. slot-order combine
+    const int64_t quads = static_cast<int64_t>(t) * H / 4;
+    const dim3 cgrid(static_cast<unsigned>((quads + 255) / 256));
+    return out_dtype == OOMB_BF16
+               ? launch(combine_slots_kernel<true>, cgrid, dim3(256), 0, stream, dn.out,
+                        static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K)
+               : launch(combine_slots_kernel<false>, cgrid, dim3(256), 0, stream, dn.out,
+                        static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K);
+}
+
+int oomb_quantize_fp8(const uint16_t* w, int n, int k, int scale_layout, uint8_t* q, float* scale,
+                      oomb_stream stream) {
+    if (!w || !q || !scale) return OOMB_E_ARG;
+    if (scale_layout != OOMB_SCALE_1X128 && scale_layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (n <= 0 || k <= 0) return OOMB_E_SHAPE;
+    if (!device_state()) return OOMB_E_DEVICE;
+    const int nb = (k + 127) / 128;
+    const int nr = scale_layout == OOMB_SCALE_128X128 ? (n + 127) / 128 : n;
+    quantize_blocks_kernel<<<static_cast<unsigned>(nr) * nb, 128, 0, stream>>>(w, n, k, scale_layout, q, scale);
+    return cudaGetLastError() == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+}  // extern "C"

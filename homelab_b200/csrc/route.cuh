@@ -1,0 +1,275 @@
+// route.cuh - router GEMV, softmax top-k and on-device grouping by expert.
+//
+// Bit-exact contract with the CPU oracle (oracle/oomb_oracle.c):
+//   - logits: logit[t, e] = xor-tree over 32 lanes of lane l's fmaf chain over
+//     columns 256*i + 8*l + j (i ascending, j = 0..7) of x[t] * bf16(W[e]);
+//   - softmax: max over the row, exp by oomb_expf (the same Cody-Waite + Taylor
+//     arithmetic as oo_expf), sum = xor-tree of 32 lane partials (lane l adds
+//     experts l, l+32, ... in order), p = exp / sum (IEEE division);
+//   - top-k: k rounds of argmax over p, ties to the lower id, picked entries set
+//     to -2 (ops.cu:234-294); weights = p / (sum of picked p in pick order).
+// Grouping (Moe::begin_routed / finish_routed, moe.rs:532-582, 638-659, all
+// experts resident): assignments ordered by expert id, each expert's slots in
+// slot order; off[n_e + 1], assign_tok[A], slot_assign[A], active[n_e] and the
+// active experts' record addresses.
+#pragma once
+
+#include "common.cuh"
+
+namespace oomb {
+
+// exp(x) by Cody & Waite (1980) argument reduction x = n ln2 + r with ln2 split
+// into a 16-bit head and an fp32 tail, the degree-7 Taylor polynomial of exp(r)
+// on |r| <= ln2/2 in Horner form (fused multiply-adds), and 2^n applied in two
+// exact power-of-two steps.  Identical arithmetic to oo_expf in the oracle.
+__device__ __forceinline__ float oomb_expf(float x) {
+    if (x != x) return x;
+    if (x < -104.0f) return 0.0f;
+    if (x > 88.5f) return __int_as_float(0x7f800000);
+    const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+    float r = __fmaf_rn(-n, 0.693145751953125f, x);
+    r = __fmaf_rn(-n, 1.42860682030941723212e-6f, r);
+    float p = 1.98412698412698413e-4f;
+    p = __fmaf_rn(p, r, 1.38888888888888889e-3f);
+    p = __fmaf_rn(p, r, 8.33333333333333333e-3f);
+    p = __fmaf_rn(p, r, 4.16666666666666667e-2f);
+    p = __fmaf_rn(p, r, 1.66666666666666667e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ni = static_cast<int>(n);
+    const int n1 = ni / 2, n2 = ni - n1;
+    const float s1 = __int_as_float((n1 + 127) << 23);
+    const float s2 = __int_as_float((n2 + 127) << 23);
+    return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
+__device__ __forceinline__ float xor_tree32(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+struct RouteParams {
+    const void* x;            // [T, H] activations
+    int x_bf16;
+    const uint16_t* w;        // bf16 router [E, H]
+    float* logits;            // [T, E]
+    int T, H, E, K;
+    // top-k outputs
+    int32_t* ids;             // [T, K]
+    float* weights;           // [T, K]
+    // grouping outputs (null to skip)
+    const uint64_t* recs_all; // [E] record addresses of the layer (null: no recs_active)
+    int32_t* n_active;        // [1]
+    int32_t* active;          // [E]
+    int32_t* off;             // [E + 1]
+    int32_t* assign_tok;      // [T*K]
+    int32_t* slot_assign;     // [T*K]
+    uint64_t* recs_active;    // [E]
+    unsigned* ticket;         // self-resetting arrival counter (zero before first use)
+    int do_logits, do_topk, do_group;
+    unsigned* err;
+};
+
+constexpr int kRouteThreads = 256;
+constexpr int kRouteTT = 4;  // tokens per warp task in the logits phase
+
+// Logits for rows e and tokens [t0, t0 + nt) (nt <= kRouteTT) in the canonical order.
+template <bool XBF16>
+__device__ __forceinline__ void router_row(const RouteParams& p, int e, int t0, int nt, int lane) {
+    float acc[kRouteTT];
+#pragma unroll
+    for (int j = 0; j < kRouteTT; j++) acc[j] = 0.0f;
+    const uint16_t* wr = p.w + static_cast<int64_t>(e) * p.H;
+    for (int base = lane * 8; base < p.H; base += 256) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + base));
+        const unsigned ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        float wf[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            wf[2 * i] = __uint_as_float(ww[i] << 16);
+            wf[2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
+        }
+#pragma unroll
+        for (int j = 0; j < kRouteTT; j++) {
+            if (j < nt) {
+                float xv[8];
+                const int64_t xi = static_cast<int64_t>(t0 + j) * p.H + base;
+                if (XBF16) {
+                    const uint4 a = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi));
+                    const unsigned aa[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        xv[2 * i] = __uint_as_float(aa[i] << 16);
+                        xv[2 * i + 1] = __uint_as_float(aa[i] & 0xffff0000u);
+                    }
+                } else {
+                    const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi));
+                    const float4 b = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi) + 1);
+                    xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+                    xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) acc[j] = __fmaf_rn(xv[i], wf[i], acc[j]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kRouteTT; j++) {
+        const float v = xor_tree32(acc[j]);
+        if (j < nt && lane == 0) p.logits[static_cast<int64_t>(t0 + j) * p.E + e] = v;
+    }
+}
+
+// Softmax top-k of one token by one warp (probabilities recomputed from the
+// logits on each pass, so any E fits).
+__device__ __forceinline__ void topk_token(const RouteParams& p, int t, int lane, int32_t* ids_sm) {
+    const float* l = p.logits + static_cast<int64_t>(t) * p.E;
+    float mx = -__int_as_float(0x7f800000);
+    for (int i = lane; i < p.E; i += 32) mx = fmaxf(mx, __ldcg(l + i));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float s = 0.0f;
+    for (int i = lane; i < p.E; i += 32) s = __fadd_rn(s, oomb_expf(__fsub_rn(__ldcg(l + i), mx)));
+    const float sum = xor_tree32(s);
+    // Each round scans this lane's experts; picked ones are remembered in a
+    // 32-bit mask per lane chunk (k <= 32 picks in total).
+    int picked[32];
+    float picked_p[32];
+    int npicked = 0;
+    float psum = 0.0f;
+    for (int r = 0; r < p.K; r++) {
+        float bv = -3.0f;
+        int bi = 0x7fffffff;
+        for (int i = lane; i < p.E; i += 32) {
+            bool used = false;
+            for (int q = 0; q < npicked; q++) used |= picked[q] == i;
+            const float pi = used ? -2.0f : __fdiv_rn(oomb_expf(__fsub_rn(__ldcg(l + i), mx)), sum);
+            if (pi > bv) { bv = pi; bi = i; }  // lane's experts ascend: ties keep the lower id
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        picked[npicked] = bi;
+        picked_p[npicked] = bv;
+        npicked++;
+    }
+    for (int r = 0; r < p.K; r++) psum = __fadd_rn(psum, picked_p[r]);
+    if (lane < p.K) {
+        // lane r writes pick r (registers indexed through a shuffle-free select)
+        int id = 0;
+        float pp = 0.0f;
+        for (int r = 0; r < p.K; r++)
+            if (r == lane) { id = picked[r]; pp = picked_p[r]; }
+        p.ids[static_cast<int64_t>(t) * p.K + lane] = id;
+        p.weights[static_cast<int64_t>(t) * p.K + lane] = __fdiv_rn(pp, psum);
+        if (ids_sm) ids_sm[t * p.K + lane] = id;
+    }
+}
+
+// Groups the T*K assignments by expert (counting sort, stable in slot order).
+// Runs on one CTA; ids in shared memory.  counts: E ints of shared scratch.
+__device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, int32_t* counts,
+                                  int32_t* base) {
+    const int A = p.T * p.K;
+    for (int e = threadIdx.x; e < p.E; e += blockDim.x) counts[e] = 0;
+    __syncthreads();
+    for (int s = threadIdx.x; s < A; s += blockDim.x) {
+        const int e = ids_sm[s];
+        if (e >= 0 && e < p.E) atomicAdd(&counts[e], 1);
+        else record_error(p.err, ERR_BAD_TABLE);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        // Exclusive scans over experts: assignment start and active index.
+        const int lane = threadIdx.x;
+        int run_a = 0, run_n = 0;
+        for (int e0 = 0; e0 < p.E; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < p.E ? counts[e] : 0;
+            int inc_a = c, inc_n = c > 0 ? 1 : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int va = __shfl_up_sync(0xffffffffu, inc_a, o);
+                const int vn = __shfl_up_sync(0xffffffffu, inc_n, o);
+                if (lane >= o) { inc_a += va; inc_n += vn; }
+            }
+            const int start = run_a + inc_a - c;
+            const int idx = run_n + inc_n - (c > 0 ? 1 : 0);
+            if (e < p.E && c > 0) {
+                base[e] = start;
+                p.active[idx] = e;
+                p.off[idx] = start;
+                if (p.recs_all) p.recs_active[idx] = p.recs_all[e];
+            }
+            run_a += __shfl_sync(0xffffffffu, inc_a, 31);
+            run_n += __shfl_sync(0xffffffffu, inc_n, 31);
+        }
+        if (lane == 0) {
+            p.off[run_n] = run_a;
+            *p.n_active = run_n;
+        }
+        // Ranks in slot order, 32 slots at a time.
+        for (int s0 = 0; s0 < A; s0 += 32) {
+            const int s = s0 + lane;
+            const int e = s < A ? ids_sm[s] : -1 - lane;  // unique dummies for idle lanes
+            const unsigned peers = __match_any_sync(0xffffffffu, e);
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            if (s < A && e >= 0 && e < p.E) {
+                const int a = base[e] + rank;
+                p.assign_tok[a] = s / p.K;
+                p.slot_assign[s] = a;
+            }
+            __syncwarp();
+            // the highest lane of each peer group advances the expert's base
+            if (s < A && e >= 0 && e < p.E && (peers >> lane) == 1u) base[e] += rank + 1;
+            __syncwarp();
+        }
+    }
+}
+
+template <bool XBF16>
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams p) {
+    extern __shared__ __align__(16) int32_t rsm[];  // ids [T*K] | counts [E] | base [E]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = kRouteThreads / 32;
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (p.do_logits) {
+        const int ttiles = (p.T + kRouteTT - 1) / kRouteTT;
+        const int tasks = p.E * ttiles;
+        for (int task = blockIdx.x * nwarps + warp; task < tasks; task += gridDim.x * nwarps) {
+            const int e = task % p.E, tt = task / p.E;
+            const int t0 = tt * kRouteTT;
+            router_row<XBF16>(p, e, t0, min(kRouteTT, p.T - t0), lane);
+        }
+        if (!p.do_topk) return;
+        // The last CTA to finish its logits runs the rest (deterministic: the
+        // work it does depends only on the logits, not on which CTA it is).
+        __shared__ bool last;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+        if (threadIdx.x == 0) *p.ticket = 0u;
+    }
+    int32_t* ids_sm = p.do_group ? rsm : nullptr;
+    if (p.do_group) {
+        // grouping needs every token's picks in one CTA
+        for (int t = warp; t < p.T; t += nwarps) topk_token(p, t, lane, ids_sm);
+        __syncthreads();
+        group_assignments(p, ids_sm, rsm + p.T * p.K, rsm + p.T * p.K + p.E);
+    } else {
+        for (int t = blockIdx.x * nwarps + warp; t < p.T; t += gridDim.x * nwarps)
+            topk_token(p, t, lane, nullptr);
+    }
+}
+
+}  // namespace oomb

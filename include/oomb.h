@@ -1,0 +1,168 @@
+/*
+ * oomb.h - C ABI of the B200 (sm_100a) FP8 decode path of oom-inference.
+ *
+ * Each entry point replaces the launch body of one method of the engine's
+ * Rust backend traits (projects/oom-inference/crates/oominf-core/src/backend.rs),
+ * cited beside it.  Conventions, as in the reference backend:
+ *   - every call is stream-ordered on the `stream` it is given and enqueues no
+ *     implicit synchronisation; host reads of results sync through the stream;
+ *   - the caller owns every device buffer (inputs, outputs, workspace); the
+ *     library allocates nothing on the call path;
+ *   - shapes and alignment are checked before launch, as Gpu::check does
+ *     (crates/oominf-cuda/src/lib.rs:157-160): an unsupported shape returns
+ *     OOMB_E_SHAPE / OOMB_E_ALIGN and launches nothing;
+ *   - device pointers are plain addresses; the library needs the CUDA
+ *     runtime and an sm_100a device, and fails loudly (OOMB_E_DEVICE) elsewhere.
+ * Device-side waits are bounded: a wait that runs out records a code readable
+ * with oomb_device_error() and the kernel returns instead of hanging.
+ */
+#ifndef OOMB_H
+#define OOMB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t (0 = the legacy default stream). */
+typedef struct CUstream_st* oomb_stream;
+
+/* Status codes (0 = success). */
+#define OOMB_OK 0
+#define OOMB_E_SHAPE (-1)     /* "buffer too small or shape unsupported" (lib.rs:157-160) */
+#define OOMB_E_ALIGN (-2)     /* a pointer or stride is not 16-byte aligned */
+#define OOMB_E_LAUNCH (-3)    /* the CUDA launch failed */
+#define OOMB_E_TIMEOUT (-4)   /* a bounded device wait ran out (see oomb_device_error) */
+#define OOMB_E_ARG (-5)       /* null pointer or bad enum */
+#define OOMB_E_DEVICE (-6)    /* no usable sm_100 device */
+#define OOMB_E_WORKSPACE (-7) /* workspace smaller than the *_workspace_bytes figure */
+
+/* Element types of activations and outputs. */
+#define OOMB_F32 0
+#define OOMB_BF16 1
+
+/* Scale layouts of a block-scaled FP8 e4m3 matrix q[n, k] (row-major):
+ *   OOMB_SCALE_1X128:   w[r, c] = scale[r * ceil(k/128) + c/128] * e4m3(q[r, c])
+ *                       (Weight::Fp8, backend.rs:162-170; fp8.rs:46-88)
+ *   OOMB_SCALE_128X128: w[r, c] = scale[(r/128) * ceil(k/128) + c/128] * e4m3(q[r, c]) */
+#define OOMB_SCALE_1X128 0
+#define OOMB_SCALE_128X128 1
+
+/* Byte layout of an FP8 expert record (layout tag "fp8-e4m3-b128x128" or
+ * "fp8-e4m3-b1x128"), the FP8 counterpart of Nvfp4Record / Bf16Record
+ * (backend.rs:783-807): gate and up e4m3 [inter, hidden], down e4m3
+ * [hidden, inter], each with its own fp32 scales in `layout`.  Offsets are in
+ * bytes from the record start and must be multiples of 16. */
+typedef struct {
+    int64_t hidden;
+    int64_t inter;
+    int64_t gate_weight, gate_scale;
+    int64_t up_weight, up_scale;
+    int64_t down_weight, down_scale;
+    int32_t layout;
+    int32_t pad_;
+} oomb_fp8_record;
+
+/* A resident MoE layer for the fused decode path: the bf16 router [experts,
+ * hidden] (routers stay bf16, crates/oominf-models-qwen/src/util.rs:48-60)
+ * and one device record address per expert. */
+typedef struct {
+    int32_t hidden;
+    int32_t experts;
+    int32_t top_k;
+    int32_t pad_;
+    const uint16_t* router_w;
+    const uint64_t* recs;
+    oomb_fp8_record geo;
+} oomb_moe_layer;
+
+/* ---- library -------------------------------------------------------- */
+const char* oomb_version(void);
+const char* oomb_status_string(int status);
+/* The first bounded-wait failure recorded on the current device since the
+ * last clear (0 if none); `clear` != 0 resets it.  Synchronises the device. */
+int oomb_device_error(int* code, int clear);
+
+/* ---- Linear ------------------------------------------------------------ */
+/* y[t, n] = x[t, k] . W[n, k]^T for FP8 e4m3 W with block scales, fp32
+ * accumulation.  Replaces Linear::gemm_fp8 (backend.rs:199-209; launch body
+ * Gpu::gemm_fp8 / gemv / gemv_at, crates/oominf-cuda/src/linear.rs:35-81,
+ * 223-350).  x and y are fp32 or bf16.  k % 16 == 0; q, scale, x and y
+ * 16-byte aligned.  Steps of up to 8 tokens per launch run the CUDA-core
+ * GEMV; larger t runs as successive 8-token launches.  Workspace: none
+ * (pass NULL, 0). */
+int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* scale,
+                  int scale_layout, void* y, int y_dtype, int t, int n, int k, void* workspace,
+                  size_t workspace_bytes, oomb_stream stream);
+
+/* logits[t, e] = x[t, :] . W[e, :] for a bf16 router W [e, hidden], in the
+ * canonical order the oracle restates bit for bit (fp32 fma per lane over
+ * columns 256*i + 8*lane + j, xor-tree over 32 lanes).  The router GEMV of
+ * Moe::forward (crates/oominf-models-qwen/src/moe.rs:289-298). */
+int oomb_router_logits(const void* x, int x_dtype, const uint16_t* w, float* logits, int t,
+                       int e, int hidden, oomb_stream stream);
+
+/* ---- Experts ------------------------------------------------------------ */
+/* Softmax over e logits per row, top k (ties to the lower id), weights
+ * renormalised over the picks.  Replaces Experts::router_topk (backend.rs:
+ * 816-824; crates/oominf-cuda/src/experts.rs:10-38; ops.cu:234-294).
+ * k <= 32, k <= e <= 8192. */
+int oomb_router_topk(const float* logits, int32_t* ids, float* weights, int t, int e, int k,
+                     oomb_stream stream);
+
+/* h[a, :] = silu(x[tok(a)] . Wg^T) * (x[tok(a)] . Wu^T) for every assignment a
+ * of the n_experts groups: expert i owns assignments [off[i], off[i+1]) and
+ * its record is at recs[i]; tok(a) = assign_tok[a].  Replaces
+ * Experts::moe_gate_up (backend.rs:827-836; experts.rs:43-93; moe.cu:55-106)
+ * for FP8 records.  x: [*, hidden] fp32 or bf16; h: [A, inter] fp32.
+ * hidden <= 4096, hidden % 16 == 0, inter % 16 == 0. */
+int oomb_moe_gate_up_fp8(const uint64_t* recs, const int32_t* off, const int32_t* assign_tok,
+                         int n_experts, const void* x, int x_dtype, float* h,
+                         const oomb_fp8_record* geo, oomb_stream stream);
+
+/* y[a, :] = h[a, :] . Wd^T for every assignment.  Replaces Experts::moe_down
+ * (backend.rs:860-868; experts.rs:174-209; moe.cu:110-151).  inter <= 4096. */
+int oomb_moe_down_fp8(const uint64_t* recs, const int32_t* off, int n_experts, const float* h,
+                      float* y, const oomb_fp8_record* geo, oomb_stream stream);
+
+/* out[t, c] = sum_s w[t, s] * y[slot_assign[t, s], c], summed in slot order
+ * with fused multiply-adds (deterministic).  Replaces Experts::moe_combine_slots
+ * (backend.rs:898-907; experts.rs:303-329; moe.cu:155-164).  out fp32 or bf16. */
+int oomb_moe_combine_slots(const float* y, const int32_t* slot_assign, const float* w, void* out,
+                           int out_dtype, int t, int h, int k, oomb_stream stream);
+
+/* out = routed + sigmoid(gate_logit[t]) * shared.  Replaces Experts::moe_combine
+ * (backend.rs:909-917; ops.cu:311-316).  All fp32 [t, h]; gate_logit [t]. */
+int oomb_moe_combine(const float* routed, const float* shared, const float* gate_logit,
+                     float* out, int t, int h, oomb_stream stream);
+
+/* ---- fused decode step of one resident MoE layer ------------------------ */
+/* Router GEMV, softmax top-k, grouping of the step's assignments by expert
+ * (expert order, slots in slot order: Moe::begin_routed / finish_routed,
+ * moe.rs:532-582, 638-659), gate/up+SiLU, down and the slot-order combine, as
+ * one stream-ordered sequence of kernels with no host round trip.  Same
+ * results as calling the separate entry points in that order.
+ *   x: [t, hidden] (x_dtype); out: [t, hidden] (out_dtype);
+ *   ids, weights: optional [t, top_k] copies of the routing (NULL to skip).
+ * The workspace must hold oomb_moe_decode_workspace_bytes(t, layer) bytes and
+ * be zeroed once before first use (oomb_workspace_clear); calls that share a
+ * workspace must be ordered on one stream. */
+size_t oomb_moe_decode_workspace_bytes(int t, const oomb_moe_layer* layer);
+int oomb_moe_decode_fp8(const oomb_moe_layer* layer, const void* x, int x_dtype, int t, void* out,
+                        int out_dtype, int32_t* ids, float* weights, void* workspace,
+                        size_t workspace_bytes, oomb_stream stream);
+int oomb_workspace_clear(void* workspace, size_t bytes, oomb_stream stream);
+
+/* ---- weight preparation ------------------------------------------------- */
+/* The load-time quantizer on the device, byte-identical to fp8::quantize_blocks
+ * (crates/oominf-core/src/fp8.rs:52-88) for OOMB_SCALE_1X128 and to its 2-D
+ * block generalisation for OOMB_SCALE_128X128.  w: bf16 [n, k]. */
+int oomb_quantize_fp8(const uint16_t* w, int n, int k, int scale_layout, uint8_t* q, float* scale,
+                      oomb_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OOMB_H */

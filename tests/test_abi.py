@@ -1,0 +1,105 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol include/oomb.h
+declares, and its host-side checks reject bad arguments before any launch (the
+`ensure!` checks of Gpu::check, crates/oominf-cuda/src/lib.rs:157-160)."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+import homelab_b200 as hb
+from homelab_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", fn)).read()
+            names |= set(re.findall(r"\b(oomb_[a-z0-9_]+)\s*\(", src))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    L = hb.lib()
+    names = declared_symbols()
+    assert len(names) >= 14
+    for n in sorted(names):
+        assert hasattr(L, n), n
+
+
+def test_python_signatures_cover_header():
+    assert {n for n, _, _ in _lib.SIGNATURES} == declared_symbols()
+
+
+def test_no_oracle_dependency():
+    # The product never links, loads or imports the CPU oracle.
+    import subprocess
+    out = subprocess.run(["ldd", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    assert "oracle" not in out and "cpubase" not in out
+    pkg = os.path.join(ROOT, "homelab_b200")
+    for f in os.listdir(pkg):
+        if f.endswith(".py"):
+            src = open(os.path.join(pkg, f)).read()
+            assert not re.search(r"^\s*(import|from)\s+oracle", src, re.M), f
+            assert "liboomb_oracle" not in src and "liboomb_cpubase" not in src, f
+
+
+def test_status_strings():
+    L = hb.lib()
+    assert L.oomb_status_string(0) == b"ok"
+    assert b"shape" in L.oomb_status_string(_lib.E_SHAPE)
+    assert L.oomb_version().startswith(b"oomb")
+
+
+def test_checks_run_before_launch():
+    L = hb.lib()
+    fake = 0x10000  # never dereferenced: every call below fails its checks first
+    # k not a multiple of 16
+    assert L.oomb_gemm_fp8(fake, 0, fake, fake, 1, fake, 0, 1, 64, 17, None, 0, None) == _lib.E_SHAPE
+    # null inputs
+    assert L.oomb_gemm_fp8(0, 0, fake, fake, 1, fake, 0, 1, 64, 32, None, 0, None) == _lib.E_ARG
+    # bad dtype / layout enums
+    assert L.oomb_gemm_fp8(fake, 7, fake, fake, 1, fake, 0, 1, 64, 32, None, 0, None) == _lib.E_ARG
+    assert L.oomb_gemm_fp8(fake, 0, fake, fake, 9, fake, 0, 1, 64, 32, None, 0, None) == _lib.E_ARG
+    # misaligned pointer
+    assert L.oomb_gemm_fp8(fake + 4, 0, fake, fake, 1, fake, 0, 1, 64, 32, None, 0, None) == _lib.E_ALIGN
+    # top-k limits of experts.rs:19 (k <= 32, e <= 8192), and k <= e
+    assert L.oomb_router_topk(fake, fake, fake, 1, 8193, 8, None) == _lib.E_SHAPE
+    assert L.oomb_router_topk(fake, fake, fake, 1, 64, 33, None) == _lib.E_SHAPE
+    assert L.oomb_router_topk(fake, fake, fake, 1, 4, 8, None) == _lib.E_SHAPE
+    # expert widths must be multiples of 16 (experts.rs:55-58), hidden <= 4096
+    g = hb.Fp8Record(hidden=2048, inter=770, layout=1)
+    assert L.oomb_moe_gate_up_fp8(fake, fake, fake, 1, fake, 0, fake, C.byref(g), None) == _lib.E_SHAPE
+    g = hb.Fp8Record(hidden=8192, inter=768, layout=1)
+    assert L.oomb_moe_gate_up_fp8(fake, fake, fake, 1, fake, 0, fake, C.byref(g), None) == _lib.E_SHAPE
+    g = hb.Fp8Record(hidden=2048, inter=768, layout=1, down_weight=8)
+    assert L.oomb_moe_down_fp8(fake, fake, 1, fake, fake, C.byref(g), None) == _lib.E_ALIGN
+
+
+def test_decode_workspace_size_and_checks():
+    L = hb.lib()
+    layer = hb.MoeLayer(hidden=2048, experts=128, top_k=8, router_w=0x10000, recs=0x10000)
+    from homelab_b200.records import record_layout
+    layer.geo, _ = record_layout(2048, 768)
+    n1 = L.oomb_moe_decode_workspace_bytes(1, C.byref(layer))
+    n16 = L.oomb_moe_decode_workspace_bytes(16, C.byref(layer))
+    assert n1 > 0 and n16 > n1
+    # A = t * k assignments of h [A, inter] and y [A, hidden] fp32 dominate
+    assert n16 >= 16 * 8 * (768 + 2048) * 4
+    bad = hb.MoeLayer(hidden=2048, experts=128, top_k=200, router_w=0x10000, recs=0x10000)
+    bad.geo = layer.geo
+    assert L.oomb_moe_decode_workspace_bytes(1, C.byref(bad)) == 0
+    ws = 0x10000
+    assert L.oomb_moe_decode_fp8(C.byref(layer), 0x10000, 1, 1, 0x10000, 1, None, None, ws, 16, None) == _lib.E_WORKSPACE
+
+
+def test_no_gpu_fails_loudly():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    L = hb.lib()
+    fake = 0x10000
+    assert L.oomb_gemm_fp8(fake, 0, fake, fake, 1, fake, 0, 1, 64, 32, None, 0, None) == _lib.E_DEVICE
