@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=8,
+                    help="layer replicas rotated through (8 x 604 MB keeps every step out of L2)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU work of the cpu_baseline / reference sample")
@@ -60,10 +62,10 @@ def parse():
     return ap.parse_args()
 
 
-def config_dict(batch):
+def config_dict(batch, layers=LAYERS):
     return {"workload": WORKLOAD, "hidden": H, "experts": E, "top_k": K_TOP, "inter": I,
-            "batch_per_gpu": batch, "scale_blocks": "128x128", "layers_rotated": LAYERS,
-            "l2": "inputs larger than L2: each step reads a different layer's experts (8 x 604 MB)"}
+            "batch_per_gpu": batch, "scale_blocks": "128x128", "layers_rotated": layers,
+            "l2": f"inputs larger than L2: each step reads a different layer's experts ({layers} x 604 MB)"}
 
 
 def load_peaks():
@@ -92,8 +94,8 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, index):
+        self.index = index  # nvidia-smi -i accepts an index or a GPU UUID
         self.proc = None
 
     def __enter__(self):
@@ -225,6 +227,7 @@ def run_ours(args, rank, world, local_rank):
     B = args.batch
 
     # ---- weights: 8 layer replicas ----
+    LAYERS = args.layers
     layers = []
     gen = torch.Generator(device=dev)
     for li in range(LAYERS):
@@ -296,7 +299,11 @@ def run_ours(args, rank, world, local_rank):
     for g, _ in plan:
         g.replay()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as cs:
+    try:
+        smi_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        smi_id = str(local_rank)
+    with ClockSampler(smi_id) as cs:
         # keep the GPU busy ~0.5 s before the timed region so the sampler sees load
         t_end = time.time() + 0.5
         while time.time() < t_end:
@@ -322,7 +329,8 @@ def run_ours(args, rank, world, local_rank):
     del ge_main, ge_rem
 
     # ---- roofline of the dominant kernel: gate/up+SiLU over the 8 experts of a step ----
-    roof = measure_gate_up(gpu, layers, dev, s, B)
+    roof = measure_gate_up(gpu, layers, dev, s, B, LAYERS)
+    gemv1 = measure_gemv_config1(gpu, dev, s)
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
     step_bytes = E * H * 2 + 8 * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
@@ -333,13 +341,16 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(config_dict(B), parallelism=f"replicas{world}" if world > 1 else "single"),
+            "config": dict(config_dict(B, LAYERS), parallelism=f"replicas{world}" if world > 1 else "single"),
             "roofline": {"bound": "hbm", "achieved": roof["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": roof["gbs"] / peak, "peak_kind": peak_kind,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                         "kernel": "moe_fp8_kernel<2> (gate/up+SiLU, 8 experts)",
+                         "kernel": "stream_kernel<2> (gate/up+SiLU over the 8 experts of a step)",
                          "algorithmic_bytes_per_launch": roof["bytes"], "launch_us": roof["us"]},
             "step_hbm_gbs": step_bytes * K / (ms / 1e3) / 1e9 / 1.0 if world == 1 else None,
+            "gemv_config1": {"workload": "config1: 4096x4096 e4m3, 128x128 scales, x bf16 batch 1, bf16 out",
+                             "achieved_gbs": gemv1["gbs"], "frac": gemv1["gbs"] / peak, "launch_us": gemv1["us"],
+                             "algorithmic_bytes_per_launch": gemv1["bytes"]},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
             "gpu_launches": 4 * K,
@@ -348,8 +359,12 @@ def run_ours(args, rank, world, local_rank):
     return result, roof
 
 
-def measure_gate_up(gpu, layers, dev, s, B, launches=400):
-    """Average duration of back-to-back gate/up launches over 8 fixed experts per launch."""
+def measure_gate_up(gpu, layers, dev, s, B, LAYERS, launches=400):
+    """Average duration of back-to-back gate/up launches over 8 fixed experts per launch.
+
+    The routing tables are written before the loop (OOMB_TABLES_READY), so each
+    launch streams its experts' weights while the previous launch drains, as
+    the down projection does behind gate/up in the decode step."""
     import numpy as np
     import torch
 
@@ -369,7 +384,7 @@ def measure_gate_up(gpu, layers, dev, s, B, launches=400):
 
     def one(i):
         recs, off, tok, n = tables[i % LAYERS]
-        gpu.moe_gate_up(recs, off, tok, n, x, h, geo)
+        gpu.moe_gate_up(recs, off, tok, n, x, h, geo, 1, tables_ready=True)
 
     for i in range(16):
         one(i)
@@ -390,6 +405,46 @@ def measure_gate_up(gpu, layers, dev, s, B, launches=400):
         best = min(best, ev0.elapsed_time(ev1) / launches)
     n_e = tables[0][3]
     nbytes = n_e * (2 * I * H + 2 * scale_bytes(I, H, geo.layout)) + n_e * H * 2 + n_e * I * 4
+    us = best * 1e3
+    return {"gbs": nbytes / (us * 1e-6) / 1e9, "bytes": nbytes, "us": us}
+
+
+def measure_gemv_config1(gpu, dev, s, copies=16, launches=320):
+    """y = W x, W 4096 x 4096 e4m3 with 128x128 block scales,
+    x bf16 [1, 4096], bf16 out; back-to-back launches over `copies` weight
+    copies (268 MB, beyond L2).  Returns GB/s of algorithmic bytes."""
+    import torch
+
+    import homelab_b200 as hb
+    n = k = 4096
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    qs, ss = [], []
+    for c in range(copies):
+        w = (torch.randn((n, k), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        q, sc = gpu.quantize_fp8(w.view(torch.int16), n, k, hb.SCALE_128X128)
+        qs.append(q)
+        ss.append(sc)
+    x = torch.randn((1, k), generator=gen, device=dev).to(torch.bfloat16)
+    y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+    for i in range(8):
+        gpu.gemm_fp8(x, qs[i % copies], ss[i % copies], y, 1, n, k, hb.SCALE_128X128)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(launches):
+            gpu.gemm_fp8(x, qs[i % copies], ss[i % copies], y, 1, n, k, hb.SCALE_128X128)
+    g.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = float("inf")
+    for _ in range(3):
+        with torch.cuda.stream(s):
+            ev0.record(s)
+            g.replay()
+            ev1.record(s)
+        ev1.synchronize()
+        best = min(best, ev0.elapsed_time(ev1) / launches)
+    nbytes = n * k + (n // 128) * (k // 128) * 4 + k * 2 + n * 2
     us = best * 1e3
     return {"gbs": nbytes / (us * 1e-6) / 1e9, "bytes": nbytes, "us": us}
 

@@ -25,6 +25,7 @@ F32 = 0
 BF16 = 1
 SCALE_1X128 = 0
 SCALE_128X128 = 1
+TABLES_READY = 1
 
 
 class Fp8Record(C.Structure):
@@ -58,8 +59,8 @@ SIGNATURES = [
     ("oomb_gemm_fp8", I, [P, I, P, P, I, P, I, I, I, I, P, Z, S]),
     ("oomb_router_logits", I, [P, I, P, P, I, I, I, S]),
     ("oomb_router_topk", I, [P, P, P, I, I, I, S]),
-    ("oomb_moe_gate_up_fp8", I, [P, P, P, I, P, I, P, C.POINTER(Fp8Record), S]),
-    ("oomb_moe_down_fp8", I, [P, P, I, P, P, C.POINTER(Fp8Record), S]),
+    ("oomb_moe_gate_up_fp8", I, [P, P, P, I, P, I, P, C.POINTER(Fp8Record), I, I, S]),
+    ("oomb_moe_down_fp8", I, [P, P, I, P, P, C.POINTER(Fp8Record), I, I, S]),
     ("oomb_moe_combine_slots", I, [P, P, P, P, I, I, I, I, S]),
     ("oomb_moe_combine", I, [P, P, P, P, I, I, S]),
     ("oomb_moe_decode_workspace_bytes", Z, [I, C.POINTER(MoeLayer)]),

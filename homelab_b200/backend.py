@@ -64,16 +64,19 @@ class Gpu:
         check(self.L.oomb_router_topk(_ptr(logits), _ptr(ids), _ptr(weights), t, e, k,
                                       self._stream()), "router_topk")
 
-    def moe_gate_up(self, recs, off, assign_tok, n_experts: int, x, h, geo: Fp8Record):
+    def moe_gate_up(self, recs, off, assign_tok, n_experts: int, x, h, geo: Fp8Record, max_per_expert: int = 0,
+                    tables_ready: bool = False):
         """h[a] = silu(x[tok(a)] . Wg) * (x[tok(a)] . Wu) (Experts::moe_gate_up, backend.rs:827-836)."""
         check(self.L.oomb_moe_gate_up_fp8(_ptr(recs), _ptr(off), _ptr(assign_tok), n_experts, _ptr(x),
-                                          _dtype_code(x), _ptr(h), C.byref(geo), self._stream()),
-              "moe_gate_up")
+                                          _dtype_code(x), _ptr(h), C.byref(geo), max_per_expert,
+                                          _lib.TABLES_READY if tables_ready else 0, self._stream()), "moe_gate_up")
 
-    def moe_down(self, recs, off, n_experts: int, h, y, geo: Fp8Record):
+    def moe_down(self, recs, off, n_experts: int, h, y, geo: Fp8Record, max_per_expert: int = 0,
+                 tables_ready: bool = False):
         """y[a] = h[a] . Wd^T (Experts::moe_down, backend.rs:860-868)."""
         check(self.L.oomb_moe_down_fp8(_ptr(recs), _ptr(off), n_experts, _ptr(h), _ptr(y), C.byref(geo),
-                                       self._stream()), "moe_down")
+                                       max_per_expert, _lib.TABLES_READY if tables_ready else 0, self._stream()),
+              "moe_down")
 
     def moe_combine_slots(self, y, slot_assign, w, out, t: int, h: int, k: int):
         """out[t] = sum_s w[t, s] * y[slot_assign[t, s]] in slot order (backend.rs:898-907)."""

@@ -13,10 +13,10 @@
 #include <unordered_map>
 
 #include "../../include/oomb.h"
-#include "gemv_fp8.cuh"
-#include "moe_fp8.cuh"
+#include "combine.cuh"
 #include "quant.cuh"
 #include "route.cuh"
+#include "stream.cuh"
 
 namespace oomb {
 namespace {
@@ -97,37 +97,108 @@ int launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t strea
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// ---- GEMV -------------------------------------------------------------------
+// ---- streaming kernels ----------------------------------------------------------
 
-template <int T, bool XB>
-int gemv_launch_t(const GemvPlan& pl, GemvParams& gp, cudaStream_t s) {
-    const size_t smem = gemv_smem_bytes(pl.maxg, T);
-    if (pl.maxg == 1)
-        return launch(gemv_fp8_kernel<T, XB, 1>, dim3(pl.grid), dim3(kGemvThreads), smem, s, gp);
-    if constexpr (T == 4)
-        return launch(gemv_fp8_kernel<T, XB, 2>, dim3(pl.grid), dim3(kGemvThreads), smem, s, gp);
-    else
-        return launch(gemv_fp8_kernel<T, XB, 4>, dim3(pl.grid), dim3(kGemvThreads), smem, s, gp);
+// Token slots for units with at most `maxn` assignments (0: unknown), and
+// whether more than TB may occur (then P = 1 and chunks of TB are reduced one
+// by one against the stage in shared memory).
+struct TbP {
+    int tb;
+    bool chunked;
+};
+TbP tb_p(int maxn) {
+    if (maxn == 1) return {1, false};
+    if (maxn == 2) return {2, false};
+    return {2, true};
 }
 
-template <bool XB>
-int gemv_launch(int tpad, const GemvPlan& pl, GemvParams& gp, cudaStream_t s) {
-    switch (tpad) {
-        case 1: return gemv_launch_t<1, XB>(pl, gp, s);
-        case 2: return gemv_launch_t<2, XB>(pl, gp, s);
-        default: return gemv_launch_t<4, XB>(pl, gp, s);
-    }
+// Completes the plan for (PARTS, P) and launches one CTA per SM, or one per
+// unit when there are fewer.  `groups` bounds the expert groups the kernel can
+// see (their count may live on the device); dense launches pass 1.
+template <int PARTS, int TB, int P, bool XB, bool MOE, bool EARLY>
+int stream_launch_tp(const DeviceState* d, int groups, StreamParams sp, cudaStream_t s) {
+    const StreamPlan pl = stream_plan(sp.k, PARTS, P, sp.layout);
+    if (pl.stage_bytes > kStageBytes || pl.smem > static_cast<size_t>(kSmemLimit)) return OOMB_E_SHAPE;
+    sp.kc = pl.kc;
+    sp.ks = pl.ks;
+    sp.nsl = pl.nsl;
+    sp.rp = pl.rp;
+    sp.rpp = pl.rpp;
+    sp.nb = pl.nb;
+    sp.sr = pl.sr;
+    sp.stages = pl.stages;
+    sp.gpe = (sp.nrows + pl.rpp - 1) / pl.rpp;
+    const int64_t units = static_cast<int64_t>(groups) * sp.gpe;
+    const int grid = units < d->sms ? static_cast<int>(units > 0 ? units : 1) : d->sms;
+    if (sp.layout == OOMB_SCALE_128X128)
+        return launch(stream_kernel<PARTS, TB, P, XB, MOE, EARLY, true>, dim3(grid), dim3(kThreads), pl.smem, s, sp);
+    return launch(stream_kernel<PARTS, TB, P, XB, MOE, EARLY, false>, dim3(grid), dim3(kThreads), pl.smem, s, sp);
 }
 
-template <int PARTS, bool XB, bool EARLY>
-int moe_launch(int tb, int grid, const MoeParams& p, cudaStream_t s) {
-    if (tb == 1)
-        return launch(moe_fp8_kernel<PARTS, XB, EARLY, 1>, dim3(grid), dim3(kGemvThreads), moe_smem_bytes(), s, p);
-    return launch(moe_fp8_kernel<PARTS, XB, EARLY, kMoeTB>, dim3(grid), dim3(kGemvThreads), moe_smem_bytes(), s, p);
+// Units per pass: as many as kRedV partials per lane allow.
+template <int TB>
+constexpr int pass_len() {
+    return kRedV / (kRows * TB) > 0 ? kRedV / (kRows * TB) : 1;
 }
 
-int moe_grid(const DeviceState* d, int units) {
-    return units < d->sms ? (units > 0 ? units : 1) : d->sms;
+template <int PARTS, bool XB, bool MOE, bool EARLY>
+int stream_launch(const DeviceState* d, TbP tp, int groups, const StreamParams& sp, cudaStream_t s) {
+    if (tp.chunked) return stream_launch_tp<PARTS, 2, 1, XB, MOE, EARLY>(d, groups, sp, s);
+    if (tp.tb == 1) return stream_launch_tp<PARTS, 1, pass_len<1>(), XB, MOE, EARLY>(d, groups, sp, s);
+    return stream_launch_tp<PARTS, 2, pass_len<2>(), XB, MOE, EARLY>(d, groups, sp, s);
+}
+
+// gate/up + SwiGLU over expert groups; the group count is n_e or *n_e_dev
+// (then at most max_groups)
+int launch_gate_up(const DeviceState* d, const uint64_t* recs, const int32_t* off, const int32_t* assign_tok,
+                   const int32_t* n_e_dev, int n_e, int max_groups, const void* x, bool xbf16, float* h,
+                   const oomb_fp8_record* geo, int maxn, bool early, cudaStream_t stream) {
+    StreamParams sp{};
+    sp.recs = recs;
+    sp.off = off;
+    sp.assign_tok = assign_tok;
+    sp.n_e_dev = n_e_dev;
+    sp.n_e_host = n_e;
+    sp.w_off[0] = geo->gate_weight;
+    sp.w_off[1] = geo->up_weight;
+    sp.s_off[0] = geo->gate_scale;
+    sp.s_off[1] = geo->up_scale;
+    sp.layout = geo->layout;
+    sp.k = static_cast<int>(geo->hidden);
+    sp.nrows = static_cast<int>(geo->inter);
+    sp.x = x;
+    sp.y = h;
+    sp.err = d->err;
+    const int groups = n_e_dev ? max_groups : n_e;
+    const TbP tp = tb_p(maxn);
+    if (early)
+        return xbf16 ? stream_launch<2, true, true, true>(d, tp, groups, sp, stream)
+                     : stream_launch<2, false, true, true>(d, tp, groups, sp, stream);
+    return xbf16 ? stream_launch<2, true, true, false>(d, tp, groups, sp, stream)
+                 : stream_launch<2, false, true, false>(d, tp, groups, sp, stream);
+}
+
+// down projection over expert groups
+int launch_down(const DeviceState* d, const uint64_t* recs, const int32_t* off, const int32_t* n_e_dev, int n_e,
+                int max_groups, const float* h, float* y, const oomb_fp8_record* geo, int maxn, bool early,
+                cudaStream_t stream) {
+    StreamParams sp{};
+    sp.recs = recs;
+    sp.off = off;
+    sp.n_e_dev = n_e_dev;
+    sp.n_e_host = n_e;
+    sp.w_off[0] = sp.w_off[1] = geo->down_weight;
+    sp.s_off[0] = sp.s_off[1] = geo->down_scale;
+    sp.layout = geo->layout;
+    sp.k = static_cast<int>(geo->inter);
+    sp.nrows = static_cast<int>(geo->hidden);
+    sp.x = h;
+    sp.y = y;
+    sp.err = d->err;
+    const int groups = n_e_dev ? max_groups : n_e;
+    const TbP tp = tb_p(maxn);
+    return early ? stream_launch<1, false, true, true>(d, tp, groups, sp, stream)
+                 : stream_launch<1, false, true, false>(d, tp, groups, sp, stream);
 }
 
 }  // namespace
@@ -180,29 +251,27 @@ int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* sca
     if (t == 0) return OOMB_OK;
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
+    // Token chunks are reduced per stage, which needs whole rows in a stage:
+    // with K split over several stages (k > 4096) run 2-token launches.
+    const bool k_split = (k + 511) / 512 > 8;
+    const int per = k_split ? 2 : t;
     const size_t xs = x_dtype == OOMB_BF16 ? 2 : 4, ys = y_dtype == OOMB_BF16 ? 2 : 4;
-    for (int t0 = 0; t0 < t; t0 += kGemvMaxTokens) {
-        const int tc = t - t0 < kGemvMaxTokens ? t - t0 : kGemvMaxTokens;
-        const int tpad = gemv_tpad(tc);
-        const GemvPlan pl = gemv_plan(n, k, tpad, d->sms);
-        GemvParams gp{};
-        gp.x = static_cast<const uint8_t*>(x) + static_cast<size_t>(t0) * k * xs;
-        gp.q = q;
-        gp.scale = scale;
-        gp.y = static_cast<uint8_t*>(y) + static_cast<size_t>(t0) * n * ys;
-        gp.n = n;
-        gp.k = k;
-        gp.t = tc;
-        gp.layout = scale_layout;
-        gp.y_bf16 = y_dtype == OOMB_BF16;
-        gp.rg = pl.rg;
-        gp.kc = pl.kc;
-        gp.ks = pl.ks;
-        gp.nsl = pl.nsl;
-        gp.groups = pl.groups;
-        gp.err = d->err;
-        const int rc = x_dtype == OOMB_BF16 ? gemv_launch<true>(tpad, pl, gp, stream)
-                                            : gemv_launch<false>(tpad, pl, gp, stream);
+    for (int t0 = 0; t0 < t; t0 += per) {
+        const int tc = t - t0 < per ? t - t0 : per;
+        StreamParams sp{};
+        sp.q = q;
+        sp.scale = scale;
+        sp.layout = scale_layout;
+        sp.k = k;
+        sp.nrows = n;
+        sp.x = static_cast<const uint8_t*>(x) + static_cast<size_t>(t0) * k * xs;
+        sp.t = tc;
+        sp.y = static_cast<uint8_t*>(y) + static_cast<size_t>(t0) * n * ys;
+        sp.y_bf16 = y_dtype == OOMB_BF16;
+        sp.err = d->err;
+        const TbP tp = tb_p(tc);
+        const int rc = x_dtype == OOMB_BF16 ? stream_launch<1, true, false, false>(d, tp, 1, sp, stream)
+                                            : stream_launch<1, false, false, false>(d, tp, 1, sp, stream);
         if (rc) return rc;
     }
     return OOMB_OK;
@@ -256,68 +325,40 @@ int oomb_router_topk(const float* logits, int32_t* ids, float* weights, int t, i
 
 int oomb_moe_gate_up_fp8(const uint64_t* recs, const int32_t* off, const int32_t* assign_tok,
                          int n_experts, const void* x, int x_dtype, float* h,
-                         const oomb_fp8_record* geo, oomb_stream stream) {
+                         const oomb_fp8_record* geo, int max_per_expert, int flags,
+                         oomb_stream stream) {
     if (!recs || !off || !assign_tok || !x || !h || !geo) return OOMB_E_ARG;
+    if (flags & ~OOMB_TABLES_READY) return OOMB_E_ARG;
     if (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) return OOMB_E_ARG;
     if (geo->layout != OOMB_SCALE_1X128 && geo->layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
-    if (n_experts < 0 || geo->hidden <= 0 || geo->inter <= 0 || geo->hidden % 16 || geo->inter % 16 ||
-        geo->hidden > 4096)
+    if (n_experts < 0 || max_per_expert < 0 || geo->hidden <= 0 || geo->inter <= 0 || geo->hidden % 16 ||
+        geo->inter % 16 || geo->hidden > 4096)
         return OOMB_E_SHAPE;
     if ((geo->gate_weight | geo->up_weight | geo->gate_scale | geo->up_scale) & 15) return OOMB_E_ALIGN;
     if (!aligned16(x)) return OOMB_E_ALIGN;
     if (n_experts == 0) return OOMB_OK;
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
-    MoeParams p{};
-    p.recs = recs;
-    p.off = off;
-    p.assign_tok = assign_tok;
-    p.n_e_host = n_experts;
-    p.x = x;
-    p.out = h;
-    p.kdim = static_cast<int>(geo->hidden);
-    p.nrows = static_cast<int>(geo->inter);
-    p.w_off[0] = geo->gate_weight;
-    p.w_off[1] = geo->up_weight;
-    p.s_off[0] = geo->gate_scale;
-    p.s_off[1] = geo->up_scale;
-    p.layout = geo->layout;
-    moe_plan(p.kdim, 2, &p.rgp, &p.nsl);
-    p.gpe = (p.nrows + p.rgp - 1) / p.rgp;
-    p.err = d->err;
-    const int grid = moe_grid(d, n_experts * p.gpe);
-    return x_dtype == OOMB_BF16 ? moe_launch<2, true, false>(kMoeTB, grid, p, stream)
-                                : moe_launch<2, false, false>(kMoeTB, grid, p, stream);
+    return launch_gate_up(d, recs, off, assign_tok, nullptr, n_experts, n_experts, x, x_dtype == OOMB_BF16, h, geo,
+                          max_per_expert, (flags & OOMB_TABLES_READY) != 0, stream);
 }
 
 int oomb_moe_down_fp8(const uint64_t* recs, const int32_t* off, int n_experts, const float* h,
-                      float* y, const oomb_fp8_record* geo, oomb_stream stream) {
+                      float* y, const oomb_fp8_record* geo, int max_per_expert, int flags,
+                      oomb_stream stream) {
     if (!recs || !off || !h || !y || !geo) return OOMB_E_ARG;
+    if (flags & ~OOMB_TABLES_READY) return OOMB_E_ARG;
     if (geo->layout != OOMB_SCALE_1X128 && geo->layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
-    if (n_experts < 0 || geo->hidden <= 0 || geo->inter <= 0 || geo->hidden % 16 || geo->inter % 16 ||
-        geo->inter > 4096)
+    if (n_experts < 0 || max_per_expert < 0 || geo->hidden <= 0 || geo->inter <= 0 || geo->hidden % 16 ||
+        geo->inter % 16 || geo->inter > 4096)
         return OOMB_E_SHAPE;
     if ((geo->down_weight | geo->down_scale) & 15) return OOMB_E_ALIGN;
     if (!aligned16(h)) return OOMB_E_ALIGN;
     if (n_experts == 0) return OOMB_OK;
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
-    MoeParams p{};
-    p.recs = recs;
-    p.off = off;
-    p.n_e_host = n_experts;
-    p.x = h;
-    p.out = y;
-    p.kdim = static_cast<int>(geo->inter);
-    p.nrows = static_cast<int>(geo->hidden);
-    p.w_off[0] = p.w_off[1] = geo->down_weight;
-    p.s_off[0] = p.s_off[1] = geo->down_scale;
-    p.layout = geo->layout;
-    moe_plan(p.kdim, 1, &p.rgp, &p.nsl);
-    p.gpe = (p.nrows + p.rgp - 1) / p.rgp;
-    p.err = d->err;
-    const int grid = moe_grid(d, n_experts * p.gpe);
-    return moe_launch<1, false, false>(kMoeTB, grid, p, stream);
+    return launch_down(d, recs, off, nullptr, n_experts, n_experts, h, y, geo, max_per_expert,
+                       (flags & OOMB_TABLES_READY) != 0, stream);
 }
 
 int oomb_moe_combine_slots(const float* y, const int32_t* slot_assign, const float* w, void* out,
@@ -420,7 +461,6 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
     if (!d) return OOMB_E_DEVICE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const int E = L->experts, K = L->top_k, H = L->hidden;
-    const int I = static_cast<int>(L->geo.inter);
     const int A = t * K;
 
     // 1. router logits + top-k + grouping (one launch; the last CTA groups)
@@ -455,53 +495,24 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
                        : launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), smem, stream, rp);
         if (rc) return rc;
     }
-    // 2. gate/up + SiLU over the active experts
-    MoeParams gu{};
-    gu.recs = rp.recs_active;
-    gu.off = rp.off;
-    gu.assign_tok = rp.assign_tok;
-    gu.n_e_dev = rp.n_active;
-    gu.x = x;
-    gu.out = reinterpret_cast<float*>(ws + lay.h);
-    gu.kdim = H;
-    gu.nrows = I;
-    gu.w_off[0] = L->geo.gate_weight;
-    gu.w_off[1] = L->geo.up_weight;
-    gu.s_off[0] = L->geo.gate_scale;
-    gu.s_off[1] = L->geo.up_scale;
-    gu.layout = L->geo.layout;
-    moe_plan(H, 2, &gu.rgp, &gu.nsl);
-    gu.gpe = (I + gu.rgp - 1) / gu.rgp;
-    gu.err = d->err;
+    // 2. gate/up + SiLU over the active experts (an expert gets at most one
+    //    assignment per token, so at most t)
     const int max_e = A < E ? A : E;
-    const int tb = moe_tb(t);
-    rc = rp.x_bf16 ? moe_launch<2, true, false>(tb, moe_grid(d, max_e * gu.gpe), gu, stream)
-                   : moe_launch<2, false, false>(tb, moe_grid(d, max_e * gu.gpe), gu, stream);
+    float* h = reinterpret_cast<float*>(ws + lay.h);
+    float* y = reinterpret_cast<float*>(ws + lay.y);
+    rc = launch_gate_up(d, rp.recs_active, rp.off, rp.assign_tok, rp.n_active, 0, max_e, x, rp.x_bf16 != 0, h,
+                        &L->geo, t, false, stream);
     if (rc) return rc;
-    // 3. down (its producer starts streaming weights while gate/up finishes)
-    MoeParams dn{};
-    dn.recs = rp.recs_active;
-    dn.off = rp.off;
-    dn.n_e_dev = rp.n_active;
-    dn.x = gu.out;
-    dn.out = reinterpret_cast<float*>(ws + lay.y);
-    dn.kdim = I;
-    dn.nrows = H;
-    dn.w_off[0] = dn.w_off[1] = L->geo.down_weight;
-    dn.s_off[0] = dn.s_off[1] = L->geo.down_scale;
-    dn.layout = L->geo.layout;
-    moe_plan(I, 1, &dn.rgp, &dn.nsl);
-    dn.gpe = (H + dn.rgp - 1) / dn.rgp;
-    dn.err = d->err;
-    rc = moe_launch<1, false, true>(tb, moe_grid(d, max_e * dn.gpe), dn, stream);
+    // 3. down; its producer starts streaming weights while gate/up finishes
+    rc = launch_down(d, rp.recs_active, rp.off, rp.n_active, 0, max_e, h, y, &L->geo, t, true, stream);
     if (rc) return rc;
     // 4. slot-order combine
     const int64_t quads = static_cast<int64_t>(t) * H / 4;
     const dim3 cgrid(static_cast<unsigned>((quads + 255) / 256));
     return out_dtype == OOMB_BF16
-               ? launch(combine_slots_kernel<true>, cgrid, dim3(256), 0, stream, dn.out,
+               ? launch(combine_slots_kernel<true>, cgrid, dim3(256), 0, stream, static_cast<const float*>(y),
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K)
-               : launch(combine_slots_kernel<false>, cgrid, dim3(256), 0, stream, dn.out,
+               : launch(combine_slots_kernel<false>, cgrid, dim3(256), 0, stream, static_cast<const float*>(y),
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K);
 }
 

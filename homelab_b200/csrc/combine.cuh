@@ -1,0 +1,68 @@
+// combine.cuh - slot-order weighted combine and the shared-expert combine.
+#pragma once
+
+#include "common.cuh"
+
+namespace oomb {
+
+// out[t, c] = sum_s w[t, s] * y[slot[t, s], c] in slot order with fmaf
+// (moe_combine_slots, moe.cu:155-164).  Four columns per thread; the slot
+// indices and weights of a group of 8 slots are loaded before their rows so the
+// row loads are in flight together.
+template <bool OUT_BF16>
+__global__ void combine_slots_kernel(const float* y, const int32_t* slot, const float* w, void* out,
+                                     int T, int H, int K) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i >= static_cast<int64_t>(T) * H) return;
+    const int t = static_cast<int>(i / H), c = static_cast<int>(i % H);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < K; s0 += 8) {
+        int a[8];
+        float ws[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const bool ok = s0 + j < K;
+            a[j] = ok ? __ldcg(slot + t * K + s0 + j) : 0;
+            ws[j] = ok ? __ldcg(w + t * K + s0 + j) : 0.0f;
+        }
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            v[j] = s0 + j < K ? __ldcg(reinterpret_cast<const float4*>(y + static_cast<int64_t>(a[j]) * H + c))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (s0 + j < K) {
+                acc.x = fmaf(ws[j], v[j].x, acc.x);
+                acc.y = fmaf(ws[j], v[j].y, acc.y);
+                acc.z = fmaf(ws[j], v[j].z, acc.z);
+                acc.w = fmaf(ws[j], v[j].w, acc.w);
+            }
+        }
+    }
+    if (OUT_BF16) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<unsigned*>(&lo);
+        pk.y = *reinterpret_cast<unsigned*>(&hi);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + i) = pk;
+    } else {
+        *reinterpret_cast<float4*>(static_cast<float*>(out) + i) = acc;
+    }
+}
+
+// out = routed + sigmoid(gate_logit[t]) * shared (ops.cu:311-316).
+__global__ void moe_combine_kernel(const float* routed, const float* shared, const float* gate_logit,
+                                   float* out, int T, int H) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(T) * H) return;
+    const float g = gate_logit[i / H];
+    out[i] = routed[i] + (1.0f / (1.0f + expf(-g))) * shared[i];
+}
+
+}  // namespace oomb

@@ -73,45 +73,66 @@ struct RouteParams {
 };
 
 constexpr int kRouteThreads = 256;
-constexpr int kRouteTT = 4;  // tokens per warp task in the logits phase
+constexpr int kRouteTT = 4;        // tokens per warp task in the logits phase
+constexpr int kRouteMaxH = 4096;   // router rows held in registers up to this width
+constexpr int kRouteSmallE = 256;  // experts whose probabilities fit 8 per lane
 
-// Logits for rows e and tokens [t0, t0 + nt) (nt <= kRouteTT) in the canonical order.
+// One router row in registers: lane l holds columns 256*i + 8*l + j.
+struct RouterRow {
+    uint4 w[kRouteMaxH / 256];
+};
+
+__device__ __forceinline__ void router_row_load(const RouteParams& p, int e, int lane, RouterRow& r) {
+    const uint16_t* wr = p.w + static_cast<int64_t>(e) * p.H;
+#pragma unroll
+    for (int i = 0; i < kRouteMaxH / 256; i++) {
+        const int base = i * 256 + lane * 8;
+        r.w[i] = base < p.H ? __ldg(reinterpret_cast<const uint4*>(wr + base)) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// Logits of row e for tokens [t0, t0 + nt) (nt <= kRouteTT) in the canonical
+// order: per lane one fmaf chain over its columns in ascending order, then the
+// xor tree.
 template <bool XBF16>
-__device__ __forceinline__ void router_row(const RouteParams& p, int e, int t0, int nt, int lane) {
+__device__ __forceinline__ void router_row_dot(const RouteParams& p, const RouterRow& r, int e, int t0, int nt,
+                                               int lane) {
     float acc[kRouteTT];
 #pragma unroll
     for (int j = 0; j < kRouteTT; j++) acc[j] = 0.0f;
-    const uint16_t* wr = p.w + static_cast<int64_t>(e) * p.H;
-    for (int base = lane * 8; base < p.H; base += 256) {
-        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + base));
-        const unsigned ww[4] = {wv.x, wv.y, wv.z, wv.w};
-        float wf[8];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            wf[2 * i] = __uint_as_float(ww[i] << 16);
-            wf[2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
-        }
+    for (int i = 0; i < kRouteMaxH / 256; i++) {
+        const int base = i * 256 + lane * 8;
+        if (base < p.H) {
+            const unsigned ww[4] = {r.w[i].x, r.w[i].y, r.w[i].z, r.w[i].w};
+            float wf[8];
 #pragma unroll
-        for (int j = 0; j < kRouteTT; j++) {
-            if (j < nt) {
-                float xv[8];
-                const int64_t xi = static_cast<int64_t>(t0 + j) * p.H + base;
-                if (XBF16) {
-                    const uint4 a = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi));
-                    const unsigned aa[4] = {a.x, a.y, a.z, a.w};
+            for (int q = 0; q < 4; q++) {
+                wf[2 * q] = __uint_as_float(ww[q] << 16);
+                wf[2 * q + 1] = __uint_as_float(ww[q] & 0xffff0000u);
+            }
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        xv[2 * i] = __uint_as_float(aa[i] << 16);
-                        xv[2 * i + 1] = __uint_as_float(aa[i] & 0xffff0000u);
+            for (int j = 0; j < kRouteTT; j++) {
+                if (j < nt) {
+                    float xv[8];
+                    const int64_t xi = static_cast<int64_t>(t0 + j) * p.H + base;
+                    if (XBF16) {
+                        const uint4 a = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi));
+                        const unsigned aa[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            xv[2 * q] = __uint_as_float(aa[q] << 16);
+                            xv[2 * q + 1] = __uint_as_float(aa[q] & 0xffff0000u);
+                        }
+                    } else {
+                        const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi);
+                        const float4 a = __ldcg(xp), b = __ldcg(xp + 1);
+                        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+                        xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
                     }
-                } else {
-                    const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi));
-                    const float4 b = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi) + 1);
-                    xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
-                    xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
-                }
 #pragma unroll
-                for (int i = 0; i < 8; i++) acc[j] = __fmaf_rn(xv[i], wf[i], acc[j]);
+                    for (int q = 0; q < 8; q++) acc[j] = __fmaf_rn(xv[q], wf[q], acc[j]);
+                }
             }
         }
     }
@@ -122,52 +143,139 @@ __device__ __forceinline__ void router_row(const RouteParams& p, int e, int t0, 
     }
 }
 
-// Softmax top-k of one token by one warp (probabilities recomputed from the
-// logits on each pass, so any E fits).
+// Wide routers (hidden > kRouteMaxH): the same order streamed from memory.
+template <bool XBF16>
+__device__ __forceinline__ void router_row_wide(const RouteParams& p, int e, int t0, int nt, int lane) {
+    float acc[kRouteTT];
+#pragma unroll
+    for (int j = 0; j < kRouteTT; j++) acc[j] = 0.0f;
+    const uint16_t* wr = p.w + static_cast<int64_t>(e) * p.H;
+    for (int base = lane * 8; base < p.H; base += 256) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + base));
+        const unsigned ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        float wf[8];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            wf[2 * q] = __uint_as_float(ww[q] << 16);
+            wf[2 * q + 1] = __uint_as_float(ww[q] & 0xffff0000u);
+        }
+#pragma unroll
+        for (int j = 0; j < kRouteTT; j++) {
+            if (j < nt) {
+                float xv[8];
+                const int64_t xi = static_cast<int64_t>(t0 + j) * p.H + base;
+                if (XBF16) {
+                    const uint4 a = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi));
+                    const unsigned aa[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        xv[2 * q] = __uint_as_float(aa[q] << 16);
+                        xv[2 * q + 1] = __uint_as_float(aa[q] & 0xffff0000u);
+                    }
+                } else {
+                    const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi);
+                    const float4 a = __ldcg(xp), b = __ldcg(xp + 1);
+                    xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+                    xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+                }
+#pragma unroll
+                for (int q = 0; q < 8; q++) acc[j] = __fmaf_rn(xv[q], wf[q], acc[j]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kRouteTT; j++) {
+        const float v = xor_tree32(acc[j]);
+        if (j < nt && lane == 0) p.logits[static_cast<int64_t>(t0 + j) * p.E + e] = v;
+    }
+}
+
+// Softmax top-k of one token by one warp.  Lane l owns experts l, l+32, ...;
+// with E <= 256 their probabilities stay in registers.
 __device__ __forceinline__ void topk_token(const RouteParams& p, int t, int lane, int32_t* ids_sm) {
     const float* l = p.logits + static_cast<int64_t>(t) * p.E;
-    float mx = -__int_as_float(0x7f800000);
-    for (int i = lane; i < p.E; i += 32) mx = fmaxf(mx, __ldcg(l + i));
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    int my_id = 0;
+    float my_p = 0.0f, psum = 0.0f;
+    if (p.E <= kRouteSmallE) {
+        float pe[kRouteSmallE / 32];
+        float mx = NEG_INF;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float s = 0.0f;
-    for (int i = lane; i < p.E; i += 32) s = __fadd_rn(s, oomb_expf(__fsub_rn(__ldcg(l + i), mx)));
-    const float sum = xor_tree32(s);
-    // Each round scans this lane's experts; picked ones are remembered in a
-    // 32-bit mask per lane chunk (k <= 32 picks in total).
-    int picked[32];
-    float picked_p[32];
-    int npicked = 0;
-    float psum = 0.0f;
-    for (int r = 0; r < p.K; r++) {
-        float bv = -3.0f;
-        int bi = 0x7fffffff;
-        for (int i = lane; i < p.E; i += 32) {
-            bool used = false;
-            for (int q = 0; q < npicked; q++) used |= picked[q] == i;
-            const float pi = used ? -2.0f : __fdiv_rn(oomb_expf(__fsub_rn(__ldcg(l + i), mx)), sum);
-            if (pi > bv) { bv = pi; bi = i; }  // lane's experts ascend: ties keep the lower id
+        for (int j = 0; j < kRouteSmallE / 32; j++) {
+            const int e = lane + 32 * j;
+            pe[j] = e < p.E ? __ldcg(l + e) : NEG_INF;
+            mx = fmaxf(mx, pe[j]);
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kRouteSmallE / 32; j++) {
+            if (lane + 32 * j < p.E) {
+                pe[j] = oomb_expf(__fsub_rn(pe[j], mx));
+                s = __fadd_rn(s, pe[j]);
+            }
         }
-        picked[npicked] = bi;
-        picked_p[npicked] = bv;
-        npicked++;
+        const float sum = xor_tree32(s);
+#pragma unroll
+        for (int j = 0; j < kRouteSmallE / 32; j++) pe[j] = lane + 32 * j < p.E ? __fdiv_rn(pe[j], sum) : -3.0f;
+        for (int r = 0; r < p.K; r++) {
+            float bv = -3.0f;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < kRouteSmallE / 32; j++)
+                if (pe[j] > bv) { bv = pe[j]; bi = lane + 32 * j; }  // ascending ids: ties keep the lower
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+#pragma unroll
+            for (int j = 0; j < kRouteSmallE / 32; j++)
+                if (lane + 32 * j == bi) pe[j] = -2.0f;  // used entries sit below every probability
+            if (lane == r) { my_id = bi; my_p = bv; }
+            psum = __fadd_rn(psum, bv);
+        }
+    } else {
+        float mx = NEG_INF;
+        for (int i = lane; i < p.E; i += 32) mx = fmaxf(mx, __ldcg(l + i));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float s = 0.0f;
+        for (int i = lane; i < p.E; i += 32) s = __fadd_rn(s, oomb_expf(__fsub_rn(__ldcg(l + i), mx)));
+        const float sum = xor_tree32(s);
+        unsigned long long picked_mask = 0;  // picks found in this lane's experts: bit j for expert lane+32j (j < 64)
+        int picked_far[32];
+        int nfar = 0;
+        for (int r = 0; r < p.K; r++) {
+            float bv = -3.0f;
+            int bi = 0x7fffffff;
+            for (int i = lane, j = 0; i < p.E; i += 32, j++) {
+                bool used = j < 64 ? ((picked_mask >> j) & 1ull) != 0 : false;
+                for (int q = 0; q < nfar; q++) used |= picked_far[q] == i;
+                const float pi = used ? -2.0f : __fdiv_rn(oomb_expf(__fsub_rn(__ldcg(l + i), mx)), sum);
+                if (pi > bv) { bv = pi; bi = i; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            if ((bi & 31) == lane) {
+                const int j = bi >> 5;
+                if (j < 64) picked_mask |= 1ull << j;
+                else picked_far[nfar++] = bi;
+            }
+            if (lane == r) { my_id = bi; my_p = bv; }
+            psum = __fadd_rn(psum, bv);
+        }
     }
-    for (int r = 0; r < p.K; r++) psum = __fadd_rn(psum, picked_p[r]);
     if (lane < p.K) {
-        // lane r writes pick r (registers indexed through a shuffle-free select)
-        int id = 0;
-        float pp = 0.0f;
-        for (int r = 0; r < p.K; r++)
-            if (r == lane) { id = picked[r]; pp = picked_p[r]; }
-        p.ids[static_cast<int64_t>(t) * p.K + lane] = id;
-        p.weights[static_cast<int64_t>(t) * p.K + lane] = __fdiv_rn(pp, psum);
-        if (ids_sm) ids_sm[t * p.K + lane] = id;
+        p.ids[static_cast<int64_t>(t) * p.K + lane] = my_id;
+        p.weights[static_cast<int64_t>(t) * p.K + lane] = __fdiv_rn(my_p, psum);
+        if (ids_sm) ids_sm[t * p.K + lane] = my_id;
     }
 }
 
@@ -237,16 +345,34 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
     extern __shared__ __align__(16) int32_t rsm[];  // ids [T*K] | counts [E] | base [E]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps = kRouteThreads / 32;
-    pdl_wait();
-    pdl_launch_dependents();
 
     if (p.do_logits) {
         const int ttiles = (p.T + kRouteTT - 1) / kRouteTT;
         const int tasks = p.E * ttiles;
-        for (int task = blockIdx.x * nwarps + warp; task < tasks; task += gridDim.x * nwarps) {
+        int task = blockIdx.x * nwarps + warp;
+        // The router rows do not depend on the previous kernel: fetch the first
+        // task's row before waiting for it.
+        RouterRow row;
+        const bool narrow = p.H <= kRouteMaxH;
+        int row_e = -1;
+        if (narrow && task < tasks) {
+            row_e = task % p.E;
+            router_row_load(p, row_e, lane, row);
+        }
+        pdl_wait();
+        pdl_launch_dependents();
+        for (; task < tasks; task += gridDim.x * nwarps) {
             const int e = task % p.E, tt = task / p.E;
             const int t0 = tt * kRouteTT;
-            router_row<XBF16>(p, e, t0, min(kRouteTT, p.T - t0), lane);
+            if (narrow) {
+                if (e != row_e) {
+                    router_row_load(p, e, lane, row);
+                    row_e = e;
+                }
+                router_row_dot<XBF16>(p, row, e, t0, min(kRouteTT, p.T - t0), lane);
+            } else {
+                router_row_wide<XBF16>(p, e, t0, min(kRouteTT, p.T - t0), lane);
+            }
         }
         if (!p.do_topk) return;
         // The last CTA to finish its logits runs the rest (deterministic: the
@@ -259,6 +385,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         if (!last) return;
         __threadfence();
         if (threadIdx.x == 0) *p.ticket = 0u;
+    } else {
+        pdl_wait();
+        pdl_launch_dependents();
     }
     int32_t* ids_sm = p.do_group ? rsm : nullptr;
     if (p.do_group) {
@@ -267,8 +396,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         __syncthreads();
         group_assignments(p, ids_sm, rsm + p.T * p.K, rsm + p.T * p.K + p.E);
     } else {
-        for (int t = blockIdx.x * nwarps + warp; t < p.T; t += gridDim.x * nwarps)
-            topk_token(p, t, lane, nullptr);
+        for (int t = blockIdx.x * nwarps + warp; t < p.T; t += gridDim.x * nwarps) topk_token(p, t, lane, nullptr);
     }
 }
 

@@ -39,6 +39,12 @@ typedef struct CUstream_st* oomb_stream;
 #define OOMB_E_DEVICE (-6)    /* no usable sm_100 device */
 #define OOMB_E_WORKSPACE (-7) /* workspace smaller than the *_workspace_bytes figure */
 
+/* Flags of the expert entry points.  OOMB_TABLES_READY: recs, off and
+ * assign_tok were written before the kernel preceding this call in the stream
+ * started (by the host, or earlier), so the kernel may read them and start
+ * streaming weights before that kernel finishes. */
+#define OOMB_TABLES_READY 1
+
 /* Element types of activations and outputs. */
 #define OOMB_F32 0
 #define OOMB_BF16 1
@@ -90,9 +96,9 @@ int oomb_device_error(int* code, int clear);
  * accumulation.  Replaces Linear::gemm_fp8 (backend.rs:199-209; launch body
  * Gpu::gemm_fp8 / gemv / gemv_at, crates/oominf-cuda/src/linear.rs:35-81,
  * 223-350).  x and y are fp32 or bf16.  k % 16 == 0; q, scale, x and y
- * 16-byte aligned.  Steps of up to 8 tokens per launch run the CUDA-core
- * GEMV; larger t runs as successive 8-token launches.  Workspace: none
- * (pass NULL, 0). */
+ * 16-byte aligned.  One launch streams the weights once for all t tokens
+ * (CUDA cores; t <= 16 is the decode/verify range of linear.rs:131-134); for
+ * k > 4096 tokens go in launches of 2.  Workspace: none (pass NULL, 0). */
 int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* scale,
                   int scale_layout, void* y, int y_dtype, int t, int n, int k, void* workspace,
                   size_t workspace_bytes, oomb_stream stream);
@@ -117,15 +123,21 @@ int oomb_router_topk(const float* logits, int32_t* ids, float* weights, int t, i
  * its record is at recs[i]; tok(a) = assign_tok[a].  Replaces
  * Experts::moe_gate_up (backend.rs:827-836; experts.rs:43-93; moe.cu:55-106)
  * for FP8 records.  x: [*, hidden] fp32 or bf16; h: [A, inter] fp32.
- * hidden <= 4096, hidden % 16 == 0, inter % 16 == 0. */
+ * hidden <= 4096, hidden % 16 == 0, inter % 16 == 0.  max_per_expert: the
+ * largest assignment count of any group (Moe::run_group computes it for
+ * moe_tiled, moe.rs:739-740), or 0 if unknown; 1 selects the fastest path.
+ * flags: 0 or OOMB_TABLES_READY. */
 int oomb_moe_gate_up_fp8(const uint64_t* recs, const int32_t* off, const int32_t* assign_tok,
                          int n_experts, const void* x, int x_dtype, float* h,
-                         const oomb_fp8_record* geo, oomb_stream stream);
+                         const oomb_fp8_record* geo, int max_per_expert, int flags,
+                         oomb_stream stream);
 
 /* y[a, :] = h[a, :] . Wd^T for every assignment.  Replaces Experts::moe_down
- * (backend.rs:860-868; experts.rs:174-209; moe.cu:110-151).  inter <= 4096. */
+ * (backend.rs:860-868; experts.rs:174-209; moe.cu:110-151).  inter <= 4096;
+ * max_per_expert and flags as for oomb_moe_gate_up_fp8. */
 int oomb_moe_down_fp8(const uint64_t* recs, const int32_t* off, int n_experts, const float* h,
-                      float* y, const oomb_fp8_record* geo, oomb_stream stream);
+                      float* y, const oomb_fp8_record* geo, int max_per_expert, int flags,
+                      oomb_stream stream);
 
 /* out[t, c] = sum_s w[t, s] * y[slot_assign[t, s], c], summed in slot order
  * with fused multiply-adds (deterministic).  Replaces Experts::moe_combine_slots

@@ -72,11 +72,13 @@ def test_checks_run_before_launch():
     assert L.oomb_router_topk(fake, fake, fake, 1, 4, 8, None) == _lib.E_SHAPE
     # expert widths must be multiples of 16 (experts.rs:55-58), hidden <= 4096
     g = hb.Fp8Record(hidden=2048, inter=770, layout=1)
-    assert L.oomb_moe_gate_up_fp8(fake, fake, fake, 1, fake, 0, fake, C.byref(g), None) == _lib.E_SHAPE
+    assert L.oomb_moe_gate_up_fp8(fake, fake, fake, 1, fake, 0, fake, C.byref(g), 0, 0, None) == _lib.E_SHAPE
     g = hb.Fp8Record(hidden=8192, inter=768, layout=1)
-    assert L.oomb_moe_gate_up_fp8(fake, fake, fake, 1, fake, 0, fake, C.byref(g), None) == _lib.E_SHAPE
+    assert L.oomb_moe_gate_up_fp8(fake, fake, fake, 1, fake, 0, fake, C.byref(g), 0, 0, None) == _lib.E_SHAPE
+    g = hb.Fp8Record(hidden=2048, inter=768, layout=1)
+    assert L.oomb_moe_down_fp8(fake, fake, 1, fake, fake, C.byref(g), 0, 4, None) == _lib.E_ARG  # unknown flag
     g = hb.Fp8Record(hidden=2048, inter=768, layout=1, down_weight=8)
-    assert L.oomb_moe_down_fp8(fake, fake, 1, fake, fake, C.byref(g), None) == _lib.E_ALIGN
+    assert L.oomb_moe_down_fp8(fake, fake, 1, fake, fake, C.byref(g), 0, 0, None) == _lib.E_ALIGN
 
 
 def test_decode_workspace_size_and_checks():
