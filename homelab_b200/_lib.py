@@ -26,6 +26,7 @@ BF16 = 1
 SCALE_1X128 = 0
 SCALE_128X128 = 1
 TABLES_READY = 1
+NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
 
 
 class Fp8Record(C.Structure):
@@ -66,6 +67,7 @@ SIGNATURES = [
     ("oomb_moe_decode_workspace_bytes", Z, [I, C.POINTER(MoeLayer)]),
     ("oomb_moe_decode_fp8", I, [C.POINTER(MoeLayer), P, I, I, P, I, P, P, P, Z, S]),
     ("oomb_workspace_clear", I, [P, Z, S]),
+    ("oomb_moe_decode_fp8_noalloc", I, [C.POINTER(MoeLayer), P, I, I, P, I, P, P, S]),
     ("oomb_quantize_fp8", I, [P, I, I, I, P, P, S]),
 ]
 

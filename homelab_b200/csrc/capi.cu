@@ -529,3 +529,57 @@ int oomb_quantize_fp8(const uint16_t* w, int n, int k, int scale_layout, uint8_t
 }
 
 }  // extern "C"
+
+// ---- fused decode step without a caller workspace -----------------------------
+//
+// The same kernels as oomb_moe_decode_fp8, with their scratch in a fixed
+// device array instead of caller memory, so the call allocates nothing.
+namespace {
+
+__device__ __align__(256) uint8_t g_noalloc_scratch[OOMB_NOALLOC_SCRATCH_BYTES];
+
+struct NoallocState {
+    bool init = false;
+    bool ok = false;
+    uint8_t* scratch = nullptr;
+};
+
+NoallocState g_noalloc[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// One-time set-up per device, with that device current: look up the array's
+// address and zero its first 256 bytes (the arrival counter, which the route
+// kernel resets after every call).  Returns nullptr if set-up failed.
+uint8_t* noalloc_scratch(oomb_stream stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoallocState& s = g_noalloc[dev];
+    if (!s.init) {
+        s.init = true;
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) == cudaSuccess &&
+            cudaMemsetAsync(p, 0, 256, stream) == cudaSuccess) {
+            s.scratch = static_cast<uint8_t*>(p);
+            s.ok = true;
+        }
+    }
+    return s.ok ? s.scratch : nullptr;
+}
+
+}  // namespace
+
+extern "C" int oomb_moe_decode_fp8_noalloc(const oomb_moe_layer* layer, const void* x, int x_dtype, int t,
+                                           void* out, int out_dtype, int32_t* ids, float* weights,
+                                           oomb_stream stream) {
+    const int rc = check_layer(layer);
+    if (rc) return rc;
+    if (t < 0) return OOMB_E_SHAPE;
+    if (t > 0 && decode_layout(t, layer).total > static_cast<size_t>(OOMB_NOALLOC_SCRATCH_BYTES))
+        return OOMB_E_WORKSPACE;
+    if (!device_state()) return OOMB_E_DEVICE;
+    uint8_t* scratch = noalloc_scratch(stream);
+    if (!scratch) return OOMB_E_DEVICE;
+    return oomb_moe_decode_fp8(layer, x, x_dtype, t, out, out_dtype, ids, weights, scratch,
+                               OOMB_NOALLOC_SCRATCH_BYTES, stream);
+}

@@ -167,6 +167,30 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* layer, const void* x, int x_dtype,
                         size_t workspace_bytes, oomb_stream stream);
 int oomb_workspace_clear(void* workspace, size_t bytes, oomb_stream stream);
 
+/* ---- fused decode step that allocates nothing --------------------------- */
+/* No counterpart in the reference: an addition of this library.  For callers
+ * that cannot allocate or hold device memory where they call the decode step:
+ * cudaMalloc and cudaFree may synchronise the device, which a decode loop must
+ * not do, and some hosts (an engine whose device budget is fixed at start-up,
+ * an FFI caller with no device allocator) have no workspace to pass.  The step
+ * computes exactly what oomb_moe_decode_fp8 computes, with its scratch in one
+ * fixed device array of OOMB_NOALLOC_SCRATCH_BYTES per device inside this
+ * library; it calls no allocator.
+ *   - Limit: a call fits when oomb_moe_decode_workspace_bytes(t, layer) <=
+ *     OOMB_NOALLOC_SCRATCH_BYTES (8 MiB; with hidden 2048, 128 experts, top-8
+ *     and intermediate 768 that is t <= 92); larger calls return
+ *     OOMB_E_WORKSPACE before any launch.
+ *   - The first call on each device, made with that device current, does a
+ *     one-time set-up: it looks up the array's address and zeroes its arrival
+ *     counter (a 256-byte memset on `stream`).  Make that first call before
+ *     any stream capture.
+ *   - All calls on one device share the array: they must be ordered (one
+ *     stream, or otherwise serialised).  Overlapping calls race on the
+ *     scratch and corrupt each other's results. */
+#define OOMB_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+int oomb_moe_decode_fp8_noalloc(const oomb_moe_layer* layer, const void* x, int x_dtype, int t, void* out,
+                                int out_dtype, int32_t* ids, float* weights, oomb_stream stream);
+
 /* ---- weight preparation ------------------------------------------------- */
 /* The load-time quantizer on the device, byte-identical to fp8::quantize_blocks
  * (crates/oominf-core/src/fp8.rs:52-88) for OOMB_SCALE_1X128 and to its 2-D
