@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU work of the cpu_baseline / reference sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--profile", type=int, default=0, metavar="N",
+                    help="run N eager decode steps of the workload and exit (a small driver for ncu)")
     return ap.parse_args()
 
 
@@ -247,6 +249,13 @@ def run_ours(args, rank, world, local_rank):
 
     def step(i, x=None, o=None):
         gpu.moe_decode(layers[i % LAYERS][2], xs[i % NX] if x is None else x, B, out if o is None else o, ws)
+
+    if args.profile:
+        for i in range(args.profile):
+            step(i)
+        torch.cuda.synchronize()
+        assert gpu.device_error() == 0
+        return None, None
 
     # ---- warm-up (eager) ----
     for i in range(max(args.warmup, 3)):
@@ -466,6 +475,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     result, _ = run_ours(args, rank, world, local_rank)
+    if args.profile:
+        print(f"ran {args.profile} eager decode steps", flush=True)
+        return
     if rank == 0 and world == 1 and not args.no_cpu:
         per, threads, sample, _ = time_cpu(args.batch, args.cpu_seconds)
         result["cpu_baseline"] = {"value": args.batch / per, "unit": "tokens/s", "cores": threads,

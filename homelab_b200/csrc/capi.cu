@@ -65,7 +65,8 @@ std::unordered_map<const void*, size_t> g_attr_done[kMaxDevices];
 
 template <typename Kernel>
 bool set_smem(Kernel k, size_t bytes) {
-    if (bytes <= 48 * 1024) return true;
+    // the default limit covers static and dynamic shared memory together
+    if (bytes <= 40 * 1024) return true;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
     const void* key = reinterpret_cast<const void*>(k);
@@ -127,6 +128,7 @@ int stream_launch_tp(const DeviceState* d, int groups, StreamParams sp, cudaStre
     sp.nb = pl.nb;
     sp.sr = pl.sr;
     sp.stages = pl.stages;
+    sp.slot_bytes = pl.slot_bytes;
     sp.gpe = (sp.nrows + pl.rpp - 1) / pl.rpp;
     const int64_t units = static_cast<int64_t>(groups) * sp.gpe;
     const int grid = units < d->sms ? static_cast<int>(units > 0 ? units : 1) : d->sms;
@@ -296,11 +298,11 @@ int oomb_router_logits(const void* x, int x_dtype, const uint16_t* w, float* log
     p.E = e;
     p.do_logits = 1;
     p.err = d->err;
-    const int tasks = e * ((t + kRouteTT - 1) / kRouteTT);
-    int grid = (tasks + 7) / 8;
-    if (grid > 4 * d->sms) grid = 4 * d->sms;
-    return p.x_bf16 ? launch(route_kernel<true>, dim3(grid), dim3(kRouteThreads), 0, stream, p)
-                    : launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), 0, stream, p);
+    // one router row per warp
+    const int grid = (e + kRouteThreads / 32 - 1) / (kRouteThreads / 32);
+    const size_t smem = route_smem(t, hidden, e, 0, p.x_bf16 != 0, true, false, false).total;
+    return p.x_bf16 ? launch(route_kernel<true>, dim3(grid), dim3(kRouteThreads), smem, stream, p)
+                    : launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), smem, stream, p);
 }
 
 int oomb_router_topk(const float* logits, int32_t* ids, float* weights, int t, int e, int k,
@@ -320,7 +322,8 @@ int oomb_router_topk(const float* logits, int32_t* ids, float* weights, int t, i
     p.do_topk = 1;
     p.err = d->err;
     const int grid = (t + 7) / 8;
-    return launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), 0, stream, p);
+    const size_t smem = route_smem(t, 0, e, k, false, false, true, false).total;
+    return launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), smem, stream, p);
 }
 
 int oomb_moe_gate_up_fp8(const uint64_t* recs, const int32_t* off, const int32_t* assign_tok,
@@ -486,10 +489,9 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
     rp.do_logits = rp.do_topk = rp.do_group = 1;
     rp.err = d->err;
     {
-        const int tasks = E * ((t + kRouteTT - 1) / kRouteTT);
-        int grid = (tasks + 7) / 8;
-        if (grid > d->sms) grid = d->sms;
-        const size_t smem = (static_cast<size_t>(A) + 2 * static_cast<size_t>(E)) * 4;
+        // one router row per warp; the last CTA to finish runs top-k and grouping
+        const int grid = (E + kRouteThreads / 32 - 1) / (kRouteThreads / 32);
+        const size_t smem = route_smem(t, H, E, K, rp.x_bf16 != 0, true, true, true).total;
         if (smem > 200 * 1024) return OOMB_E_SHAPE;
         rc = rp.x_bf16 ? launch(route_kernel<true>, dim3(grid), dim3(kRouteThreads), smem, stream, rp)
                        : launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), smem, stream, rp);

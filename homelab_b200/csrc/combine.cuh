@@ -12,8 +12,10 @@ namespace oomb {
 template <bool OUT_BF16>
 __global__ void combine_slots_kernel(const float* y, const int32_t* slot, const float* w, void* out,
                                      int T, int H, int K) {
+    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_ENTRY);
     pdl_wait();
     pdl_launch_dependents();
+    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_WAITED);
     const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (i >= static_cast<int64_t>(T) * H) return;
     const int t = static_cast<int>(i / H), c = static_cast<int>(i % H);
@@ -52,6 +54,7 @@ __global__ void combine_slots_kernel(const float* y, const int32_t* slot, const 
     } else {
         *reinterpret_cast<float4*>(static_cast<float*>(out) + i) = acc;
     }
+    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
 }
 
 // out = routed + sigmoid(gate_logit[t]) * shared (ops.cu:311-316).

@@ -38,6 +38,27 @@ __device__ __forceinline__ void record_error(unsigned* err, unsigned code) {
     if (err) atomicCAS(err, 0u, code);
 }
 
+// Device timeline (built only with -DOOMB_TIMELINE): kernels stamp
+// %globaltimer at fixed points into a slot per (kind, event, CTA) with a plain
+// store (no atomics on the kernel's path).  Each launch overwrites the slots of
+// its kind, so after a replay of a chain of launches the table holds the last
+// launch of every kind: a host tool reads it to lay out where the chain spends
+// its time.
+enum : unsigned {
+    TL_ROUTE = 1, TL_GATE_UP = 2, TL_DOWN = 3, TL_COMBINE = 4, TL_GEMV = 5,
+    TL_ENTRY = 0, TL_WAITED = 1, TL_END = 2, TL_FIRST_COPY = 3, TL_FIRST_STAGE = 4, TL_LOGITS_DONE = 5,
+    TL_LAST_CTA = 6, TL_X_STAGED = 7, TL_TOPK_DONE = 8, TL_FIRST_META = 9, TL_LAST_COPY = 10,
+};
+#ifdef OOMB_TIMELINE
+constexpr int kTimelineKinds = 8, kTimelineEvents = 16, kTimelineCtas = 1024;
+__device__ unsigned long long g_timeline[kTimelineKinds][kTimelineEvents][kTimelineCtas];
+__device__ __forceinline__ void tl_mark(unsigned kind, unsigned event) {
+    if (blockIdx.x < kTimelineCtas) g_timeline[kind][event][blockIdx.x] = global_ns();
+}
+#else
+__device__ __forceinline__ void tl_mark(unsigned, unsigned) {}
+#endif
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

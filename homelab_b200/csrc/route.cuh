@@ -76,27 +76,46 @@ constexpr int kRouteThreads = 256;
 constexpr int kRouteTT = 4;        // tokens per warp task in the logits phase
 constexpr int kRouteMaxH = 4096;   // router rows held in registers up to this width
 constexpr int kRouteSmallE = 256;  // experts whose probabilities fit 8 per lane
+constexpr size_t kRouteXTileBytes = 64 * 1024;  // shared-memory tile of activations
+constexpr int kRouteRecsSmem = 1024;  // layers with at most this many experts stage their record table
 
 // One router row in registers: lane l holds columns 256*i + 8*l + j.
 struct RouterRow {
     uint4 w[kRouteMaxH / 256];
 };
 
+// A 16-byte load kept in program order with the dependency wait: issued
+// before griddepcontrol.wait, it overlaps the wait; its result is used after.
+__device__ __forceinline__ uint4 ld_prefetch_v4(const void* ptr) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr));
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_prefetch_u64(const void* ptr) {
+    unsigned long long v;
+    asm volatile("ld.global.nc.u64 %0, [%1];" : "=l"(v) : "l"(ptr));
+    return v;
+}
+
 __device__ __forceinline__ void router_row_load(const RouteParams& p, int e, int lane, RouterRow& r) {
     const uint16_t* wr = p.w + static_cast<int64_t>(e) * p.H;
 #pragma unroll
     for (int i = 0; i < kRouteMaxH / 256; i++) {
         const int base = i * 256 + lane * 8;
-        r.w[i] = base < p.H ? __ldg(reinterpret_cast<const uint4*>(wr + base)) : make_uint4(0, 0, 0, 0);
+        r.w[i] = base < p.H ? ld_prefetch_v4(wr + base) : make_uint4(0, 0, 0, 0);
     }
 }
 
 // Logits of row e for tokens [t0, t0 + nt) (nt <= kRouteTT) in the canonical
 // order: per lane one fmaf chain over its columns in ascending order, then the
-// xor tree.
+// xor tree.  The activations come from the CTA's shared-memory tile `xs`
+// (tokens from `xt0`, row stride p.H).
 template <bool XBF16>
-__device__ __forceinline__ void router_row_dot(const RouteParams& p, const RouterRow& r, int e, int t0, int nt,
-                                               int lane) {
+__device__ __forceinline__ void router_row_dot(const RouteParams& p, const RouterRow& r, const uint8_t* xs,
+                                               int xt0, int e, int t0, int nt, int lane) {
     float acc[kRouteTT];
 #pragma unroll
     for (int j = 0; j < kRouteTT; j++) acc[j] = 0.0f;
@@ -115,9 +134,9 @@ __device__ __forceinline__ void router_row_dot(const RouteParams& p, const Route
             for (int j = 0; j < kRouteTT; j++) {
                 if (j < nt) {
                     float xv[8];
-                    const int64_t xi = static_cast<int64_t>(t0 + j) * p.H + base;
+                    const int xi = (t0 + j - xt0) * p.H + base;
                     if (XBF16) {
-                        const uint4 a = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi));
+                        const uint4 a = *reinterpret_cast<const uint4*>(xs + static_cast<size_t>(xi) * 2);
                         const unsigned aa[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
                         for (int q = 0; q < 4; q++) {
@@ -125,8 +144,8 @@ __device__ __forceinline__ void router_row_dot(const RouteParams& p, const Route
                             xv[2 * q + 1] = __uint_as_float(aa[q] & 0xffff0000u);
                         }
                     } else {
-                        const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi);
-                        const float4 a = __ldcg(xp), b = __ldcg(xp + 1);
+                        const float4* xp = reinterpret_cast<const float4*>(xs + static_cast<size_t>(xi) * 4);
+                        const float4 a = xp[0], b = xp[1];
                         xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
                         xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
                     }
@@ -279,11 +298,87 @@ __device__ __forceinline__ void topk_token(const RouteParams& p, int t, int lane
     }
 }
 
+// Softmax top-k of tokens [t0, t1) by the whole CTA, E <= kRouteSmallE.
+// 1. Each warp computes the softmax of whole tokens in the canonical order
+//    of topk_token (lane l owns experts l, l+32, ...) into prob[token][E]
+//    (shared memory; NaN stored as -3, below every probability).
+// 2. Every thread takes (token, candidate) pairs and counts the experts that
+//    beat the candidate: e beats i when p_e > p_i, or p_e == p_i and e < i.
+//    The candidate beaten by exactly r others is the r-th pick of k argmax
+//    rounds with ties to the lower id (ops.cu:234-294).
+// 3. weights = p / (sum of the picked p in pick order).
+// Writes p.ids, p.weights and, if non-null, ids_sm.  prob: (t1 - t0) * E
+// floats; pick_id / pick_p: (t1 - t0) * K entries.
+__device__ void topk_block(const RouteParams& p, int t0, int t1, float* prob, int32_t* pick_id, float* pick_p,
+                           int32_t* ids_sm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int nwarps = kRouteThreads / 32;
+    constexpr int NJ = kRouteSmallE / 32;
+    const int nt = t1 - t0, E = p.E;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    for (int tl = warp; tl < nt; tl += nwarps) {
+        const float* l = p.logits + static_cast<int64_t>(t0 + tl) * E;
+        float pe[NJ];
+        float mx = NEG_INF;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            pe[j] = e < E ? __ldcg(l + e) : NEG_INF;
+            mx = fmaxf(mx, pe[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            if (lane + 32 * j < E) {
+                pe[j] = oomb_expf(__fsub_rn(pe[j], mx));
+                s = __fadd_rn(s, pe[j]);
+            }
+        }
+        const float sum = xor_tree32(s);
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            if (e < E) {
+                const float v = __fdiv_rn(pe[j], sum);
+                prob[tl * E + e] = v == v ? v : -3.0f;
+            }
+        }
+    }
+    __syncthreads();
+    for (int pr = threadIdx.x; pr < nt * E; pr += kRouteThreads) {
+        const int tl = pr / E, i = pr - tl * E;
+        const float* pt = prob + tl * E;
+        const float pi = pt[i];
+        int beats = 0;
+        for (int e = 0; e < i; e++) beats += pt[e] >= pi ? 1 : 0;
+        for (int e = i + 1; e < E; e++) beats += pt[e] > pi ? 1 : 0;
+        if (beats < p.K) {
+            pick_id[tl * p.K + beats] = i;
+            pick_p[tl * p.K + beats] = pi;
+        }
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < nt * p.K; o += kRouteThreads) {
+        const int tl = o / p.K, r = o - tl * p.K;
+        float psum = 0.0f;
+        for (int q = 0; q < p.K; q++) psum = __fadd_rn(psum, pick_p[tl * p.K + q]);
+        const int64_t gi = static_cast<int64_t>(t0 + tl) * p.K + r;
+        p.ids[gi] = pick_id[o];
+        p.weights[gi] = __fdiv_rn(pick_p[o], psum);
+        if (ids_sm) ids_sm[(t0 + tl) * p.K + r] = pick_id[o];
+    }
+}
+
 // Groups the T*K assignments by expert (counting sort, stable in slot order).
-// Runs on one CTA; ids in shared memory.  counts: E ints of shared scratch.
+// Runs on one CTA; ids in shared memory.  counts, base: E ints of shared
+// scratch; recs_sm: the layer's record addresses staged in shared memory, or
+// null to read them from p.recs_all.
 __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, int32_t* counts,
-                                  int32_t* base) {
+                                  int32_t* base, const uint64_t* recs_sm) {
     const int A = p.T * p.K;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int e = threadIdx.x; e < p.E; e += blockDim.x) counts[e] = 0;
     __syncthreads();
     for (int s = threadIdx.x; s < A; s += blockDim.x) {
@@ -292,9 +387,38 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
         else record_error(p.err, ERR_BAD_TABLE);
     }
     __syncthreads();
-    if (threadIdx.x < 32) {
-        // Exclusive scans over experts: assignment start and active index.
-        const int lane = threadIdx.x;
+    if (p.E <= kRouteThreads) {
+        // One expert per thread: exclusive scans of the assignment counts and of
+        // the active flags over the CTA (warp scans, then the warp totals).
+        __shared__ int wtot_a[kRouteThreads / 32], wtot_n[kRouteThreads / 32];
+        const int e = threadIdx.x;
+        const int c = e < p.E ? counts[e] : 0;
+        int inc_a = c, inc_n = c > 0 ? 1 : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int va = __shfl_up_sync(0xffffffffu, inc_a, o);
+            const int vn = __shfl_up_sync(0xffffffffu, inc_n, o);
+            if (lane >= o) { inc_a += va; inc_n += vn; }
+        }
+        if (lane == 31) { wtot_a[warp] = inc_a; wtot_n[warp] = inc_n; }
+        __syncthreads();
+        int pre_a = 0, pre_n = 0;
+        for (int w = 0; w < warp; w++) { pre_a += wtot_a[w]; pre_n += wtot_n[w]; }
+        const int start = pre_a + inc_a - c;
+        const int idx = pre_n + inc_n - (c > 0 ? 1 : 0);
+        if (c > 0) {
+            base[e] = start;
+            p.active[idx] = e;
+            p.off[idx] = start;
+            if (p.recs_all) p.recs_active[idx] = recs_sm ? recs_sm[e] : __ldcg(p.recs_all + e);
+        }
+        if (threadIdx.x == kRouteThreads - 1) {
+            p.off[pre_n + inc_n] = pre_a + inc_a;
+            *p.n_active = pre_n + inc_n;
+        }
+        __syncthreads();
+    } else if (threadIdx.x < 32) {
+        // Exclusive scans over experts, 32 at a time: assignment start and active index.
         int run_a = 0, run_n = 0;
         for (int e0 = 0; e0 < p.E; e0 += 32) {
             const int e = e0 + lane;
@@ -312,7 +436,7 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
                 base[e] = start;
                 p.active[idx] = e;
                 p.off[idx] = start;
-                if (p.recs_all) p.recs_active[idx] = p.recs_all[e];
+                if (p.recs_all) p.recs_active[idx] = recs_sm ? recs_sm[e] : __ldcg(p.recs_all + e);
             }
             run_a += __shfl_sync(0xffffffffu, inc_a, 31);
             run_n += __shfl_sync(0xffffffffu, inc_n, 31);
@@ -321,6 +445,8 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
             p.off[run_n] = run_a;
             *p.n_active = run_n;
         }
+    }
+    if (threadIdx.x < 32) {
         // Ranks in slot order, 32 slots at a time.
         for (int s0 = 0; s0 < A; s0 += 32) {
             const int s = s0 + lane;
@@ -340,40 +466,99 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
     }
 }
 
+// Shared memory of route_kernel:
+//   [x tile][recs E u64][pick ids PT*K][pick p PT*K][prob PT*E][ids T*K][counts E][base E]
+// (PT: tokens one CTA ranks: all T when it also groups, else kRouteThreads/32).
+struct RouteSmem {
+    int xtile_tokens;  // tokens of x staged per tile (narrow routers), 0 otherwise
+    size_t x_bytes, recs_off, pick_off, ids_off, total;
+};
+
+__host__ __device__ inline RouteSmem route_smem(int T, int H, int E, int K, bool x_bf16, bool logits, bool topk,
+                                                bool group) {
+    RouteSmem m{};
+    const size_t xb = x_bf16 ? 2 : 4;
+    if (logits && H <= kRouteMaxH) {
+        int tt = static_cast<int>(kRouteXTileBytes / (static_cast<size_t>(H) * xb)) / kRouteTT * kRouteTT;
+        if (tt < kRouteTT) tt = kRouteTT;
+        m.xtile_tokens = T < tt ? T : tt;
+        m.x_bytes = (static_cast<size_t>(m.xtile_tokens) * H * xb + 15) & ~static_cast<size_t>(15);
+    }
+    m.recs_off = m.x_bytes;
+    const size_t recs = group && E <= kRouteRecsSmem ? static_cast<size_t>(E) * 8 : 0;
+    m.pick_off = m.recs_off + recs;
+    const size_t pt = group ? static_cast<size_t>(T) : static_cast<size_t>(kRouteThreads / 32);
+    const size_t picks = topk && E <= kRouteSmallE ? (2 * pt * K + pt * E) * 4 : 0;
+    m.ids_off = m.pick_off + picks;
+    m.total = m.ids_off + (group ? (static_cast<size_t>(T) * K + 2 * static_cast<size_t>(E)) * 4 : 0);
+    return m;
+}
+
+// Logits phase: warp w of CTA c owns router row c*8 + w (one row per warp: the
+// host launches ceil(E/8) CTAs), fetched into registers before the dependency
+// wait.  After the wait the CTA stages the activations of a tile of tokens in
+// shared memory with one cooperative load and every warp takes its row's
+// dot products from there.  The last CTA to finish (atomic ticket) runs the
+// softmax top-k of every token and the grouping, with the layer's record
+// addresses already staged by every CTA before the wait.
 template <bool XBF16>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams p) {
-    extern __shared__ __align__(16) int32_t rsm[];  // ids [T*K] | counts [E] | base [E]
+    extern __shared__ __align__(16) uint8_t rsm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nwarps = kRouteThreads / 32;
+    constexpr int nwarps = kRouteThreads / 32;
+    const RouteSmem sm = route_smem(p.T, p.H, p.E, p.K, XBF16, p.do_logits != 0, p.do_topk != 0, p.do_group != 0);
+    const bool ranked = p.E <= kRouteSmallE;
+    int32_t* pick_id = reinterpret_cast<int32_t*>(rsm + sm.pick_off);
+    const int pt = p.do_group ? p.T : nwarps;
+    float* pick_p = reinterpret_cast<float*>(rsm + sm.pick_off) + pt * p.K;
+    float* prob = pick_p + pt * p.K;
+    uint64_t* recs_sm = (p.do_group && p.recs_all && p.E <= kRouteRecsSmem)
+                            ? reinterpret_cast<uint64_t*>(rsm + sm.recs_off) : nullptr;
+    int32_t* ids_sm = p.do_group ? reinterpret_cast<int32_t*>(rsm + sm.ids_off) : nullptr;
+    if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_ENTRY);
+
+    // The layer's record addresses do not depend on the previous kernel: every
+    // CTA fetches them before waiting (only the last CTA will use them).
+    uint64_t rec_pre[kRouteRecsSmem / kRouteThreads];
+    if (recs_sm) {
+#pragma unroll
+        for (int m = 0; m < kRouteRecsSmem / kRouteThreads; m++) {
+            const int e = threadIdx.x + m * kRouteThreads;
+            rec_pre[m] = e < p.E ? ld_prefetch_u64(reinterpret_cast<const unsigned long long*>(p.recs_all) + e) : 0ull;
+        }
+    }
 
     if (p.do_logits) {
-        const int ttiles = (p.T + kRouteTT - 1) / kRouteTT;
-        const int tasks = p.E * ttiles;
-        int task = blockIdx.x * nwarps + warp;
-        // The router rows do not depend on the previous kernel: fetch the first
-        // task's row before waiting for it.
-        RouterRow row;
+        const int e = blockIdx.x * nwarps + warp;
+        const bool has_row = e < p.E;
         const bool narrow = p.H <= kRouteMaxH;
-        int row_e = -1;
-        if (narrow && task < tasks) {
-            row_e = task % p.E;
-            router_row_load(p, row_e, lane, row);
-        }
+        // The router row does not depend on the previous kernel either.
+        RouterRow row;
+        if (narrow && has_row) router_row_load(p, e, lane, row);
         pdl_wait();
         pdl_launch_dependents();
-        for (; task < tasks; task += gridDim.x * nwarps) {
-            const int e = task % p.E, tt = task / p.E;
-            const int t0 = tt * kRouteTT;
-            if (narrow) {
-                if (e != row_e) {
-                    router_row_load(p, e, lane, row);
-                    row_e = e;
-                }
-                router_row_dot<XBF16>(p, row, e, t0, min(kRouteTT, p.T - t0), lane);
-            } else {
-                router_row_wide<XBF16>(p, e, t0, min(kRouteTT, p.T - t0), lane);
+        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_WAITED);
+        if (narrow) {
+            const int xb = XBF16 ? 2 : 4;
+            for (int xt0 = 0; xt0 < p.T; xt0 += sm.xtile_tokens) {
+                const int xn = min(sm.xtile_tokens, p.T - xt0);
+                // x rows [xt0, xt0 + xn) are contiguous: copy them 16 bytes a thread
+                const int chunks = xn * p.H * xb / 16;
+                const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
+                                                                  static_cast<size_t>(xt0) * p.H * xb);
+                uint4* dst = reinterpret_cast<uint4*>(rsm);
+                for (int c = threadIdx.x; c < chunks; c += kRouteThreads) dst[c] = __ldcg(src + c);
+                __syncthreads();
+                if (threadIdx.x == 0 && xt0 == 0) tl_mark(TL_ROUTE, TL_X_STAGED);
+                if (has_row)
+                    for (int t0 = xt0; t0 < xt0 + xn; t0 += kRouteTT)
+                        router_row_dot<XBF16>(p, row, rsm, xt0, e, t0, min(kRouteTT, xt0 + xn - t0), lane);
+                __syncthreads();
             }
+        } else if (has_row) {
+            for (int t0 = 0; t0 < p.T; t0 += kRouteTT) router_row_wide<XBF16>(p, e, t0, min(kRouteTT, p.T - t0), lane);
         }
+        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_LOGITS_DONE);
         if (!p.do_topk) return;
         // The last CTA to finish its logits runs the rest (deterministic: the
         // work it does depends only on the logits, not on which CTA it is).
@@ -384,17 +569,37 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         __syncthreads();
         if (!last) return;
         __threadfence();
-        if (threadIdx.x == 0) *p.ticket = 0u;
+        if (threadIdx.x == 0) {
+            *p.ticket = 0u;
+            tl_mark(TL_ROUTE, TL_LAST_CTA);
+        }
     } else {
         pdl_wait();
         pdl_launch_dependents();
     }
-    int32_t* ids_sm = p.do_group ? rsm : nullptr;
     if (p.do_group) {
+        if (recs_sm) {
+#pragma unroll
+            for (int m = 0; m < kRouteRecsSmem / kRouteThreads; m++) {
+                const int e = threadIdx.x + m * kRouteThreads;
+                if (e < p.E) recs_sm[e] = rec_pre[m];
+            }
+        }
         // grouping needs every token's picks in one CTA
-        for (int t = warp; t < p.T; t += nwarps) topk_token(p, t, lane, ids_sm);
+        if (ranked) {
+            topk_block(p, 0, p.T, prob, pick_id, pick_p, ids_sm);
+        } else {
+            for (int t = warp; t < p.T; t += nwarps) topk_token(p, t, lane, ids_sm);
+        }
         __syncthreads();
-        group_assignments(p, ids_sm, rsm + p.T * p.K, rsm + p.T * p.K + p.E);
+        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_TOPK_DONE);
+        group_assignments(p, ids_sm, ids_sm + p.T * p.K, ids_sm + p.T * p.K + p.E, recs_sm);
+        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_END);
+    } else if (ranked) {
+        for (int t0 = blockIdx.x * nwarps; t0 < p.T; t0 += gridDim.x * nwarps) {
+            topk_block(p, t0, min(p.T, t0 + nwarps), prob, pick_id, pick_p, nullptr);
+            __syncthreads();
+        }
     } else {
         for (int t = blockIdx.x * nwarps + warp; t < p.T; t += gridDim.x * nwarps) topk_token(p, t, lane, nullptr);
     }

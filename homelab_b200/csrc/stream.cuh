@@ -10,9 +10,10 @@
 // "units" (a unit is one row group: RPP rows of each part, all K columns).
 // Warp roles:
 //   warp 8 (copy producer, one lane): streams each unit's rows (contiguous in
-//     row-major q) into a ring of three 32 KB shared-memory stages with
-//     cp.async.bulk, completed on mbarriers; consumers release stages through a
-//     second set of mbarriers.
+//     row-major q) into a ring of shared-memory stages (up to 32 KB each, as
+//     many as fit the CTA's half of shared memory) with cp.async.bulk,
+//     completed on mbarriers; consumers release stages through a second set of
+//     mbarriers.
 //   warp 9 (metadata producer): for every pass of P units it loads the units'
 //     assignment ranges and block-scale rows into a ring of shared tables,
 //     handshaked with mbarriers, so consumers never wait on L2 for them.
@@ -29,7 +30,7 @@
 //   reduces them (multi-value butterfly), the slabs are added in slab order
 //   through shared memory (deterministic) and the pass's outputs are written.
 // Kernels signal dependents at entry; the dense GEMV and the EARLY expert
-// variant stream weights before griddepcontrol.wait.
+// variant stream weights and load their unit tables before griddepcontrol.wait.
 #pragma once
 
 #include "common.cuh"
@@ -43,7 +44,7 @@ namespace oomb {
 #define OOMB_STREAM_ROWS 8
 #endif
 #ifndef OOMB_STREAM_STAGES
-#define OOMB_STREAM_STAGES 3
+#define OOMB_STREAM_STAGES 6
 #endif
 #ifndef OOMB_STREAM_CTAS_PER_SM
 #define OOMB_STREAM_CTAS_PER_SM 2
@@ -51,8 +52,8 @@ namespace oomb {
 constexpr int kWarps = OOMB_STREAM_WARPS;    // consumer warps
 constexpr int kThreads = (kWarps + 2) * 32;  // + copy producer + metadata producer
 constexpr int kRows = OOMB_STREAM_ROWS;      // rows per consumer warp per stage
-constexpr int kStageBytes = 32 * 1024;
-constexpr int kMaxStages = OOMB_STREAM_STAGES;
+constexpr int kStageBytes = 32 * 1024;  // largest stage
+constexpr int kMaxStages = OOMB_STREAM_STAGES;  // ring depth limit (smaller stages get more of them)
 constexpr int kRedV = 16;  // partials per lane per pass (kRows x P x TB)
 // A stage holds kRows rows of every consumer warp's 512-column slab.
 static_assert(kWarps * kRows * 512 <= kStageBytes, "a stage must fit its shared-memory slot");
@@ -69,10 +70,11 @@ struct StreamPlan {
     int sr;      // scale rows kept per unit and part (one block row for 128x128, RPP rows for 1x128)
     int stages;  // ring depth
     int stage_bytes;  // bytes one unit's K-stage occupies (<= kStageBytes)
+    int slot_bytes;   // ring slot: stage_bytes rounded up to 1 KB
     size_t smem;
 };
 
-// Shared-memory layout: [stages x 32 KB][full][empty][meta_full][meta_empty]
+// Shared-memory layout: [stages x slot_bytes][full][empty][meta_full][meta_empty]
 // [red 2 x kWarps x kRedV][meta kMetaBufs x (P x 4 ints + P x PARTS x SR x NB floats)]
 // [chunk headers 2 x 4 ints]
 inline size_t stream_meta_bytes(int P, int parts, int sr, int nb) {
@@ -90,11 +92,13 @@ inline StreamPlan stream_plan(int k, int parts, int P, int layout) {
     p.nb = (k + 127) / 128;
     p.sr = layout ? 1 : p.rpp;  // unit sizes divide 128: one block row per unit
     p.stage_bytes = parts * p.rpp * (p.kc < k ? p.kc : k);
+    p.slot_bytes = (p.stage_bytes + 1023) & ~1023;
     const size_t fixed = (2 * kMaxStages + 2 * kMetaBufs) * sizeof(uint64_t) + 2 * kWarps * kRedV * sizeof(float) +
                          kMetaBufs * stream_meta_bytes(P, parts, p.sr, p.nb) + 8 * sizeof(int) + 128;
+    // as many slots as fit the CTA's share of shared memory
     p.stages = kMaxStages;
-    while (p.stages > 2 && static_cast<size_t>(p.stages) * kStageBytes + fixed > kSmemLimit) p.stages--;
-    p.smem = static_cast<size_t>(p.stages) * kStageBytes + fixed;
+    while (p.stages > 2 && static_cast<size_t>(p.stages) * p.slot_bytes + fixed > kSmemLimit) p.stages--;
+    p.smem = static_cast<size_t>(p.stages) * p.slot_bytes + fixed;
     return p;
 }
 
@@ -112,7 +116,7 @@ struct StreamParams {
     int layout;  // 0: 1x128, 1: 128x128
     // shape and plan
     int k, nrows;  // columns; rows per part
-    int kc, ks, nsl, rp, rpp, nb, sr, stages;
+    int kc, ks, nsl, rp, rpp, nb, sr, stages, slot_bytes;
     int gpe;  // units per expert group (dense: units in total)
     // activations and outputs
     const void* x;  // dense: [t, k]; gate/up: [*, k] rows picked by assign_tok; down: h [A, k] fp32
@@ -320,10 +324,12 @@ __device__ __forceinline__ void reduce_write(const StreamParams& p, const float 
 template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool EARLY, bool BLK>
 __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kernel(const StreamParams p) {
     static_assert(kRows * P * TB <= kRedV, "too many partials per lane");
+    constexpr unsigned TLK = !MOE ? TL_GEMV : (PARTS == 2 ? TL_GATE_UP : TL_DOWN);
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = p.stages;
     uint8_t* stage_buf = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
+    const int slot_bytes = p.slot_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * slot_bytes);
     uint64_t* empty = full + kMaxStages;
     uint64_t* mfull = empty + kMaxStages;
     uint64_t* mempty = mfull + kMetaBufs;
@@ -348,11 +354,14 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
             mbar_init(&mempty[i], kWarps);
         }
         fence_barrier_init();
+        tl_mark(TLK, TL_ENTRY);
     }
     __syncthreads();
 
     if (warp == kWarps) {
         // ================= copy producer =================
+        // weights and (dense, or tables written two launches back) unit tables do
+        // not depend on the previous kernel
         if (MOE && !EARLY) pdl_wait();
         pdl_launch_dependents();
         if (lane != 0) return;
@@ -385,8 +394,9 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
                     const int nr = min(p.rpp, p.nrows - row0);
                     const int kc0 = ks * p.kc;
                     const int kcl = min(p.kc, p.k - kc0);
-                    uint8_t* dst = stage_buf + slot * kStageBytes;
+                    uint8_t* dst = stage_buf + slot * slot_bytes;
                     mbar_arrive_expect_tx(&full[slot], static_cast<unsigned>(PARTS * nr * kcl));
+                    if (s == 0) tl_mark(TLK, TL_FIRST_COPY);
 #pragma unroll
                     for (int part = 0; part < PARTS; part++) {
                         const uint8_t* src = (MOE ? rec + (part ? p.w_off[1] : p.w_off[0]) : rec) +
@@ -403,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
                 }
             }
         }
+        tl_mark(TLK, TL_LAST_COPY);
         if (!ok) {
             for (int d = (s > S ? s - S : 0); d < s; d++)
                 mbar_wait(&full[d % S], (d / S) & 1, p.err, ERR_DRAIN_WAIT);
@@ -412,7 +423,8 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
 
     if (warp == kWarps + 1) {
         // ================= metadata producer =================
-        pdl_wait();
+        // block scales are weights; the unit tables are as ready as for the copy producer
+        if (MOE && !EARLY) pdl_wait();
         pdl_launch_dependents();
         int u0, u1;
         cta_units(p, MOE, u0, u1);
@@ -476,6 +488,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
     // ================= consumers =================
     pdl_wait();
     pdl_launch_dependents();
+    if (threadIdx.x == 0) tl_mark(TLK, TL_WAITED);
     int u0, u1;
     cta_units(p, MOE, u0, u1);
     if (u1 <= u0) return;
@@ -502,6 +515,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
         const int pn = min(P, u1 - pf);
         const int buf = q % kMetaBufs;
         if (!mbar_wait(&mfull[buf], (q / kMetaBufs) & 1, p.err, ERR_FULL_WAIT)) return;
+        if (q == 0 && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_META);
         const int* hdr = meta + buf * meta_stride;
         const float* sct = reinterpret_cast<const float*>(hdr + meta_ints);
         float acc[P][kRows][TB];
@@ -549,7 +563,8 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
                     const int key0 = MOE ? 0 : ks;
                     const int slot = s % S;
                     if (!mbar_wait(&full[slot], (s / S) & 1, p.err, ERR_FULL_WAIT)) return;
-                    const uint8_t* base = stage_buf + slot * kStageBytes + ccol;
+                    if (s == 0 && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_STAGE);
+                    const uint8_t* base = stage_buf + slot * slot_bytes + ccol;
                     for (int a0 = a_begin; a0 < a_end; a0 += TB) {
                         const int nb = min(TB, a_end - a0);
                         if (x_key0 != key0 || x_key1 != a0) {
@@ -620,6 +635,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
         __syncwarp();
         if (lane == 0) mbar_arrive(&mempty[buf]);
     }
+    if (threadIdx.x == 0) tl_mark(TLK, TL_END);
 }
 
 }  // namespace oomb
