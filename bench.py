@@ -338,11 +338,14 @@ def run_ours(args, rank, world, local_rank):
     del ge_main, ge_rem
 
     # ---- roofline of the dominant kernel: gate/up+SiLU over the 8 experts of a step ----
+    step_bytes = E * H * 2 + 8 * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
     roof = measure_gate_up(gpu, layers, dev, s, B, LAYERS)
     gemv1 = measure_gemv_config1(gpu, dev, s)
+    del layers
+    torch.cuda.empty_cache()
+    mlp3 = measure_mlp_config3(gpu, dev, s) if world == 1 else None
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
-    step_bytes = E * H * 2 + 8 * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
 
     result = None
     if rank == 0:
@@ -360,6 +363,7 @@ def run_ours(args, rank, world, local_rank):
             "gemv_config1": {"workload": "config1: 4096x4096 e4m3, 128x128 scales, x bf16 batch 1, bf16 out",
                              "achieved_gbs": gemv1["gbs"], "frac": gemv1["gbs"] / peak, "launch_us": gemv1["us"],
                              "algorithmic_bytes_per_launch": gemv1["bytes"]},
+            "batched_dense_config3": mlp3,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
             "gpu_launches": 4 * K,
@@ -416,6 +420,68 @@ def measure_gate_up(gpu, layers, dev, s, B, LAYERS, launches=400):
     nbytes = n_e * (2 * I * H + 2 * scale_bytes(I, H, geo.layout)) + n_e * H * 2 + n_e * I * 4
     us = best * 1e3
     return {"gbs": nbytes / (us * 1e-6) / 1e9, "bytes": nbytes, "us": us}
+
+
+def measure_mlp_config3(gpu, dev, s, batches=(1, 4, 16, 64), steps=24):
+    """Llama-3-8B MLP, fused gate/up FP8 W [2 x 14336, 4096] +
+    SwiGLU + down FP8 W [4096, 14336], 128x128 block scales, x bf16 [B, 4096].
+    Two weight copies alternate (352 MB, beyond L2).  One tcgen05 workspace per
+    shape: batches of 2+ tokens run on the tensor cores, one token on the
+    CUDA-core stream (the GEMV -> tcgen05 crossover)."""
+    import torch
+
+    import homelab_b200 as hb
+    H, F = 4096, 14336
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    mats = []
+    for c in range(2):
+        pair = []
+        for (n, k) in ((2 * F, H), (H, F)):
+            w = (torch.randn((n, k), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+            pair.append(gpu.quantize_fp8(w.view(torch.int16), n, k, hb.SCALE_128X128))
+            del w
+        mats.append(pair)
+    torch.cuda.empty_cache()
+    wbytes = 2 * F * H + H * F + ((2 * F // 128) * (H // 128) + (H // 128) * (F // 128)) * 4
+    out = {}
+    for B in batches:
+        x = torch.randn((B, H), generator=gen, device=dev).to(torch.bfloat16)
+        gu = torch.empty((B, 2 * F), dtype=torch.float32, device=dev)
+        hh = torch.empty((B, F), dtype=torch.bfloat16, device=dev)
+        y = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+        ws1 = gpu.gemm_fp8_workspace(B, 2 * F, H) if B >= 2 else None
+        ws2 = gpu.gemm_fp8_workspace(B, H, F) if B >= 2 else None
+
+        def mlp(i):
+            (q1, s1), (q2, s2) = mats[i % 2]
+            gpu.gemm_fp8(x, q1, s1, gu, B, 2 * F, H, hb.SCALE_128X128, ws1)
+            gpu.silu_mul_rows(gu, hh, B, F)
+            gpu.gemm_fp8(hh, q2, s2, y, B, H, F, hb.SCALE_128X128, ws2)
+
+        for i in range(4):
+            mlp(i)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(steps):
+                mlp(i)
+        g.replay()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = float("inf")
+        for _ in range(3):
+            with torch.cuda.stream(s):
+                ev0.record(s)
+                g.replay()
+                ev1.record(s)
+            ev1.synchronize()
+            best = min(best, ev0.elapsed_time(ev1) / steps)
+        us = best * 1e3
+        nbytes = wbytes + B * (H * 2 + 2 * F * 4 * 2 + F * 2 * 2 + H * 2)
+        out[f"B{B}"] = {"us_per_mlp": us, "tokens_per_s": B / (us * 1e-6), "gbs": nbytes / (us * 1e-6) / 1e9,
+                        "path": "tcgen05" if B >= 2 else "cuda-core stream"}
+        del g
+    return out
 
 
 def measure_gemv_config1(gpu, dev, s, copies=16, launches=320):

@@ -27,6 +27,8 @@ SCALE_1X128 = 0
 SCALE_128X128 = 1
 TABLES_READY = 1
 NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
+Q_ROWS = 0
+Q_TILES = 1
 
 
 class Fp8Record(C.Structure):
@@ -58,6 +60,10 @@ SIGNATURES = [
     ("oomb_status_string", C.c_char_p, [I]),
     ("oomb_device_error", I, [C.POINTER(C.c_int), I]),
     ("oomb_gemm_fp8", I, [P, I, P, P, I, P, I, I, I, I, P, Z, S]),
+    ("oomb_gemm_fp8_workspace_bytes", Z, [I, I, I, I]),
+    ("oomb_gemm_fp8_tc", I, [P, I, P, I, P, I, P, I, I, I, I, P, Z, S]),
+    ("oomb_pack_fp8_tiles", I, [P, I, I, P, S]),
+    ("oomb_silu_mul_rows", I, [P, P, I, I, I, S]),
     ("oomb_router_logits", I, [P, I, P, P, I, I, I, S]),
     ("oomb_router_topk", I, [P, P, P, I, I, I, S]),
     ("oomb_moe_gate_up_fp8", I, [P, P, P, I, P, I, P, C.POINTER(Fp8Record), I, I, S]),

@@ -48,10 +48,40 @@ class Gpu:
         return torch.cuda.current_stream(self.device).cuda_stream
 
     # ---- Linear -------------------------------------------------------------------------
-    def gemm_fp8(self, x, q, scale, y, t: int, n: int, k: int, layout: int = SCALE_128X128):
-        """y[t, n] = x[t, k] @ w[n, k]^T for FP8 w (Linear::gemm_fp8, backend.rs:199-209)."""
+    def gemm_fp8(self, x, q, scale, y, t: int, n: int, k: int, layout: int = SCALE_128X128, workspace=None):
+        """y[t, n] = x[t, k] @ w[n, k]^T for FP8 w (Linear::gemm_fp8, backend.rs:199-209).
+        With a workspace (gemm_fp8_workspace), batches of 2+ tokens run on the tensor cores."""
         check(self.L.oomb_gemm_fp8(_ptr(x), _dtype_code(x), _ptr(q), _ptr(scale), layout, _ptr(y),
-                                   _dtype_code(y), t, n, k, None, 0, self._stream()), "gemm_fp8")
+                                   _dtype_code(y), t, n, k, _ptr(workspace) if workspace is not None else None,
+                                   workspace.numel() if workspace is not None else 0, self._stream()), "gemm_fp8")
+
+    def silu_mul_rows(self, gu, y, rows: int, n: int):
+        """y[r, i] = silu(gu[r, i]) * gu[r, n + i] (silu_mul_rows, ops.cu:302-309)."""
+        check(self.L.oomb_silu_mul_rows(_ptr(gu), _ptr(y), _dtype_code(y), rows, n, self._stream()),
+              "silu_mul_rows")
+
+    def gemm_fp8_workspace(self, t: int, n: int, k: int, x_dtype=torch.bfloat16) -> torch.Tensor:
+        """A zeroed workspace for gemm_fp8_tc (split-K partial sums and counters)."""
+        n_bytes = int(self.L.oomb_gemm_fp8_workspace_bytes(t, n, k, BF16 if x_dtype == torch.bfloat16 else F32))
+        if n_bytes == 0:
+            raise ValueError("shape not supported by the tensor-core path")
+        ws = torch.empty(n_bytes, dtype=torch.uint8, device=self.device)
+        check(self.L.oomb_workspace_clear(_ptr(ws), n_bytes, self._stream()), "workspace_clear")
+        return ws
+
+    def gemm_fp8_tc(self, x, q, scale, y, t: int, n: int, k: int, layout: int, workspace, tiles: bool = False):
+        """y = x . w^T on the tensor cores (tcgen05); n % 128 == k % 128 == 0, t <= 64.
+        tiles: q is in the packed tile layout of pack_fp8_tiles."""
+        check(self.L.oomb_gemm_fp8_tc(_ptr(x), _dtype_code(x), _ptr(q), _lib.Q_TILES if tiles else _lib.Q_ROWS,
+                                      _ptr(scale), layout, _ptr(y), _dtype_code(y), t, n, k, _ptr(workspace),
+                                      workspace.numel(), self._stream()), "gemm_fp8_tc")
+
+    def pack_fp8_tiles(self, q, n: int, k: int, tiles=None):
+        """The packed 128 x 128 tile layout of a row-major e4m3 matrix (load time)."""
+        if tiles is None:
+            tiles = torch.empty(n * k, dtype=torch.uint8, device=self.device)
+        check(self.L.oomb_pack_fp8_tiles(_ptr(q), n, k, _ptr(tiles), self._stream()), "pack_fp8_tiles")
+        return tiles
 
     def router_logits(self, x, w_bf16, logits, t: int, e: int, hidden: int):
         """logits = x . W^T for the bf16 router (moe.rs:289-298), canonical order."""

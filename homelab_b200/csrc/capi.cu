@@ -17,6 +17,7 @@
 #include "quant.cuh"
 #include "route.cuh"
 #include "stream.cuh"
+#include "tc.cuh"
 
 namespace oomb {
 namespace {
@@ -203,12 +204,183 @@ int launch_down(const DeviceState* d, const uint64_t* recs, const int32_t* off, 
                  : stream_launch<1, false, true, false>(d, tp, groups, sp, stream);
 }
 
+// ---- tensor-core path ------------------------------------------------------------
+
+// cuTensorMapEncodeTiled, fetched once from the driver through the runtime (the
+// library links only the CUDA runtime).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(f);
+    }();
+    return fn;
+}
+
+// Tensor map of an e4m3 matrix [rows, k] (row-major) in 128 x 128 boxes with
+// the 128-byte swizzle the MMA descriptors expect.  Packed tiles are mapped as
+// a [tiles * 128, 128] matrix (k = 128 there).
+bool encode_fp8_tiles(CUtensorMap* map, const uint8_t* q, int rows, int k) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
+    const cuuint32_t box[2] = {kTcTile, kTcTile};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    // As CUTLASS does for drivers up to 13.1 on tensors under 128 KiB.
+    int drv = 0;
+    if (cudaDriverGetVersion(&drv) == cudaSuccess && drv <= 13010 && static_cast<size_t>(rows) * k < 131072)
+        reinterpret_cast<uint64_t*>(map)[1] &= ~(1ull << 21);
+    return true;
+}
+
+struct TcPlan {
+    int grid, tiles, kblocks, nmma, stages, nbufs, xdepth, tmem_cols;
+    size_t smem, counters_off, partial_off, ws_bytes;
+};
+
+// Up to 4 tokens two CTAs fit on an SM (registers and shared memory), so the next
+// launch of a dependent chain can start streaming; larger batches take one.
+constexpr size_t kTcSmemLimit2 = 110 * 1024, kTcSmemLimit1 = 210 * 1024;
+constexpr int kTcMinTokens = 2;  // oomb_gemm_fp8 takes the tensor cores from this batch size
+
+bool tc_plan(const DeviceState* d, int t, int n, int k, bool x_bf16, TcPlan& pl) {
+    if (t < 1 || t > kTcMaxT || n % kTcTile != 0 || k % kTcTile != 0 || n <= 0 || k <= 0) return false;
+    const int ts = tc_ts(x_bf16), xb = x_bf16 ? 2 : 4;
+    pl.kblocks = k / kTcTile;
+    pl.tiles = (n / kTcTile) * pl.kblocks;
+    pl.grid = pl.tiles < d->sms ? pl.tiles : d->sms;
+    pl.nmma = (t * ts + 7) / 8 * 8;
+    pl.nbufs = kTcAccBufs;
+    while (pl.nbufs > 2 && pl.nbufs * pl.nmma > 256) pl.nbufs /= 2;
+    int cols = 32;
+    while (cols < pl.nbufs * pl.nmma) cols *= 2;
+    if (cols > 512) return false;
+    pl.tmem_cols = cols;
+    const size_t limit = t <= 4 ? kTcSmemLimit2 : kTcSmemLimit1;
+    pl.xdepth = kTcXDepth;
+    auto total = [&](int st) { return tc_smem(st, pl.nmma, t, ts, xb, pl.xdepth).total + 1024; };
+    // The splitters share the B ring round-robin by tile; a splitter's parity
+    // waits on a slot stay within one phase of the slot's barrier only when the
+    // ring has at least one slot per splitter.
+    pl.stages = kTcMaxStages;
+    while (pl.stages > kTcSplitters && total(pl.stages) > limit) pl.stages--;
+    if (total(pl.stages) > limit) pl.xdepth = 1;
+    pl.smem = total(pl.stages);
+    if (pl.smem > 227 * 1024) return false;
+    pl.counters_off = 0;
+    pl.partial_off = (static_cast<size_t>(n / kTcTile) * 4 * 4 + 255) & ~static_cast<size_t>(255);
+    pl.ws_bytes = pl.partial_off + static_cast<size_t>(pl.grid) * 2 * t * kTcTile * 4;
+    return true;
+}
+
+template <bool XB, int MAXT>
+int tc_launch_t(const TcPlan& pl, const CUtensorMap& map, const TcParams& tp, cudaStream_t s) {
+    return launch(tc_gemm_kernel<XB, MAXT>, dim3(pl.grid), dim3(kTcThreads), pl.smem, s, map, tp);
+}
+
+template <bool XB>
+int tc_launch(int t, const TcPlan& pl, const CUtensorMap& map, const TcParams& tp, cudaStream_t s) {
+    if (t <= 1) return tc_launch_t<XB, 1>(pl, map, tp, s);
+    if (t <= 2) return tc_launch_t<XB, 2>(pl, map, tp, s);
+    if (t <= 4) return tc_launch_t<XB, 4>(pl, map, tp, s);
+    if (t <= 8) return tc_launch_t<XB, 8>(pl, map, tp, s);
+    if (t <= 16) return tc_launch_t<XB, 16>(pl, map, tp, s);
+    if (t <= 32) return tc_launch_t<XB, 32>(pl, map, tp, s);
+    return tc_launch_t<XB, 64>(pl, map, tp, s);
+}
+
 }  // namespace
 }  // namespace oomb
 
 using namespace oomb;
 
 extern "C" {
+
+int oomb_silu_mul_rows(const float* gu, void* y, int y_dtype, int rows, int n, oomb_stream stream) {
+    if (!gu || !y) return OOMB_E_ARG;
+    if (y_dtype != OOMB_F32 && y_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (rows < 0 || n <= 0 || n % 4 != 0) return OOMB_E_SHAPE;
+    if (!aligned16(gu) || !aligned16(y)) return OOMB_E_ALIGN;
+    if (rows == 0) return OOMB_OK;
+    if (!device_state()) return OOMB_E_DEVICE;
+    const int64_t quads = static_cast<int64_t>(rows) * n / 4;
+    const dim3 grid(static_cast<unsigned>((quads + 255) / 256));
+    return y_dtype == OOMB_BF16 ? launch(silu_mul_rows_kernel<true>, grid, dim3(256), 0, stream, gu, y, rows, n)
+                                : launch(silu_mul_rows_kernel<false>, grid, dim3(256), 0, stream, gu, y, rows, n);
+}
+
+size_t oomb_gemm_fp8_workspace_bytes(int t, int n, int k, int x_dtype) {
+    const DeviceState* d = device_state();
+    TcPlan pl{};
+    if (!d || (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) || !tc_plan(d, t, n, k, x_dtype == OOMB_BF16, pl))
+        return 0;
+    return pl.ws_bytes;
+}
+
+int oomb_pack_fp8_tiles(const uint8_t* q, int n, int k, uint8_t* tiles, oomb_stream stream) {
+    if (!q || !tiles) return OOMB_E_ARG;
+    if (n <= 0 || k <= 0 || n % kTcTile || k % kTcTile) return OOMB_E_SHAPE;
+    if (!aligned16(q) || !aligned16(tiles)) return OOMB_E_ALIGN;
+    if (!device_state()) return OOMB_E_DEVICE;
+    pack_fp8_tiles_kernel<<<static_cast<unsigned>((n / kTcTile) * (k / kTcTile)), 256, 0, stream>>>(q, k, tiles);
+    return cudaGetLastError() == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_gemm_fp8_tc(const void* x, int x_dtype, const uint8_t* q, int q_format, const float* scale,
+                     int scale_layout, void* y, int y_dtype, int t, int n, int k, void* workspace,
+                     size_t workspace_bytes, oomb_stream stream) {
+    if (q_format != OOMB_Q_ROWS && q_format != OOMB_Q_TILES) return OOMB_E_ARG;
+    if (!x || !q || !scale || !y || !workspace) return OOMB_E_ARG;
+    if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) || (y_dtype != OOMB_F32 && y_dtype != OOMB_BF16) ||
+        (scale_layout != OOMB_SCALE_1X128 && scale_layout != OOMB_SCALE_128X128))
+        return OOMB_E_ARG;
+    if (!aligned16(x) || !aligned16(q) || !aligned16(scale) || !aligned16(y) || !aligned16(workspace))
+        return OOMB_E_ALIGN;
+    if (t == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    TcPlan pl{};
+    if (!tc_plan(d, t, n, k, x_dtype == OOMB_BF16, pl)) return OOMB_E_SHAPE;
+    if (workspace_bytes < pl.ws_bytes) return OOMB_E_WORKSPACE;
+    CUtensorMap map;
+    const bool packed = q_format == OOMB_Q_TILES;
+    if (!(packed ? encode_fp8_tiles(&map, q, pl.tiles * kTcTile, kTcTile) : encode_fp8_tiles(&map, q, n, k)))
+        return OOMB_E_LAUNCH;
+    TcParams tp{};
+    tp.x = x;
+    tp.T = t;
+    tp.K = k;
+    tp.nrows = n;
+    tp.scale = scale;
+    tp.layout = scale_layout;
+    tp.y = y;
+    tp.y_bf16 = y_dtype == OOMB_BF16;
+    tp.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) + pl.counters_off);
+    tp.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partial_off);
+    tp.tiles = pl.tiles;
+    tp.kblocks = pl.kblocks;
+    tp.q_tiles = packed;
+    tp.nmma = pl.nmma;
+    tp.stages = pl.stages;
+    tp.nbufs = pl.nbufs;
+    tp.xdepth = pl.xdepth;
+    tp.tmem_cols = pl.tmem_cols;
+    tp.err = d->err;
+    return x_dtype == OOMB_BF16 ? tc_launch<true>(t, pl, map, tp, stream) : tc_launch<false>(t, pl, map, tp, stream);
+}
+
 
 const char* oomb_version(void) { return "oomb 0.1 (sm_100a)"; }
 
@@ -242,8 +414,6 @@ int oomb_device_error(int* code, int clear) {
 int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* scale,
                   int scale_layout, void* y, int y_dtype, int t, int n, int k, void* workspace,
                   size_t workspace_bytes, oomb_stream stream) {
-    (void)workspace;
-    (void)workspace_bytes;
     if (!x || !q || !scale || !y) return OOMB_E_ARG;
     if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) || (y_dtype != OOMB_F32 && y_dtype != OOMB_BF16) ||
         (scale_layout != OOMB_SCALE_1X128 && scale_layout != OOMB_SCALE_128X128))
@@ -253,6 +423,14 @@ int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* sca
     if (t == 0) return OOMB_OK;
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
+    // Batches of two or more tokens go to the tensor cores when the caller gave a
+    // workspace and the shape allows (the CUDA-core stream is faster at one token).
+    if (t >= kTcMinTokens && workspace) {
+        TcPlan pl{};
+        if (tc_plan(d, t, n, k, x_dtype == OOMB_BF16, pl) && workspace_bytes >= pl.ws_bytes && aligned16(workspace))
+            return oomb_gemm_fp8_tc(x, x_dtype, q, OOMB_Q_ROWS, scale, scale_layout, y, y_dtype, t, n, k, workspace,
+                                    workspace_bytes, stream);
+    }
     // Token chunks are reduced per stage, which needs whole rows in a stage:
     // with K split over several stages (k > 4096) run 2-token launches.
     const bool k_split = (k + 511) / 512 > 8;

@@ -57,6 +57,31 @@ __global__ void combine_slots_kernel(const float* y, const int32_t* slot, const 
     if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
 }
 
+// SwiGLU on stacked rows (silu_mul_rows, ops.cu:302-309): y[r, i] =
+// silu(gu[r, i]) * gu[r, n + i], silu(v) = v / (1 + exp(-v)); gu fp32 [rows, 2n],
+// y fp32 or bf16 [rows, n].  Four columns per thread (n % 4 == 0).
+template <bool OUT_BF16>
+__global__ void silu_mul_rows_kernel(const float* gu, void* y, int rows, int n) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i >= static_cast<int64_t>(rows) * n) return;
+    const int r = static_cast<int>(i / n), c = static_cast<int>(i % n);
+    const float4 g = __ldcg(reinterpret_cast<const float4*>(gu + static_cast<int64_t>(r) * 2 * n + c));
+    const float4 u = __ldcg(reinterpret_cast<const float4*>(gu + static_cast<int64_t>(r) * 2 * n + n + c));
+    const float o0 = g.x / (1.0f + expf(-g.x)) * u.x, o1 = g.y / (1.0f + expf(-g.y)) * u.y;
+    const float o2 = g.z / (1.0f + expf(-g.z)) * u.z, o3 = g.w / (1.0f + expf(-g.w)) * u.w;
+    if (OUT_BF16) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o0, o1), hi = __floats2bfloat162_rn(o2, o3);
+        uint2 pk;
+        pk.x = *reinterpret_cast<unsigned*>(&lo);
+        pk.y = *reinterpret_cast<unsigned*>(&hi);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(y) + i) = pk;
+    } else {
+        *reinterpret_cast<float4*>(static_cast<float*>(y) + i) = make_float4(o0, o1, o2, o3);
+    }
+}
+
 // out = routed + sigmoid(gate_logit[t]) * shared (ops.cu:311-316).
 __global__ void moe_combine_kernel(const float* routed, const float* shared, const float* gate_logit,
                                    float* out, int T, int H) {

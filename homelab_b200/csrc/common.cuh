@@ -45,7 +45,7 @@ __device__ __forceinline__ void record_error(unsigned* err, unsigned code) {
 // launch of every kind: a host tool reads it to lay out where the chain spends
 // its time.
 enum : unsigned {
-    TL_ROUTE = 1, TL_GATE_UP = 2, TL_DOWN = 3, TL_COMBINE = 4, TL_GEMV = 5,
+    TL_ROUTE = 1, TL_GATE_UP = 2, TL_DOWN = 3, TL_COMBINE = 4, TL_GEMV = 5, TL_TC = 6,
     TL_ENTRY = 0, TL_WAITED = 1, TL_END = 2, TL_FIRST_COPY = 3, TL_FIRST_STAGE = 4, TL_LOGITS_DONE = 5,
     TL_LAST_CTA = 6, TL_X_STAGED = 7, TL_TOPK_DONE = 8, TL_FIRST_META = 9, TL_LAST_COPY = 10,
 };
@@ -126,6 +126,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
         " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// As bulk_g2s, with the default L2 policy (activations another kernel may read again).
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
 

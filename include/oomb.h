@@ -98,10 +98,42 @@ int oomb_device_error(int* code, int clear);
  * 223-350).  x and y are fp32 or bf16.  k % 16 == 0; q, scale, x and y
  * 16-byte aligned.  One launch streams the weights once for all t tokens
  * (CUDA cores; t <= 16 is the decode/verify range of linear.rs:131-134); for
- * k > 4096 tokens go in launches of 2.  Workspace: none (pass NULL, 0). */
+ * k > 4096 tokens go in launches of 2.  Workspace: optional.  With t >= 2 and a
+ * workspace of at least oomb_gemm_fp8_workspace_bytes(t, n, k, x_dtype) bytes
+ * (zeroed once), shapes the tensor-core path takes (n, k multiples of 128,
+ * t <= 64) run there instead (oomb_gemm_fp8_tc); otherwise pass NULL, 0. */
 int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* scale,
                   int scale_layout, void* y, int y_dtype, int t, int n, int k, void* workspace,
                   size_t workspace_bytes, oomb_stream stream);
+
+/* The same product on the tensor cores (tcgen05, kind::f8f6f4): the weights go
+ * from HBM to shared memory by TMA and straight into the MMA; each 128-column
+ * block of x is split exactly into e4m3 terms with power-of-two scales (two for
+ * bf16 x, four for fp32 x) that form the MMA's B operand, and the per-block
+ * weight and term scales are applied in fp32 as each 128-column block
+ * completes.  Needs n % 128 == 0, k % 128 == 0, 1 <= t <= 64, and a workspace of
+ * oomb_gemm_fp8_workspace_bytes(t, n, k, x_dtype) bytes (split-K partial sums
+ * and self-resetting counters) zeroed once before first use.  Returns
+ * OOMB_E_SHAPE for other shapes (use oomb_gemm_fp8).  Calls sharing a
+ * workspace must be ordered on one stream. */
+#define OOMB_Q_ROWS 0  /* q row-major [n, k] (Weight::Fp8) */
+#define OOMB_Q_TILES 1 /* q in the packed tile layout of oomb_pack_fp8_tiles */
+size_t oomb_gemm_fp8_workspace_bytes(int t, int n, int k, int x_dtype);
+int oomb_gemm_fp8_tc(const void* x, int x_dtype, const uint8_t* q, int q_format, const float* scale,
+                     int scale_layout, void* y, int y_dtype, int t, int n, int k, void* workspace,
+                     size_t workspace_bytes, oomb_stream stream);
+
+/* SwiGLU on stacked rows: y[r, i] = silu(gu[r, i]) * gu[r, n + i] with
+ * silu(v) = v / (1 + exp(-v)); gu fp32 [rows, 2n], y fp32 or bf16 [rows, n],
+ * n % 4 == 0.  The reference's silu_mul_rows (ops.cu:302-309), used between
+ * the fused gate/up projection and the down projection of a dense MLP. */
+int oomb_silu_mul_rows(const float* gu, void* y, int y_dtype, int rows, int n, oomb_stream stream);
+
+/* Load-time repack of a row-major e4m3 matrix q [n, k] (n, k multiples of 128)
+ * into 128 x 128-byte tiles, tile (rb, kb) contiguous at (rb * k/128 + kb) *
+ * 16 KiB: the tensor-core path then streams each tile as one contiguous 16 KiB
+ * read instead of 128 rows of 128 bytes.  tiles: n * k bytes. */
+int oomb_pack_fp8_tiles(const uint8_t* q, int n, int k, uint8_t* tiles, oomb_stream stream);
 
 /* logits[t, e] = x[t, :] . W[e, :] for a bf16 router W [e, hidden], in the
  * canonical order the oracle restates bit for bit (fp32 fma per lane over
