@@ -64,6 +64,11 @@ SIGNATURES = [
     ("oomb_gemm_fp8_tc", I, [P, I, P, I, P, I, P, I, I, I, I, P, Z, S]),
     ("oomb_pack_fp8_tiles", I, [P, I, I, P, S]),
     ("oomb_silu_mul_rows", I, [P, P, I, I, I, S]),
+    ("oomb_moe_experts_fp8", I, [P, P, P, P, I, P, I, P, P, C.POINTER(Fp8Record), I, S]),
+    ("oomb_ep_meta", I, [P, I, I, I, I, P, S]),
+    ("oomb_ep_group", I, [P, I, I, I, I, P, P, P, P, P, P, S]),
+    ("oomb_ep_scatter", I, [P, P, P, P, I, I, P, S]),
+    ("oomb_ep_combine", I, [P, P, P, I, I, I, I, I, P, I, S]),
     ("oomb_router_logits", I, [P, I, P, P, I, I, I, S]),
     ("oomb_router_topk", I, [P, P, P, I, I, I, S]),
     ("oomb_moe_gate_up_fp8", I, [P, P, P, I, P, I, P, C.POINTER(Fp8Record), I, I, S]),

@@ -14,6 +14,7 @@
 
 #include "../../include/oomb.h"
 #include "combine.cuh"
+#include "ep.cuh"
 #include "quant.cuh"
 #include "route.cuh"
 #include "stream.cuh"
@@ -694,6 +695,84 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K)
                : launch(combine_slots_kernel<false>, cgrid, dim3(256), 0, stream, static_cast<const float*>(y),
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K);
+}
+
+// ---- expert parallelism -------------------------------------------------------
+
+int oomb_ep_meta(const int32_t* ids, int t, int k, int experts_per_rank, int ranks, int32_t* meta,
+                 oomb_stream stream) {
+    if (!ids || !meta) return OOMB_E_ARG;
+    if (t < 0 || k <= 0 || k > 32 || experts_per_rank <= 0 || ranks <= 0) return OOMB_E_SHAPE;
+    if (t == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    const int64_t n = static_cast<int64_t>(ranks) * t * k;
+    const unsigned grid = static_cast<unsigned>(n / kEpThreads + 1 < 1024 ? n / kEpThreads + 1 : 1024);
+    return launch(ep_meta_kernel, dim3(grid), dim3(kEpThreads), 0, stream, ids, t, k, experts_per_rank, ranks, meta,
+                  d->err);
+}
+
+int oomb_ep_group(const int32_t* recv_meta, int ranks, int t, int k, int experts_per_rank, const uint64_t* recs_local,
+                  int32_t* n_active, int32_t* off, int32_t* assign_row, int32_t* assign_ret, uint64_t* recs_active,
+                  oomb_stream stream) {
+    if (!recv_meta || !recs_local || !n_active || !off || !assign_row || !assign_ret || !recs_active)
+        return OOMB_E_ARG;
+    if (ranks <= 0 || t <= 0 || k <= 0 || k > 32 || experts_per_rank <= 0 || experts_per_rank > 8192)
+        return OOMB_E_SHAPE;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    const size_t smem = 2 * static_cast<size_t>(experts_per_rank) * 4;
+    return launch(ep_group_kernel, dim3(1), dim3(kEpThreads), smem, stream, recv_meta, ranks, t, k, experts_per_rank,
+                  recs_local, n_active, off, assign_row, assign_ret, recs_active, d->err);
+}
+
+int oomb_moe_experts_fp8(const uint64_t* recs_active, const int32_t* off, const int32_t* assign_tok,
+                         const int32_t* n_active, int max_active, const void* x, int x_dtype, float* h, float* y,
+                         const oomb_fp8_record* geo, int max_per_expert, oomb_stream stream) {
+    if (!recs_active || !off || !assign_tok || !n_active || !x || !h || !y || !geo) return OOMB_E_ARG;
+    if (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (geo->layout != OOMB_SCALE_1X128 && geo->layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (max_active <= 0 || geo->hidden <= 0 || geo->inter <= 0 || geo->hidden % 16 || geo->inter % 16 ||
+        geo->hidden > 4096 || geo->inter > 4096)
+        return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(h) || !aligned16(y)) return OOMB_E_ALIGN;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    const int maxn = max_per_expert > 0 ? max_per_expert : 0;
+    int rc = launch_gate_up(d, recs_active, off, assign_tok, n_active, 0, max_active, x, x_dtype == OOMB_BF16, h, geo,
+                            maxn, false, stream);
+    if (rc) return rc;
+    return launch_down(d, recs_active, off, n_active, 0, max_active, h, y, geo, maxn, true, stream);
+}
+
+int oomb_ep_scatter(const float* y, const int32_t* n_active, const int32_t* off, const int32_t* assign_ret, int h,
+                    int max_rows, float* ret, oomb_stream stream) {
+    if (!y || !n_active || !off || !assign_ret || !ret) return OOMB_E_ARG;
+    if (h <= 0 || h % 4 || max_rows < 0) return OOMB_E_SHAPE;
+    if (!aligned16(y) || !aligned16(ret)) return OOMB_E_ALIGN;
+    if (max_rows == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    const int64_t n = static_cast<int64_t>(max_rows) * (h / 4);
+    const unsigned grid = static_cast<unsigned>(n / 256 + 1 < 4 * d->sms ? n / 256 + 1 : 4 * d->sms);
+    return launch(ep_scatter_kernel, dim3(grid), dim3(256), 0, stream, y, n_active, off, assign_ret, h, ret);
+}
+
+int oomb_ep_combine(const float* back, const int32_t* ids, const float* w, int t, int k, int h, int experts_per_rank,
+                    int ranks, void* out, int out_dtype, oomb_stream stream) {
+    if (!back || !ids || !w || !out) return OOMB_E_ARG;
+    if (out_dtype != OOMB_F32 && out_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (t < 0 || k <= 0 || h <= 0 || h % 4 || experts_per_rank <= 0 || ranks <= 0) return OOMB_E_SHAPE;
+    if (!aligned16(back) || !aligned16(out)) return OOMB_E_ALIGN;
+    if (t == 0) return OOMB_OK;
+    if (!device_state()) return OOMB_E_DEVICE;
+    const int64_t quads = static_cast<int64_t>(t) * h / 4;
+    const dim3 grid(static_cast<unsigned>((quads + 255) / 256));
+    return out_dtype == OOMB_BF16
+               ? launch(ep_combine_kernel<true>, grid, dim3(256), 0, stream, back, ids, w, t, k, h, experts_per_rank,
+                        ranks, out)
+               : launch(ep_combine_kernel<false>, grid, dim3(256), 0, stream, back, ids, w, t, k, h, experts_per_rank,
+                        ranks, out);
 }
 
 int oomb_quantize_fp8(const uint16_t* w, int n, int k, int scale_layout, uint8_t* q, float* scale,

@@ -1,0 +1,177 @@
+"""Expert parallelism: one MoE layer with its experts sharded over the ranks of a
+process group, one rank per GPU.
+
+No counterpart in the reference, which serves from a single device
+(projects/oom-inference/crates/oominf-cuda/src/lib.rs:1-5): this is the
+expert-parallel form of Moe::forward's routed half (crates/oominf-models-qwen/
+src/moe.rs:254-366).  Expert e lives on rank e // experts_per_rank; the router
+is replicated.  A decode step on every rank, for its own t tokens:
+
+  1. route: logits and softmax top-k (ids, weights) of the rank's tokens;
+  2. meta[g][t][s]: local id on rank g of slot s's expert, or -1;
+  3. all-to-all of meta and of the tokens' activations (every rank receives
+     every rank's t rows: fixed sizes, so no host round trip and the step can
+     be captured in a CUDA graph);
+  4. group the received assignments by local expert, in (source rank, token,
+     slot) order, and run gate/up+SiLU and down on them;
+  5. scatter each output row to its slot's place in the return buffer of its
+     source rank; reverse all-to-all;
+  6. combine each token's k slots in slot order.
+
+Steps 4 and 6 are the single-GPU kernels' arithmetic and an expert output does
+not depend on what else shares its launch, so each rank's output is
+bit-identical to the single-GPU decode of the same tokens.
+
+The device steps go through an `ops` object (EpGpuOps here: the C ABI of
+liboomb.so) and the exchanges through torch.distributed (NCCL on GPUs).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import BF16, F32, check
+
+
+class EpGpuOps:
+    """The device steps of an expert-parallel layer on liboomb.so."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.L = _lib.lib()
+
+    def _s(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def route(self, x, router_w, logits, ids, weights, t, e, k, hidden):
+        xd = BF16 if x.dtype == torch.bfloat16 else F32
+        check(self.L.oomb_router_logits(x.data_ptr(), xd, router_w.data_ptr(), logits.data_ptr(), t, e, hidden,
+                                        self._s()), "router_logits")
+        check(self.L.oomb_router_topk(logits.data_ptr(), ids.data_ptr(), weights.data_ptr(), t, e, k, self._s()),
+              "router_topk")
+
+    def meta(self, ids, t, k, epr, ranks, meta):
+        check(self.L.oomb_ep_meta(ids.data_ptr(), t, k, epr, ranks, meta.data_ptr(), self._s()), "ep_meta")
+
+    def group(self, recv_meta, ranks, t, k, epr, recs_local, n_active, off, assign_row, assign_ret, recs_active):
+        check(self.L.oomb_ep_group(recv_meta.data_ptr(), ranks, t, k, epr, recs_local.data_ptr(),
+                                   n_active.data_ptr(), off.data_ptr(), assign_row.data_ptr(), assign_ret.data_ptr(),
+                                   recs_active.data_ptr(), self._s()), "ep_group")
+
+    def experts(self, recs_active, off, assign_row, n_active, max_active, x, h, y, geo, max_per_expert):
+        xd = BF16 if x.dtype == torch.bfloat16 else F32
+        check(self.L.oomb_moe_experts_fp8(recs_active.data_ptr(), off.data_ptr(), assign_row.data_ptr(),
+                                          n_active.data_ptr(), max_active, x.data_ptr(), xd, h.data_ptr(),
+                                          y.data_ptr(), C.byref(geo), max_per_expert, self._s()), "moe_experts")
+
+    def scatter(self, y, n_active, off, assign_ret, hidden, max_rows, ret):
+        check(self.L.oomb_ep_scatter(y.data_ptr(), n_active.data_ptr(), off.data_ptr(), assign_ret.data_ptr(),
+                                     hidden, max_rows, ret.data_ptr(), self._s()), "ep_scatter")
+
+    def combine(self, back, ids, weights, t, k, hidden, epr, ranks, out):
+        od = BF16 if out.dtype == torch.bfloat16 else F32
+        check(self.L.oomb_ep_combine(back.data_ptr(), ids.data_ptr(), weights.data_ptr(), t, k, hidden, epr, ranks,
+                                     out.data_ptr(), od, self._s()), "ep_combine")
+
+
+class EpMoeLayer:
+    """A MoE layer whose experts are sharded over `group` (this rank holds experts
+    [rank * epr, (rank + 1) * epr)).  recs_local: int64 device addresses of the
+    local expert records; geo: their Fp8Record; router_w: bf16 [experts, hidden]
+    (replicated).  Buffers are sized for up to t_max tokens per rank."""
+
+    def __init__(self, ops, group, hidden, experts, top_k, inter, router_w, recs_local, geo, t_max,
+                 x_dtype=torch.bfloat16, ranks=None, rank=None):
+        self.ops, self.group = ops, group
+        # ranks / rank given explicitly: virtual ranks in one process (no group)
+        self.G = ranks if ranks is not None else dist.get_world_size(group)
+        self.rank = rank if rank is not None else dist.get_rank(group)
+        if experts % self.G:
+            raise ValueError("experts must divide evenly over the ranks")
+        self.H, self.E, self.K, self.I = hidden, experts, top_k, inter
+        self.epr = experts // self.G
+        self.router_w, self.recs_local, self.geo = router_w, recs_local, geo
+        self.t_max = t_max
+        dev = router_w.device
+        G, T, K, H = self.G, t_max, top_k, hidden
+        i32 = dict(dtype=torch.int32, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.logits = torch.empty((T, experts), **f32)
+        self.ids = torch.empty((T, K), **i32)
+        self.weights = torch.empty((T, K), **f32)
+        self.meta = torch.empty((G, T, K), **i32)
+        self.recv_meta = torch.empty((G, T, K), **i32)
+        self.send_x = torch.empty((G, T, H), dtype=x_dtype, device=dev)
+        self.recv_x = torch.empty((G, T, H), dtype=x_dtype, device=dev)
+        A = G * T * K
+        self.n_active = torch.zeros(1, **i32)
+        self.off = torch.zeros(self.epr + 1, **i32)
+        self.assign_row = torch.zeros(A, **i32)
+        self.assign_ret = torch.zeros(A, **i32)
+        self.recs_active = torch.zeros(self.epr, dtype=torch.int64, device=dev)
+        self.h = torch.empty((A, inter), **f32)
+        self.y = torch.empty((A, H), **f32)
+        self.ret = torch.zeros((G, T * K, H), **f32)
+        self.back = torch.empty((G, T * K, H), **f32)
+
+    # The step in three device phases separated by the two exchanges.  Each
+    # exchange is an all-to-all of equal chunks: rank g's chunk of `send` goes
+    # to rank g and lands in chunk (sender) of `recv`.
+
+    def phase_route(self, x, t: int):
+        """Route, meta, staged activations; returns the first exchange's
+        [(send_meta, recv_meta), (send_x, recv_x)] views."""
+        if t > self.t_max:
+            raise ValueError("more tokens than the layer's buffers hold")
+        G, K, H = self.G, self.K, self.H
+        self.ops.route(x, self.router_w, self.logits, self.ids, self.weights, t, self.E, K, H)
+        self.ops.meta(self.ids, t, K, self.epr, G, self.meta)
+        send_meta = self.meta.view(-1)[: G * t * K].view(G, t, K)
+        recv_meta = self.recv_meta.view(-1)[: G * t * K].view(G, t, K)
+        send_x = self.send_x.view(-1)[: G * t * H].view(G, t, H)
+        send_x.copy_(x[:t].unsqueeze(0).expand(G, t, H))
+        recv_x = self.recv_x.view(-1)[: G * t * H].view(G, t, H)
+        return [(send_meta, recv_meta), (send_x, recv_x)]
+
+    def phase_experts(self, t: int):
+        """Group the received assignments, run the local experts, stage the
+        outputs for their source ranks; returns the second exchange's (send, recv)."""
+        G, K, H = self.G, self.K, self.H
+        recv_meta = self.recv_meta.view(-1)[: G * t * K].view(G, t, K)
+        recv_x = self.recv_x.view(-1)[: G * t * H].view(G * t, H)
+        self.ops.group(recv_meta, G, t, K, self.epr, self.recs_local, self.n_active, self.off, self.assign_row,
+                       self.assign_ret, self.recs_active)
+        max_active = min(self.epr, G * t * K)
+        self.ops.experts(self.recs_active, self.off, self.assign_row, self.n_active, max_active, recv_x, self.h,
+                         self.y, self.geo, G * t)
+        ret = self.ret.view(-1)[: G * t * K * H].view(G, t * K, H)
+        self.ops.scatter(self.y, self.n_active, self.off, self.assign_ret, H, G * t * K, ret)
+        back = self.back.view(-1)[: G * t * K * H].view(G, t * K, H)
+        return ret, back
+
+    def phase_combine(self, t: int, out):
+        G, K, H = self.G, self.K, self.H
+        back = self.back.view(-1)[: G * t * K * H].view(G, t * K, H)
+        self.ops.combine(back, self.ids, self.weights, t, K, H, self.epr, G, out)
+        return self.ids[:t], self.weights[:t]
+
+    def forward(self, x, t: int, out):
+        """out[t, hidden] = the routed experts' combined output for this rank's t tokens;
+        returns (ids, weights) of the routing."""
+        for send, recv in self.phase_route(x, t):
+            dist.all_to_all_single(recv, send, group=self.group)
+        ret, back = self.phase_experts(t)
+        dist.all_to_all_single(back, ret, group=self.group)
+        return self.phase_combine(t, out)
+
+
+def exchange_local(sends, recvs):
+    """The all-to-all of equal chunks between ranks that live in one process
+    (virtual ranks on one device, tests): recvs[g][src] = sends[src][g]."""
+    G = len(sends)
+    for g in range(G):
+        for src in range(G):
+            recvs[g][src].copy_(sends[src][g])

@@ -223,6 +223,49 @@ int oomb_workspace_clear(void* workspace, size_t bytes, oomb_stream stream);
 int oomb_moe_decode_fp8_noalloc(const oomb_moe_layer* layer, const void* x, int x_dtype, int t, void* out,
                                 int out_dtype, int32_t* ids, float* weights, oomb_stream stream);
 
+/* ---- routed experts with device-side group counts ----------------------- */
+/* gate/up+SiLU then down over n_active[0] (on the device) expert groups:
+ * expert i owns assignments [off[i], off[i+1]), record recs_active[i], the
+ * assignment's activation row assign_tok[a] of x.  h: [A, inter] fp32
+ * scratch, y: [A, hidden] fp32.  max_active bounds n_active (launch size);
+ * max_per_expert bounds any group (0 if unknown).  The same kernels and
+ * arithmetic as oomb_moe_gate_up_fp8 / oomb_moe_down_fp8: an assignment's
+ * output does not depend on which other assignments share the launch. */
+int oomb_moe_experts_fp8(const uint64_t* recs_active, const int32_t* off, const int32_t* assign_tok,
+                         const int32_t* n_active, int max_active, const void* x, int x_dtype, float* h, float* y,
+                         const oomb_fp8_record* geo, int max_per_expert, oomb_stream stream);
+
+/* ---- expert parallelism (experts sharded over ranks) --------------------- */
+/* No counterpart in the reference, which runs on one device (its experts are
+ * tiered, not sharded).  Expert e lives on rank e / experts_per_rank.  A step:
+ * route on every rank; oomb_ep_meta; all-to-all of meta and of the tokens'
+ * activations (fixed sizes, no host round trip); oomb_ep_group;
+ * oomb_moe_experts_fp8; oomb_ep_scatter; reverse all-to-all; oomb_ep_combine.
+ * The expert outputs and the slot-order combine are the single-GPU path's
+ * arithmetic, so every rank's output is bit-identical to one GPU's.
+ *
+ * meta[g][t][s] (ranks x t x k int32): local id on rank g of ids[t][s]'s
+ * expert, or -1. */
+int oomb_ep_meta(const int32_t* ids, int t, int k, int experts_per_rank, int ranks, int32_t* meta,
+                 oomb_stream stream);
+/* Groups the received recv_meta[g][t][s] by local expert in (g, t, s) order
+ * (one CTA): n_active[0], off[n_active + 1], assign_row[A] = g * t + t_src
+ * (row of the received activations [ranks * t, hidden]), assign_ret[A] =
+ * g * t*k + t_src * k + s (row of the return buffer), recs_active[n_active] =
+ * recs_local[local expert].  A <= ranks * t * k. */
+int oomb_ep_group(const int32_t* recv_meta, int ranks, int t, int k, int experts_per_rank, const uint64_t* recs_local,
+                  int32_t* n_active, int32_t* off, int32_t* assign_row, int32_t* assign_ret, uint64_t* recs_active,
+                  oomb_stream stream);
+/* ret[assign_ret[a]] = y[a] for the A grouped assignments; ret: [ranks * t*k, h]
+ * fp32 (rows of absent slots are left as they are); max_rows bounds A. */
+int oomb_ep_scatter(const float* y, const int32_t* n_active, const int32_t* off, const int32_t* assign_ret, int h,
+                    int max_rows, float* ret, oomb_stream stream);
+/* out[t] = sum_s w[t, s] * back[ids[t, s] / experts_per_rank][t*k + s] in slot
+ * order with fused multiply-adds; back: [ranks][t*k][h] fp32 (the returned
+ * rows); out fp32 or bf16 [t, h]. */
+int oomb_ep_combine(const float* back, const int32_t* ids, const float* w, int t, int k, int h, int experts_per_rank,
+                    int ranks, void* out, int out_dtype, oomb_stream stream);
+
 /* ---- weight preparation ------------------------------------------------- */
 /* The load-time quantizer on the device, byte-identical to fp8::quantize_blocks
  * (crates/oominf-core/src/fp8.rs:52-88) for OOMB_SCALE_1X128 and to its 2-D

@@ -1,0 +1,100 @@
+"""Expert parallelism on one GPU with virtual ranks, against the single-GPU decode.
+
+The virtual ranks share the device; their all-to-alls are tensor copies
+(exchange_local).  Every rank's output must equal, bit for bit, the rows of the
+fused single-GPU decode (oomb_moe_decode_fp8) of the whole batch, and an
+expert's output for an assignment must not depend on which other assignments
+share its launch.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import oracle as O  # noqa: E402
+import homelab_b200 as hb  # noqa: E402
+from homelab_b200.backend import Gpu  # noqa: E402
+from homelab_b200.ep import EpGpuOps, EpMoeLayer, exchange_local  # noqa: E402
+from homelab_b200.records import ExpertBank  # noqa: E402
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a GPU", allow_module_level=True)
+
+DEV = torch.device("cuda", 0)
+H, E, K, I = 2048, 64, 8, 768
+
+
+@pytest.fixture(scope="module")
+def layer():
+    gpu = Gpu(0)
+    bank = ExpertBank(E, H, I, hb.SCALE_128X128, DEV)
+    bank.fill_random(gpu, seed=31)
+    router = torch.from_numpy(O.normal_bf16(32, E * H, 0.0, 0.02).view(np.int16)).to(DEV).view(torch.bfloat16)
+    router = router.view(E, H)
+    L = hb.MoeLayer(hidden=H, experts=E, top_k=K, router_w=router.data_ptr(), recs=bank.addrs.data_ptr())
+    L.geo = bank.geo
+    torch.cuda.synchronize()
+    yield dict(gpu=gpu, bank=bank, router=router, L=L)
+    torch.cuda.synchronize()
+    assert gpu.device_error() == 0
+
+
+def run_virtual(layer, x, G, t):
+    """The expert-parallel step over G virtual ranks, t tokens each."""
+    bank, router = layer["bank"], layer["router"]
+    ops = EpGpuOps(DEV)
+    epr = E // G
+    ranks = [EpMoeLayer(ops, None, H, E, K, I, router, bank.addrs[g * epr:(g + 1) * epr].contiguous(), bank.geo, t,
+                        ranks=G, rank=g) for g in range(G)]
+    outs = [torch.empty((t, H), dtype=torch.float32, device=DEV) for _ in range(G)]
+    ex = [r.phase_route(x[g * t:(g + 1) * t], t) for g, r in enumerate(ranks)]
+    for j in range(len(ex[0])):
+        exchange_local([e[j][0] for e in ex], [e[j][1] for e in ex])
+    rb = [r.phase_experts(t) for r in ranks]
+    exchange_local([b[0] for b in rb], [b[1] for b in rb])
+    routing = [r.phase_combine(t, outs[g]) for g, r in enumerate(ranks)]
+    return outs, routing
+
+
+@pytest.mark.parametrize("G,t", [(2, 1), (2, 3), (4, 2), (8, 1)])
+def test_expert_parallel_equals_single_gpu(layer, G, t):
+    gpu, L = layer["gpu"], layer["L"]
+    T = G * t
+    x = torch.from_numpy(O.normal_bf16(40 + G * 10 + t, T * H).view(np.int16)).to(DEV).view(torch.bfloat16).view(T, H)
+    ws = gpu.moe_decode_workspace(L, T)
+    want = torch.empty((T, H), dtype=torch.float32, device=DEV)
+    ids = torch.empty((T, K), dtype=torch.int32, device=DEV)
+    wts = torch.empty((T, K), dtype=torch.float32, device=DEV)
+    gpu.moe_decode(L, x, T, want, ws, ids, wts)
+    outs, routing = run_virtual(layer, x, G, t)
+    torch.cuda.synchronize()
+    for g in range(G):
+        assert torch.equal(routing[g][0], ids[g * t:(g + 1) * t])
+        assert torch.equal(routing[g][1], wts[g * t:(g + 1) * t])
+        assert torch.equal(outs[g], want[g * t:(g + 1) * t]), f"rank {g} differs from one GPU"
+
+
+def test_expert_outputs_do_not_depend_on_grouping(layer):
+    """The same (expert, token) assignment gives the same bits alone or in a larger launch."""
+    gpu, bank = layer["gpu"], layer["bank"]
+    t = 3
+    x = torch.from_numpy(O.normal_bf16(77, t * H).view(np.int16)).to(DEV).view(torch.bfloat16).view(t, H)
+
+    def run(experts, toks):
+        recs = bank.addrs[torch.tensor(experts, device=DEV)].contiguous()
+        off = torch.tensor(np.concatenate([[0], np.cumsum([len(tk) for tk in toks])]), dtype=torch.int32, device=DEV)
+        tok = torch.tensor([v for tk in toks for v in tk], dtype=torch.int32, device=DEV)
+        A = int(off[-1])
+        h = torch.empty((A, I), dtype=torch.float32, device=DEV)
+        y = torch.empty((A, H), dtype=torch.float32, device=DEV)
+        gpu.moe_gate_up(recs, off, tok, len(experts), x, h, bank.geo)
+        gpu.moe_down(recs, off, len(experts), h, y, bank.geo)
+        torch.cuda.synchronize()
+        return y
+
+    big = run([3, 9, 20, 41], [[0, 2], [1], [0, 1, 2], [2]])
+    alone = run([20], [[1]])
+    assert torch.equal(big[4], alone[0])  # expert 20, token 1
+    pair = run([9, 41], [[1], [2]])
+    assert torch.equal(big[2], pair[0]) and torch.equal(big[6], pair[1])
