@@ -228,14 +228,15 @@ def run_ours(args, rank, world, local_rank):
     gpu = Gpu(local_rank)
     B = args.batch
 
-    # ---- weights: 8 layer replicas ----
+    # ---- weights: 8 layer replicas; with N > 1 every rank holds E/N of each layer's experts ----
     LAYERS = args.layers
+    epr = E // world
     layers = []
     gen = torch.Generator(device=dev)
     for li in range(LAYERS):
-        bank = ExpertBank(E, H, I, hb.SCALE_128X128, dev)
+        bank = ExpertBank(epr, H, I, hb.SCALE_128X128, dev)
         bank.fill_random(gpu, seed=1000 * (rank + 1) + li)
-        gen.manual_seed(77 + li)
+        gen.manual_seed(77 + li)  # the router is replicated: the same on every rank
         router = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
         L = hb.MoeLayer(hidden=H, experts=E, top_k=K_TOP, router_w=router.data_ptr(), recs=bank.addrs.data_ptr())
         L.geo = bank.geo
@@ -244,11 +245,21 @@ def run_ours(args, rank, world, local_rank):
     gen.manual_seed(5 + rank)
     xs = (torch.randn((NX, B, H), generator=gen, device=dev)).to(torch.bfloat16)
     out = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
-    ws = gpu.moe_decode_workspace(layers[0][2], B)
-    torch.cuda.synchronize()
+    if world == 1:
+        ws = gpu.moe_decode_workspace(layers[0][2], B)
 
-    def step(i, x=None, o=None):
-        gpu.moe_decode(layers[i % LAYERS][2], xs[i % NX] if x is None else x, B, out if o is None else o, ws)
+        def step(i, x=None, o=None):
+            gpu.moe_decode(layers[i % LAYERS][2], xs[i % NX] if x is None else x, B, out if o is None else o, ws)
+    else:
+        # expert parallelism: route locally, all-to-all dispatch, local experts, all-to-all return, combine
+        from homelab_b200.ep import EpGpuOps, EpMoeLayer
+        ops = EpGpuOps(dev)
+        ep_layers = [EpMoeLayer(ops, dist.group.WORLD, H, E, K_TOP, I, router, bank.addrs, bank.geo, B)
+                     for (bank, router, _) in layers]
+
+        def step(i, x=None, o=None):
+            ep_layers[i % LAYERS].forward(xs[i % NX] if x is None else x, B, out if o is None else o)
+    torch.cuda.synchronize()
 
     if args.profile:
         for i in range(args.profile):
@@ -279,6 +290,40 @@ def run_ours(args, rank, world, local_rank):
                 else:
                     step(i)
         return g
+
+    class Eager:
+        """Replays n steps eagerly (used where the steps cannot be captured)."""
+
+        def __init__(self, n, e2e=False, xh=None, oh=None, xdev=None):
+            self.n, self.e2e, self.xh, self.oh, self.xdev = n, e2e, xh, oh, xdev
+
+        def replay(self):
+            with torch.cuda.stream(s):
+                for i in range(self.n):
+                    if self.e2e:
+                        self.xdev.copy_(self.xh[i % NX], non_blocking=True)
+                        step(i, self.xdev, out)
+                        self.oh[i % NX].copy_(out, non_blocking=True)
+                    else:
+                        step(i)
+
+    graphs_ok = True
+    if world > 1:
+        # NCCL collectives inside a CUDA graph: try once, fall back to eager steps
+        try:
+            torch.cuda.synchronize()
+            gt = capture(2)
+            gt.replay()
+            torch.cuda.synchronize()
+            del gt
+        except Exception:
+            graphs_ok = False
+        if dist:
+            flag = torch.tensor([1 if graphs_ok else 0], device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            graphs_ok = bool(flag.item())
+    if not graphs_ok:
+        capture = Eager  # noqa: F811
 
     def timed(graphs_and_counts, sampler_index):
         if dist:
@@ -338,7 +383,7 @@ def run_ours(args, rank, world, local_rank):
     del ge_main, ge_rem
 
     # ---- roofline of the dominant kernel: gate/up+SiLU over the 8 experts of a step ----
-    step_bytes = E * H * 2 + 8 * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
+    step_bytes = E * H * 2 + 8 * B * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
     roof = measure_gate_up(gpu, layers, dev, s, B, LAYERS)
     gemv1 = measure_gemv_config1(gpu, dev, s)
     del layers
@@ -353,7 +398,9 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(config_dict(B, LAYERS), parallelism=f"replicas{world}" if world > 1 else "single"),
+            "config": dict(config_dict(B, LAYERS), parallelism=f"ep{world}" if world > 1 else "single",
+                           **({"expert_parallel": f"{E // world} experts per GPU, NCCL all-to-all dispatch and combine",
+                               "step_capture": "cuda graph" if graphs_ok else "eager"} if world > 1 else {})),
             "roofline": {"bound": "hbm", "achieved": roof["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": roof["gbs"] / peak, "peak_kind": peak_kind,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None,
@@ -366,7 +413,9 @@ def run_ours(args, rank, world, local_rank):
             "batched_dense_config3": mlp3,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
-            "gpu_launches": 4 * K,
+            # per step: route, gate/up, down, combine; expert-parallel: router logits, top-k,
+            # meta, group, gate/up, down, scatter, combine (NCCL's own kernels not counted)
+            "gpu_launches": (4 if world == 1 else 8) * K,
             "clocks": clocks,
         }
     return result, roof
@@ -386,7 +435,8 @@ def measure_gate_up(gpu, layers, dev, s, B, LAYERS, launches=400):
     tables = []
     for li in range(LAYERS):
         bank = layers[li][0]
-        ids = np.sort(rng.choice(E, 8 * B if 8 * B <= E else E, replace=False)).astype(np.int32)
+        ne = bank.experts
+        ids = np.sort(rng.choice(ne, min(8 * B, ne), replace=False)).astype(np.int32)
         recs = bank.addrs[torch.from_numpy(ids).long().to(dev)].contiguous()
         off = torch.arange(0, len(ids) + 1, dtype=torch.int32, device=dev)
         tok = torch.zeros(len(ids), dtype=torch.int32, device=dev)
