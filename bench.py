@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="run N eager decode steps of the workload and exit (a small driver for ncu)")
+    ap.add_argument("--profile-mlp", type=int, default=0, metavar="B",
+                    help="with --profile: run N config-3 MLP steps at batch B instead (tensor-core path)")
     return ap.parse_args()
 
 
@@ -262,8 +264,11 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     if args.profile:
-        for i in range(args.profile):
-            step(i)
+        if args.profile_mlp:
+            profile_mlp(gpu, dev, args.profile_mlp, args.profile)
+        else:
+            for i in range(args.profile):
+                step(i)
         torch.cuda.synchronize()
         assert gpu.device_error() == 0
         return None, None
@@ -389,6 +394,7 @@ def run_ours(args, rank, world, local_rank):
     del layers
     torch.cuda.empty_cache()
     mlp3 = measure_mlp_config3(gpu, dev, s) if world == 1 else None
+    staging = measure_staging(dev) if world == 1 else None
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
 
@@ -411,6 +417,7 @@ def run_ours(args, rank, world, local_rank):
                              "achieved_gbs": gemv1["gbs"], "frac": gemv1["gbs"] / peak, "launch_us": gemv1["us"],
                              "algorithmic_bytes_per_launch": gemv1["bytes"]},
             "batched_dense_config3": mlp3,
+            "offload_staging_config5": staging,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
             # per step: route, gate/up, down, combine; expert-parallel: router logits, top-k,
@@ -470,6 +477,31 @@ def measure_gate_up(gpu, layers, dev, s, B, LAYERS, launches=400):
     nbytes = n_e * (2 * I * H + 2 * scale_bytes(I, H, geo.layout)) + n_e * H * 2 + n_e * I * 4
     us = best * 1e3
     return {"gbs": nbytes / (us * 1e-6) / 1e9, "bytes": nbytes, "us": us}
+
+
+def profile_mlp(gpu, dev, B, steps):
+    """`steps` eager config-3 MLP steps at batch B (one weight copy): an ncu driver."""
+    import torch
+
+    import homelab_b200 as hb
+    H, F = 4096, 14336
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    mats = []
+    for (n, k) in ((2 * F, H), (H, F)):
+        w = (torch.randn((n, k), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        mats.append(gpu.quantize_fp8(w.view(torch.int16), n, k, hb.SCALE_128X128))
+        del w
+    x = torch.randn((B, H), generator=gen, device=dev).to(torch.bfloat16)
+    gu = torch.empty((B, 2 * F), dtype=torch.float32, device=dev)
+    hh = torch.empty((B, F), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    ws1 = gpu.gemm_fp8_workspace(B, 2 * F, H) if B >= 2 else None
+    ws2 = gpu.gemm_fp8_workspace(B, H, F) if B >= 2 else None
+    for _ in range(steps):
+        gpu.gemm_fp8(x, mats[0][0], mats[0][1], gu, B, 2 * F, H, hb.SCALE_128X128, ws1)
+        gpu.silu_mul_rows(gu, hh, B, F)
+        gpu.gemm_fp8(hh, mats[1][0], mats[1][1], y, B, H, F, hb.SCALE_128X128, ws2)
 
 
 def measure_mlp_config3(gpu, dev, s, batches=(1, 4, 16, 64), steps=24):
@@ -532,6 +564,39 @@ def measure_mlp_config3(gpu, dev, s, batches=(1, 4, 16, 64), steps=24):
                         "path": "tcgen05" if B >= 2 else "cuda-core stream"}
         del g
     return out
+
+
+def measure_staging(dev, records=8, reps=5):
+    """BASELINE config 5 offload: cold expert records (hidden 4096, intermediate
+    2048, FP8 128x128: 25.2 MB each) staged from a pinned host arena into device
+    slots on a copy queue (homelab_b200.stage), one copy per record; device-timed
+    on the queue.  Returns the host-to-device GB/s (PCIe)."""
+    import torch
+
+    import homelab_b200 as hb
+    from homelab_b200.records import record_layout
+    from homelab_b200.stage import HostArena, Transfer, stage_records
+    geo, stride = record_layout(4096, 2048, hb.SCALE_128X128)
+    arena = HostArena(records, stride)
+    arena.buf.fill_(1)
+    slots = torch.empty(records * stride, dtype=torch.uint8, device=dev)
+    addrs = [slots.data_ptr() + j * stride for j in range(records)]
+    tr = Transfer(dev)
+    q = torch.cuda.ExternalStream(tr.queue, device=dev)
+    stage_records(tr, arena, range(records), addrs)
+    tr.copies_sync()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(q)
+        stage_records(tr, arena, range(records), addrs)
+        e1.record(q)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    tr.copies_sync()
+    tr.close()
+    return {"record_bytes": stride, "records": records, "h2d_gbs": records * stride / (best * 1e-3) / 1e9,
+            "ms_per_batch": best}
 
 
 def measure_gemv_config1(gpu, dev, s, copies=16, launches=320):

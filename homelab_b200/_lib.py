@@ -69,6 +69,20 @@ SIGNATURES = [
     ("oomb_ep_group", I, [P, I, I, I, I, P, P, P, P, P, P, S]),
     ("oomb_ep_scatter", I, [P, P, P, P, I, I, P, S]),
     ("oomb_ep_combine", I, [P, P, P, I, I, I, I, I, P, I, S]),
+    ("oomb_copy_queue_create", I, [C.POINTER(C.c_void_p)]),
+    ("oomb_copy_queue_destroy", I, [P]),
+    ("oomb_pin_host", I, [P, Z]),
+    ("oomb_unpin_host", I, [P]),
+    ("oomb_copy_to_device", I, [P, P, P, Z]),
+    ("oomb_copy_on_device", I, [P, P, P, Z]),
+    ("oomb_record_compute", I, [S, C.POINTER(C.c_void_p)]),
+    ("oomb_record_copies", I, [P, C.POINTER(C.c_void_p)]),
+    ("oomb_copies_wait", I, [P, P]),
+    ("oomb_compute_wait", I, [S, P]),
+    ("oomb_event_done", I, [P]),
+    ("oomb_event_wait", I, [P]),
+    ("oomb_event_destroy", I, [P]),
+    ("oomb_copies_sync", I, [P]),
     ("oomb_router_logits", I, [P, I, P, P, I, I, I, S]),
     ("oomb_router_topk", I, [P, P, P, I, I, I, S]),
     ("oomb_moe_gate_up_fp8", I, [P, P, P, I, P, I, P, C.POINTER(Fp8Record), I, I, S]),

@@ -775,6 +775,108 @@ int oomb_ep_combine(const float* back, const int32_t* ids, const float* w, int t
                         ranks, out);
 }
 
+// ---- offload staging (Transfer, crates/oominf-core/src/backend.rs:945-1018) --------
+
+int oomb_copy_queue_create(oomb_copy_queue* queue) {
+    if (!queue) return OOMB_E_ARG;
+    if (!device_state()) return OOMB_E_DEVICE;
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return OOMB_E_LAUNCH;
+    *queue = reinterpret_cast<oomb_copy_queue>(s);
+    return OOMB_OK;
+}
+
+int oomb_copy_queue_destroy(oomb_copy_queue queue) {
+    if (!queue) return OOMB_E_ARG;
+    return cudaStreamDestroy(reinterpret_cast<cudaStream_t>(queue)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_pin_host(void* ptr, size_t len) {
+    if (!ptr || len == 0) return OOMB_E_ARG;
+    if (!device_state()) return OOMB_E_DEVICE;
+    return cudaHostRegister(ptr, len, cudaHostRegisterPortable) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_unpin_host(void* ptr) {
+    if (!ptr) return OOMB_E_ARG;
+    return cudaHostUnregister(ptr) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_copy_to_device(oomb_copy_queue queue, void* dst, const void* src, size_t len) {
+    if (!queue || !dst || !src) return OOMB_E_ARG;
+    if (len == 0) return OOMB_OK;
+    return cudaMemcpyAsync(dst, src, len, cudaMemcpyHostToDevice, reinterpret_cast<cudaStream_t>(queue)) == cudaSuccess
+               ? OOMB_OK
+               : OOMB_E_LAUNCH;
+}
+
+int oomb_copy_on_device(oomb_copy_queue queue, void* dst, const void* src, size_t len) {
+    if (!queue || !dst || !src) return OOMB_E_ARG;
+    if (len == 0) return OOMB_OK;
+    return cudaMemcpyAsync(dst, src, len, cudaMemcpyDeviceToDevice, reinterpret_cast<cudaStream_t>(queue)) ==
+                   cudaSuccess
+               ? OOMB_OK
+               : OOMB_E_LAUNCH;
+}
+
+namespace {
+int record_on(cudaStream_t s, oomb_event* ev) {
+    if (!ev) return OOMB_E_ARG;
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return OOMB_E_LAUNCH;
+    if (cudaEventRecord(e, s) != cudaSuccess) {
+        cudaEventDestroy(e);
+        return OOMB_E_LAUNCH;
+    }
+    *ev = reinterpret_cast<oomb_event>(e);
+    return OOMB_OK;
+}
+}  // namespace
+
+int oomb_record_compute(oomb_stream compute, oomb_event* ev) { return record_on(compute, ev); }
+
+int oomb_record_copies(oomb_copy_queue queue, oomb_event* ev) {
+    if (!queue) return OOMB_E_ARG;
+    return record_on(reinterpret_cast<cudaStream_t>(queue), ev);
+}
+
+int oomb_copies_wait(oomb_copy_queue queue, oomb_event ev) {
+    if (!queue || !ev) return OOMB_E_ARG;
+    return cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(queue), reinterpret_cast<cudaEvent_t>(ev), 0) ==
+                   cudaSuccess
+               ? OOMB_OK
+               : OOMB_E_LAUNCH;
+}
+
+int oomb_compute_wait(oomb_stream compute, oomb_event ev) {
+    if (!ev) return OOMB_E_ARG;
+    return cudaStreamWaitEvent(compute, reinterpret_cast<cudaEvent_t>(ev), 0) == cudaSuccess ? OOMB_OK
+                                                                                             : OOMB_E_LAUNCH;
+}
+
+int oomb_event_done(oomb_event ev) {
+    if (!ev) return OOMB_E_ARG;
+    const cudaError_t r = cudaEventQuery(reinterpret_cast<cudaEvent_t>(ev));
+    if (r == cudaSuccess) return 1;
+    if (r == cudaErrorNotReady) return 0;
+    return OOMB_E_LAUNCH;
+}
+
+int oomb_event_wait(oomb_event ev) {
+    if (!ev) return OOMB_E_ARG;
+    return cudaEventSynchronize(reinterpret_cast<cudaEvent_t>(ev)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_event_destroy(oomb_event ev) {
+    if (!ev) return OOMB_E_ARG;
+    return cudaEventDestroy(reinterpret_cast<cudaEvent_t>(ev)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_copies_sync(oomb_copy_queue queue) {
+    if (!queue) return OOMB_E_ARG;
+    return cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(queue)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
 int oomb_quantize_fp8(const uint16_t* w, int n, int k, int scale_layout, uint8_t* q, float* scale,
                       oomb_stream stream) {
     if (!w || !q || !scale) return OOMB_E_ARG;

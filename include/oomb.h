@@ -266,6 +266,31 @@ int oomb_ep_scatter(const float* y, const int32_t* n_active, const int32_t* off,
 int oomb_ep_combine(const float* back, const int32_t* ids, const float* w, int t, int k, int h, int experts_per_rank,
                     int ranks, void* out, int out_dtype, oomb_stream stream);
 
+/* ---- offload staging ---------------------------------------------------- */
+/* Copies that run beside compute, from pinned host memory or within the
+ * device, ordered against compute with events: the Transfer trait
+ * (crates/oominf-core/src/backend.rs:945-1018; CUDA body
+ * crates/oominf-cuda/src/memory.rs:300-398) as used by TieredExperts to bring
+ * cold expert records into device slots (crates/oominf-tiers/src/tiered.rs).
+ * A copy queue is a non-blocking stream; events carry no timing.  Each record
+ * is one cudaMemcpyAsync. */
+typedef struct oomb_copy_queue_st* oomb_copy_queue;
+typedef struct oomb_event_st* oomb_event;
+int oomb_copy_queue_create(oomb_copy_queue* queue);   /* Transfer::copy_queue */
+int oomb_copy_queue_destroy(oomb_copy_queue queue);
+int oomb_pin_host(void* ptr, size_t len);            /* Transfer::pin_host (portable registration) */
+int oomb_unpin_host(void* ptr);                      /* Transfer::unpin_host */
+int oomb_copy_to_device(oomb_copy_queue queue, void* dst, const void* src, size_t len); /* copy_to_device */
+int oomb_copy_on_device(oomb_copy_queue queue, void* dst, const void* src, size_t len); /* copy_on_device */
+int oomb_record_compute(oomb_stream compute, oomb_event* ev); /* completes with the compute issued so far */
+int oomb_record_copies(oomb_copy_queue queue, oomb_event* ev); /* completes with the copies queued so far */
+int oomb_copies_wait(oomb_copy_queue queue, oomb_event ev);   /* later copies wait for ev */
+int oomb_compute_wait(oomb_stream compute, oomb_event ev);    /* later compute waits for ev */
+int oomb_event_done(oomb_event ev);                           /* 1 done, 0 pending, < 0 error */
+int oomb_event_wait(oomb_event ev);                           /* blocks the host */
+int oomb_event_destroy(oomb_event ev);
+int oomb_copies_sync(oomb_copy_queue queue);                  /* blocks the host */
+
 /* ---- weight preparation ------------------------------------------------- */
 /* The load-time quantizer on the device, byte-identical to fp8::quantize_blocks
  * (crates/oominf-core/src/fp8.rs:52-88) for OOMB_SCALE_1X128 and to its 2-D
