@@ -27,9 +27,10 @@
 //     multiply; fp32 activations take the fp32 path (decode to fp32, packed
 //     fma.rn.f32x2).
 //   Partial sums stay in registers over a pass of P units; then each warp
-//   reduces every one of them by the same xor tree, the slabs are added in slab
-//   order through shared memory, and the pass's outputs are written: each
-//   output's arithmetic is fixed whatever else shares its launch.
+//   reduces them (a multi-value butterfly, the same lane tree for every value),
+//   the slabs are added in slab order through shared memory, and the pass's
+//   outputs are written: each output's arithmetic is fixed whatever else shares
+//   its launch.
 // Kernels signal dependents at entry; the dense GEMV and the EARLY expert
 // variant stream weights and load their unit tables before griddepcontrol.wait.
 #pragma once
@@ -261,12 +262,11 @@ __device__ __forceinline__ int slot_row(int rpi, int rp, int j) {
 template <int PARTS, int TB, int P, bool MOE>
 __device__ __forceinline__ void reduce_write(const StreamParams& p, const float (&acc)[P][kRows][TB], float* rb,
                                              const int* hdr, int pn, int warp, int lane) {
-    // Every partial is summed over the 32 lanes by the same xor tree, so an
-    // output's arithmetic does not depend on its position in the pass (which
-    // unit, row slot or token slot it occupies): results are identical however
-    // the assignments are grouped into launches.
-    constexpr int NV = kRows * P * TB;
-    float v[NV];
+    // The multi-value butterfly sums every partial over the 32 lanes by the same
+    // tree (pairs at lane distance 16, then 8, 4, 2, 1; addition commutes), so
+    // an output's arithmetic does not depend on its position in the pass: results
+    // are identical however the assignments are grouped into launches.
+    float v[kRedV];
 #pragma unroll
     for (int a = 0; a < P; a++)
 #pragma unroll
@@ -274,12 +274,9 @@ __device__ __forceinline__ void reduce_write(const StreamParams& p, const float 
 #pragma unroll
             for (int b = 0; b < TB; b++) v[(a * kRows + j) * TB + b] = acc[a][j][b];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < NV; i++) v[i] = __fadd_rn(v[i], __shfl_xor_sync(0xffffffffu, v[i], o));
-#pragma unroll
-    for (int i = 0; i < NV; i++)
-        if (lane == i) rb[warp * kRedV + i] = v[i];
+    for (int j = kRows * P * TB; j < kRedV; j++) v[j] = 0.0f;
+    warp_reduce_multi<kRedV>(v, lane);
+    if ((lane & 1) == 0) rb[warp * kRedV + reduce_index<kRedV>(lane, 0)] = v[0];
     asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
     // outputs of the pass: unit pi, output row r (of RPP), token b
     const int outs = pn * p.rpp * TB;
