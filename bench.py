@@ -387,8 +387,11 @@ def run_ours(args, rank, world, local_rank):
     e2e = world * B * K / (ms_e2e / 1e3)
     del ge_main, ge_rem
 
-    # ---- roofline of the dominant kernel: gate/up+SiLU over the 8 experts of a step ----
+    # ---- roofline: at N = 1 and B <= 16 the step is one launch (decode_kernel), so its
+    # algorithmic bytes over the device-timed step are that kernel's achieved bandwidth;
+    # the stand-alone gate/up kernel is timed beside it ----
     step_bytes = E * H * 2 + 8 * B * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
+    fused = world == 1 and B <= 16 and os.environ.get("OOMB_DECODE_CHAIN") != "1"
     roof = measure_gate_up(gpu, layers, dev, s, B, LAYERS)
     gemv1 = measure_gemv_config1(gpu, dev, s)
     del layers
@@ -407,11 +410,11 @@ def run_ours(args, rank, world, local_rank):
             "config": dict(config_dict(B, LAYERS), parallelism=f"ep{world}" if world > 1 else "single",
                            **({"expert_parallel": f"{E // world} experts per GPU, NCCL all-to-all dispatch and combine",
                                "step_capture": "cuda graph" if graphs_ok else "eager"} if world > 1 else {})),
-            "roofline": {"bound": "hbm", "achieved": roof["gbs"], "peak": peak, "unit": "GB/s",
-                         "frac": roof["gbs"] / peak, "peak_kind": peak_kind,
-                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                         "kernel": "stream_kernel<2> (gate/up+SiLU over the 8 experts of a step)",
-                         "algorithmic_bytes_per_launch": roof["bytes"], "launch_us": roof["us"]},
+            "roofline": roofline_line(fused, step_bytes, ms / K, roof, peak, peak_kind, traffic),
+            "gate_up_kernel": {"kernel": "stream_kernel<2> (gate/up+SiLU over the 8 experts of a step, "
+                                         "back-to-back stand-alone launches)",
+                               "achieved_gbs": roof["gbs"], "frac": roof["gbs"] / peak, "launch_us": roof["us"],
+                               "algorithmic_bytes_per_launch": roof["bytes"]},
             "step_hbm_gbs": step_bytes * K / (ms / 1e3) / 1e9 / 1.0 if world == 1 else None,
             "gemv_config1": {"workload": "config1: 4096x4096 e4m3, 128x128 scales, x bf16 batch 1, bf16 out",
                              "achieved_gbs": gemv1["gbs"], "frac": gemv1["gbs"] / peak, "launch_us": gemv1["us"],
@@ -420,12 +423,32 @@ def run_ours(args, rank, world, local_rank):
             "offload_staging_config5": staging,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
-            # per step: route, gate/up, down, combine; expert-parallel: router logits, top-k,
-            # meta, group, gate/up, down, scatter, combine (NCCL's own kernels not counted)
-            "gpu_launches": (4 if world == 1 else 8) * K,
+            # per step: one decode_kernel (the chain route, gate/up, down, combine when
+            # OOMB_DECODE_CHAIN=1 or B > 16); expert-parallel: router logits, top-k, meta,
+            # group, gate/up, down, scatter, combine (NCCL's own kernels not counted)
+            "gpu_launches": (1 if fused else (4 if world == 1 else 8)) * K,
             "clocks": clocks,
         }
     return result, roof
+
+
+def roofline_line(fused, step_bytes, ms_per_step, gate_up, peak, peak_kind, traffic):
+    """The roofline object of the step's dominant kernel: the one-launch decode
+    kernel when the step is one launch, else the gate/up kernel."""
+    if fused:
+        kernel = "decode_kernel"
+        us = ms_per_step * 1e3
+        gbs = step_bytes / (us * 1e-6) / 1e9
+        desc = "decode_kernel (the whole step in one launch: router, top-k, grouping, gate/up, down, combine)"
+        nbytes = step_bytes
+    else:
+        kernel = "stream_kernel<2"
+        us, gbs, nbytes = gate_up["us"], gate_up["gbs"], gate_up["bytes"]
+        desc = "stream_kernel<2> (gate/up+SiLU over the 8 experts of a step)"
+    t = traffic.get("bytes_per_launch") if traffic and str(traffic.get("kernel", "")).startswith(kernel) else None
+    return {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+            "peak_kind": peak_kind, "traffic": t, "kernel": desc, "algorithmic_bytes_per_launch": nbytes,
+            "launch_us": us}
 
 
 def measure_gate_up(gpu, layers, dev, s, B, LAYERS, launches=400):

@@ -14,6 +14,7 @@
 
 #include "../../include/oomb.h"
 #include "combine.cuh"
+#include "decode.cuh"
 #include "ep.cuh"
 #include "quant.cuh"
 #include "route.cuh"
@@ -302,6 +303,132 @@ int tc_launch(int t, const TcPlan& pl, const CUtensorMap& map, const TcParams& t
     return tc_launch_t<XB, 64>(pl, map, tp, s);
 }
 
+
+// The one-launch decode (decode.cuh) for up to kDecodeMaxT tokens and routers of
+// at most kRouteSmallE experts: its plan, or false when the layer or batch is
+// outside what it covers (the chain of kernels serves those).
+struct FusedDecode {
+    DecodeParams prm;
+    size_t smem;
+    int grid, tb, p;
+};
+
+std::mutex g_occ_mu;
+std::unordered_map<const void*, int> g_occ[kMaxDevices];
+
+// CTAs of `kernel` one SM holds at once with `smem` bytes of dynamic shared memory.
+template <typename Kernel>
+int resident_ctas(Kernel kernel, size_t smem) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    const void* key = reinterpret_cast<const void*>(kernel);
+    {
+        std::lock_guard<std::mutex> lk(g_occ_mu);
+        auto it = g_occ[dev].find(key);
+        if (it != g_occ[dev].end() && (it->second >> 20) == static_cast<int>(smem >> 10)) return it->second & 0xff;
+    }
+    if (!set_smem(kernel, smem)) return 0;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    g_occ[dev][key] = (static_cast<int>(smem >> 10) << 20) | (n & 0xff);
+    return n;
+}
+
+template <bool XB, bool BLK, int TB, int P>
+auto decode_kernel_ptr() {
+    return decode_kernel<XB, BLK, TB, P>;
+}
+
+template <bool XB, bool BLK>
+int fused_resident(int tb, size_t smem) {
+    return tb == 1 ? resident_ctas(decode_kernel_ptr<XB, BLK, 1, pass_len<1>()>(), smem)
+                   : resident_ctas(decode_kernel_ptr<XB, BLK, 2, 1>(), smem);
+}
+
+bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, bool xbf16, FusedDecode& f) {
+    const char* env = getenv("OOMB_DECODE_CHAIN");
+    if (env && env[0] == '1') return false;
+    const int E = L->experts, K = L->top_k, H = static_cast<int>(L->geo.hidden), I = static_cast<int>(L->geo.inter);
+    const int layout = L->geo.layout;
+    if (t < 1 || t > kDecodeMaxT || E > kRouteSmallE || H > kRouteMaxH) return false;
+    const TbP tp = tb_p(t);
+    f.tb = tp.chunked ? 2 : tp.tb;
+    f.p = f.tb == 1 ? pass_len<1>() : 1;
+    const StreamPlan pg = stream_plan(H, 2, f.p, layout), pd = stream_plan(I, 1, f.p, layout);
+    if (pg.stage_bytes > kStageBytes || pd.stage_bytes > kStageBytes) return false;
+    const int gpe_g = (I + pg.rpp - 1) / pg.rpp, gpe_d = (H + pd.rpp - 1) / pd.rpp;
+    if (gpe_d > kDecodeMaxGroups) return false;
+    const int slot = pg.slot_bytes > pd.slot_bytes ? pg.slot_bytes : pd.slot_bytes;
+    const int ms_g = f.p * 4 + f.p * 2 * pg.sr * pg.nb, ms_d = f.p * 4 + f.p * pd.sr * pd.nb;
+    const int meta_stride = ms_g > ms_d ? ms_g : ms_d;
+    const DecodeTabs dt = decode_tabs(t, K, E);
+    // [ring][bars][red][meta][chunk][tables]
+    const size_t bars = (2 * kMaxStages + 2 * kMetaBufs) * sizeof(uint64_t);
+    const size_t red = 2 * kWarps * kRedV * sizeof(float);
+    const size_t meta = static_cast<size_t>(kMetaBufs) * meta_stride * 4;
+    const size_t fixed = bars + red + ((meta + 15) & ~static_cast<size_t>(15)) + 8 * sizeof(int) + dt.total;
+    int stages = kMaxStages;
+    while (stages > 2 && static_cast<size_t>(stages) * slot + fixed > static_cast<size_t>(kSmemLimit)) stages--;
+    const size_t ring = static_cast<size_t>(stages) * slot;
+    if (ring + fixed > static_cast<size_t>(kSmemLimit)) return false;
+    f.smem = ring + fixed;
+    // every CTA must be resident at once (grid barriers)
+    const int occ = xbf16 ? (layout ? fused_resident<true, true>(f.tb, f.smem) : fused_resident<true, false>(f.tb, f.smem))
+                          : (layout ? fused_resident<false, true>(f.tb, f.smem) : fused_resident<false, false>(f.tb, f.smem));
+    if (occ < 1) return false;
+    f.grid = d->sms * (occ < OOMB_STREAM_CTAS_PER_SM ? occ : OOMB_STREAM_CTAS_PER_SM);
+    const int rows_per_cta = (E + f.grid - 1) / f.grid;
+    if (rows_per_cta > kWarps || ring < decode_ring_borrow(t, H, E, K, rows_per_cta, 0)) return false;
+    // the activations are staged in the ring after the router rows when they fit
+    const size_t x_bytes = static_cast<size_t>(t) * H * (xbf16 ? 2 : 4);
+    const bool x_staged = ring >= decode_ring_borrow(t, H, E, K, rows_per_cta, x_bytes);
+
+    DecodeParams& q = f.prm;
+    q = DecodeParams{};
+    q.stages = stages;
+    q.slot_bytes = slot;
+    q.meta_stride = meta_stride;
+    q.off_bars = static_cast<int>(ring);
+    q.off_red = static_cast<int>(ring + bars);
+    q.off_meta = static_cast<int>(ring + bars + red);
+    q.off_chunk = static_cast<int>(q.off_meta + ((meta + 15) & ~static_cast<size_t>(15)));
+    q.off_tabs = q.off_chunk + 8 * static_cast<int>(sizeof(int));
+    q.x_off = x_staged ? rows_per_cta * H * 2 : -1;
+    auto fill = [&](StreamParams& sp, const StreamPlan& pl, int k, int nrows, int gpe) {
+        sp.layout = layout;
+        sp.k = k;
+        sp.nrows = nrows;
+        sp.kc = pl.kc;
+        sp.ks = pl.ks;
+        sp.nsl = pl.nsl;
+        sp.rp = pl.rp;
+        sp.rpp = pl.rpp;
+        sp.nb = pl.nb;
+        sp.sr = pl.sr;
+        sp.stages = stages;
+        sp.slot_bytes = slot;
+        sp.gpe = gpe;
+        sp.err = d->err;
+    };
+    fill(q.gu, pg, H, I, gpe_g);
+    q.gu.w_off[0] = L->geo.gate_weight;
+    q.gu.w_off[1] = L->geo.up_weight;
+    q.gu.s_off[0] = L->geo.gate_scale;
+    q.gu.s_off[1] = L->geo.up_scale;
+    fill(q.dn, pd, I, H, gpe_d);
+    q.dn.w_off[0] = q.dn.w_off[1] = L->geo.down_weight;
+    q.dn.s_off[0] = q.dn.s_off[1] = L->geo.down_scale;
+    return true;
+}
+
+template <bool XB, bool BLK>
+int fused_launch(const FusedDecode& f, cudaStream_t s) {
+    if (f.tb == 1)
+        return launch(decode_kernel<XB, BLK, 1, pass_len<1>()>, dim3(f.grid), dim3(kThreads), f.smem, s, f.prm);
+    return launch(decode_kernel<XB, BLK, 2, 1>, dim3(f.grid), dim3(kThreads), f.smem, s, f.prm);
+}
+
 }  // namespace
 }  // namespace oomb
 
@@ -573,7 +700,7 @@ int oomb_moe_combine(const float* routed, const float* shared, const float* gate
 
 namespace {
 struct DecodeLayout {
-    size_t ticket, logits, ids, weights, n_active, active, off, assign_tok, slot_assign, recs_active,
+    size_t ticket, sync, logits, ids, weights, n_active, active, off, assign_tok, slot_assign, recs_active,
         h, y, total;
 };
 
@@ -585,6 +712,7 @@ DecodeLayout decode_layout(int t, const oomb_moe_layer* L) {
     const size_t H = L->geo.hidden, I = L->geo.inter;
     size_t o = 0;
     d.ticket = o; o += 256;
+    d.sync = o; o = up256(o + kSyncWords * 4);
     d.logits = o; o = up256(o + T * E * 4);
     d.ids = o; o = up256(o + A * 4);
     d.weights = o; o = up256(o + A * 4);
@@ -644,6 +772,34 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const int E = L->experts, K = L->top_k, H = L->hidden;
     const int A = t * K;
+
+    FusedDecode f;
+    if (fused_decode_plan(d, L, t, x_dtype == OOMB_BF16, f)) {
+        // the whole step in one persistent launch
+        DecodeParams& q = f.prm;
+        q.r.x = x;
+        q.r.x_bf16 = x_dtype == OOMB_BF16;
+        q.r.w = L->router_w;
+        q.r.logits = reinterpret_cast<float*>(ws + lay.logits);
+        q.r.T = t;
+        q.r.H = H;
+        q.r.E = E;
+        q.r.K = K;
+        q.r.recs_all = L->recs;
+        q.r.err = d->err;
+        q.gu.x = x;
+        q.gu.y = ws + lay.h;
+        q.dn.x = ws + lay.h;
+        q.dn.y = ws + lay.y;
+        q.sync = reinterpret_cast<unsigned*>(ws + lay.sync);
+        q.ids_out = ids ? ids : reinterpret_cast<int32_t*>(ws + lay.ids);
+        q.w_out = weights ? weights : reinterpret_cast<float*>(ws + lay.weights);
+        q.out = out;
+        q.out_bf16 = out_dtype == OOMB_BF16;
+        if (x_dtype == OOMB_BF16)
+            return L->geo.layout ? fused_launch<true, true>(f, stream) : fused_launch<true, false>(f, stream);
+        return L->geo.layout ? fused_launch<false, true>(f, stream) : fused_launch<false, false>(f, stream);
+    }
 
     // 1. router logits + top-k + grouping (one launch; the last CTA groups)
     RouteParams rp{};

@@ -1,0 +1,434 @@
+// decode.cuh - one routed-MoE decode step (router GEMV, softmax top-k, grouping,
+// gate/up+SiLU, down, slot-order combine) in one persistent launch.
+//
+// The routed half of Moe::forward (crates/oominf-models-qwen/src/moe.rs:254-366
+// with begin_routed / finish_routed, moe.rs:532-582, 638-659) for a layer whose
+// experts are all resident, with the arithmetic of the separate kernels
+// (route.cuh, stream.cuh, combine.cuh): every output is bit-identical to the
+// chain route_kernel -> gate/up -> down -> combine_slots.
+//
+// Every CTA of the grid (one or two per SM, all resident at once) runs:
+//   1. before the dependency wait: its router rows land in shared memory by
+//      bulk copy, and the layer's record table is fetched;
+//   2. CTA c computes the logits of router rows c, c + grid, ... for every
+//      token (activations staged by one bulk copy after the wait, when they
+//      fit), writes them to global memory; a grid barrier, then every CTA
+//      loads all T x E logits into shared memory;
+//   3. softmax top-k and grouping of all tokens from the logits, the same in
+//      every CTA (deterministic), into shared-memory routing tables: no
+//      second hand-off through global memory;
+//   4. the streaming engine over the CTA's slice of gate/up units, then of down
+//      units, through one weight ring: the copy producer runs straight on from
+//      gate/up into down, so the down weights stream in while gate/up finishes
+//      and the consumers wait at the second grid barrier (down reads every h row
+//      of its expert);
+//   5. per down row group a counter; the CTA whose unit completes a group (the
+//      last of the n_e experts) combines that group's rows of every token in
+//      slot order and writes the output.
+// The two grid barriers count arrivals in a slot of a ring indexed by a launch
+// epoch, so a CTA that starts late (launches overlap under programmatic
+// dependent launch) cannot disturb a count it does not own: every CTA reads
+// the epoch word after the dependency wait and uses epoch + 1; CTA 0 zeroes the
+// slot two launches ahead (last used by a launch that has completed, next used
+// by one that cannot start before this one completes) and stores the epoch
+// back once every CTA has arrived at the second barrier (so all have read it).
+// An arrival is a release add, a wait one thread per CTA polling the count with
+// acquire loads: a single hot word, polled by one thread of each CTA.  All
+// waits are bounded.  The row-group counters are reset by the CTA that
+// completes the group.  The host launches only a grid that fits on the GPU at
+// once.
+#pragma once
+
+#include "route.cuh"
+#include "stream.cuh"
+
+namespace oomb {
+
+constexpr int kDecodeMaxT = 16;         // tokens per launch
+constexpr int kDecodeMaxGroups = 512;   // down row groups (combine counters, bitmap bits)
+// sync-area words: the launch epoch; a ring of 4 slots of the two barriers'
+// arrival counts (slot epoch % 4, counts 32 words apart); the row-group counters
+constexpr int kSyncEpoch = 0, kSyncBars = 32, kSyncGroups = kSyncBars + 4 * 2 * 32;
+constexpr int kSyncWords = kSyncGroups + kDecodeMaxGroups;
+
+enum : unsigned {
+    ERR_GRID_WAIT = 0x600,    // a grid barrier ran out (CTAs not resident together)
+    ERR_ROUTER_WAIT = 0x610,  // the router rows never landed in shared memory
+};
+
+struct DecodeParams {
+    RouteParams r;        // x, x_bf16, w, logits (scratch), T, H, E, K, recs_all, err
+    StreamParams gu, dn;  // planned phases: gu.x = x, gu.y = h; dn.x = h, dn.y = y
+    unsigned* sync;       // kSyncWords words, zero before first use
+    int32_t* ids_out;     // [T, K]
+    float* w_out;         // [T, K]
+    void* out;            // [T, H]
+    int out_bf16;
+    int stages, slot_bytes, meta_stride;
+    int off_bars, off_red, off_meta, off_chunk, off_tabs;  // shared-memory layout (bytes)
+    int x_off;  // ring offset (bytes) of the staged activations, or -1 to read them from global memory
+};
+
+// Routing tables in shared memory (byte offsets from the table area).
+struct DecodeTabs {
+    int recs, recs_active, rbar, xbar, lg, ids, w, counts, base, active, off, assign_tok, slot_assign, n_active, cbits,
+        total;
+};
+
+__host__ __device__ inline DecodeTabs decode_tabs(int T, int K, int E) {
+    DecodeTabs d{};
+    const int A = T * K;
+    int o = 0;
+    d.recs = o; o += E * 8;
+    d.recs_active = o; o += E * 8;
+    d.rbar = o; o += 8;
+    d.xbar = o; o += 8;
+    d.lg = o; o += T * E * 4;
+    d.ids = o; o += A * 4;
+    d.w = o; o += A * 4;
+    d.counts = o; o += E * 4;
+    d.base = o; o += E * 4;
+    d.active = o; o += E * 4;
+    d.off = o; o += (E + 1) * 4;
+    d.assign_tok = o; o += A * 4;
+    d.slot_assign = o; o += A * 4;
+    d.n_active = o; o += 4;
+    d.cbits = o; o += (kDecodeMaxGroups / 32) * 4;
+    d.total = (o + 15) & ~15;
+    return d;
+}
+
+// Bytes of the ring that the routing phase borrows: the CTA's router rows (and
+// the staged activations after them), later the softmax probabilities and
+// picks.
+__host__ __device__ inline size_t decode_ring_borrow(int T, int H, int E, int K, int rows_per_cta, size_t x_bytes) {
+    const size_t rows = static_cast<size_t>(rows_per_cta) * H * 2 + x_bytes;
+    const size_t ranks = (static_cast<size_t>(T) * E + 2 * static_cast<size_t>(T) * K) * 4;
+    return rows > ranks ? rows : ranks;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_u32(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// One thread per CTA, after a CTA barrier that follows the writes to publish:
+// a release add to the arrival count at ctr.
+__device__ __forceinline__ void bar_arrive(unsigned* ctr) {
+    fence_acq_rel_gpu();
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
+// One thread per CTA: polls the arrival count at ctr (acquire) until it reaches
+// n.  False when the wait ran out (the error code is recorded).
+__device__ __forceinline__ bool bar_wait(const unsigned* ctr, unsigned n, unsigned* err, unsigned code) {
+    if (ld_acquire_u32(ctr) >= n) return true;
+    const unsigned long long t0 = global_ns();
+    while (ld_acquire_u32(ctr) < n) {
+        if (global_ns() - t0 > kWaitLimitNs) {
+            record_error(err, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory"); }
+
+// Logits of router row e (bf16, in shared memory) for tokens [t0, t0 + nt):
+// the canonical order of router_row_dot (per lane one fmaf chain over columns
+// 256*i + 8*lane + j, i ascending, then the xor tree).  Activations from
+// global memory, or staged in shared memory (XSM, rows of p.H).  The logits go
+// to p.logits.
+template <bool XBF16, bool XSM>
+__device__ __forceinline__ void logits_row(const RouteParams& p, const uint8_t* wrow, const uint8_t* xsm, int e, int t0,
+                                           int nt, int lane) {
+    float acc[kRouteTT];
+#pragma unroll
+    for (int j = 0; j < kRouteTT; j++) acc[j] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRouteMaxH / 256; i++) {
+        const int base = i * 256 + lane * 8;
+        if (base < p.H) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(wrow + static_cast<size_t>(base) * 2);
+            const unsigned ww[4] = {wv.x, wv.y, wv.z, wv.w};
+            float wf[8];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                wf[2 * q] = __uint_as_float(ww[q] << 16);
+                wf[2 * q + 1] = __uint_as_float(ww[q] & 0xffff0000u);
+            }
+#pragma unroll
+            for (int j = 0; j < kRouteTT; j++) {
+                if (j < nt) {
+                    float xv[8];
+                    const int64_t xi = static_cast<int64_t>(t0 + j) * p.H + base;
+                    if (XBF16) {
+                        const uint4* xp = XSM ? reinterpret_cast<const uint4*>(xsm + xi * 2)
+                                              : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi);
+                        const uint4 a = XSM ? *xp : __ldcg(xp);
+                        const unsigned aa[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            xv[2 * q] = __uint_as_float(aa[q] << 16);
+                            xv[2 * q + 1] = __uint_as_float(aa[q] & 0xffff0000u);
+                        }
+                    } else {
+                        const float4* xp = XSM ? reinterpret_cast<const float4*>(xsm + xi * 4)
+                                               : reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi);
+                        const float4 a = XSM ? xp[0] : __ldcg(xp), b = XSM ? xp[1] : __ldcg(xp + 1);
+                        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+                        xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+                    }
+#pragma unroll
+                    for (int q = 0; q < 8; q++) acc[j] = __fmaf_rn(xv[q], wf[q], acc[j]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kRouteTT; j++) {
+        if (j < nt) {
+            const float v = xor_tree32(acc[j]);
+            if (lane == 0) p.logits[static_cast<int64_t>(t0 + j) * p.E + e] = v;
+        }
+    }
+}
+
+// XBF16: activations bf16 (else fp32).  BLK: 128x128 block scales.  TB, P: the
+// token slots and units per pass of both streaming phases (as the stand-alone
+// kernels would take them for at most T assignments per expert).
+template <bool XBF16, bool BLK, int TB, int P>
+__global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kernel(const DecodeParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_fail;
+    __shared__ unsigned s_epoch;
+    Ring rg;
+    rg.stages = p.stages;
+    rg.slot_bytes = p.slot_bytes;
+    rg.stage_buf = smem;
+    rg.full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+    rg.empty = rg.full + kMaxStages;
+    rg.mfull = rg.empty + kMaxStages;
+    rg.mempty = rg.mfull + kMetaBufs;
+    rg.red = reinterpret_cast<float*>(smem + p.off_red);
+    rg.meta = reinterpret_cast<int*>(smem + p.off_meta);
+    rg.meta_stride = p.meta_stride;
+    rg.chunk_hdr = reinterpret_cast<int*>(smem + p.off_chunk);
+
+    const int T = p.r.T, H = p.r.H, E = p.r.E, K = p.r.K, A = T * K;
+    const DecodeTabs dt = decode_tabs(T, K, E);
+    uint8_t* tabs = smem + p.off_tabs;
+    uint64_t* recs_sm = reinterpret_cast<uint64_t*>(tabs + dt.recs);
+    uint64_t* recs_active = reinterpret_cast<uint64_t*>(tabs + dt.recs_active);
+    uint64_t* rbar = reinterpret_cast<uint64_t*>(tabs + dt.rbar);
+    int32_t* ids_sm = reinterpret_cast<int32_t*>(tabs + dt.ids);
+    float* w_sm = reinterpret_cast<float*>(tabs + dt.w);
+    int32_t* off_sm = reinterpret_cast<int32_t*>(tabs + dt.off);
+    int32_t* assign_tok = reinterpret_cast<int32_t*>(tabs + dt.assign_tok);
+    int32_t* slot_sm = reinterpret_cast<int32_t*>(tabs + dt.slot_assign);
+    int32_t* n_active = reinterpret_cast<int32_t*>(tabs + dt.n_active);
+    unsigned* cbits = reinterpret_cast<unsigned*>(tabs + dt.cbits);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(tabs + dt.xbar);
+    float* lg = reinterpret_cast<float*>(tabs + dt.lg);
+    // This CTA's router rows blockIdx.x + i * grid, i < nrow; row i lands at i * H * 2.
+    int nrow = 0;
+    while (nrow < kWarps && static_cast<int>(blockIdx.x + gridDim.x * nrow) < E) nrow++;
+    const unsigned x_bytes = static_cast<unsigned>(T * H * (XBF16 ? 2 : 4));
+    const bool xsm = p.x_off >= 0;
+
+    // ---- 1. before the dependency wait: only weights and the record table ----
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        ring_init(rg);
+        mbar_init(rbar, 1);
+        mbar_init(xbar, 1);
+        fence_barrier_init();
+        tl_mark(TL_ROUTE, TL_ENTRY);
+        if (nrow > 0) {
+            mbar_arrive_expect_tx(rbar, static_cast<unsigned>(nrow * H * 2));
+            for (int i = 0; i < nrow; i++)
+                bulk_g2s_plain(smem + static_cast<size_t>(i) * H * 2,
+                               p.r.w + static_cast<int64_t>(blockIdx.x + gridDim.x * i) * H,
+                               static_cast<unsigned>(H * 2), rbar);
+        }
+    }
+    const unsigned long long rec_pre =
+        static_cast<int>(threadIdx.x) < E
+            ? ld_prefetch_u64(reinterpret_cast<const unsigned long long*>(p.r.recs_all) + threadIdx.x)
+            : 0ull;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) {
+        tl_mark(TL_ROUTE, TL_WAITED);
+        // every launch on this workspace before this one has completed
+        s_epoch = ld_relaxed_u32(p.sync + kSyncEpoch) + 1u;
+        if (blockIdx.x == 0) {
+            unsigned* ahead = p.sync + kSyncBars + ((s_epoch + 2u) & 3u) * 64;
+            ahead[0] = 0u;
+            ahead[32] = 0u;
+        }
+        if (xsm && nrow > 0) {
+            // the activations may come from the previous kernel: staged after the wait
+            mbar_arrive_expect_tx(xbar, x_bytes);
+            bulk_g2s_plain(smem + p.x_off, p.r.x, x_bytes, xbar);
+        }
+    }
+    if (static_cast<int>(threadIdx.x) < E) recs_sm[threadIdx.x] = rec_pre;
+    if (threadIdx.x < kDecodeMaxGroups / 32) cbits[threadIdx.x] = 0u;
+    __syncthreads();
+    const unsigned epoch = s_epoch;
+
+    // ---- 2. router logits of this CTA's rows, grid barrier, all logits into shared memory ----
+    if (warp < nrow) {
+        const bool ok = mbar_wait(rbar, 0, p.r.err, ERR_ROUTER_WAIT) &&
+                        (!xsm || mbar_wait(xbar, 0, p.r.err, ERR_ROUTER_WAIT));
+        if (ok) {
+            const int e = static_cast<int>(blockIdx.x + gridDim.x * warp);
+            const uint8_t* wrow = smem + static_cast<size_t>(warp) * H * 2;
+            for (int t0 = 0; t0 < T; t0 += kRouteTT) {
+                if (xsm) logits_row<XBF16, true>(p.r, wrow, smem + p.x_off, e, t0, min(kRouteTT, T - t0), lane);
+                else logits_row<XBF16, false>(p.r, wrow, nullptr, e, t0, min(kRouteTT, T - t0), lane);
+            }
+        } else {
+            s_fail = 1;
+        }
+    }
+    __syncthreads();
+    // the CTAs with router rows publish their logits; every CTA waits for all of them
+    unsigned* bars = p.sync + kSyncBars + (epoch & 3u) * 64;
+    if (threadIdx.x == 0) {
+        tl_mark(TL_ROUTE, TL_LOGITS_DONE);
+        if (nrow > 0 && !s_fail) bar_arrive(bars);
+        const unsigned writers = static_cast<unsigned>(min(E, static_cast<int>(gridDim.x)));
+        if (!s_fail && !bar_wait(bars, writers, p.r.err, ERR_GRID_WAIT)) s_fail = 1;
+        tl_mark(TL_ROUTE, TL_LAST_CTA);
+    }
+    __syncthreads();
+    if (s_fail) return;
+    for (int o = threadIdx.x; o < T * E; o += kThreads) lg[o] = __ldcg(p.r.logits + o);
+    __syncthreads();
+
+    // ---- 3. top-k and grouping of every token, in every CTA ----
+    {
+        topk_warps<kThreads, true>(p.r, lg, 0, T, ids_sm, w_sm);
+        __syncthreads();
+        if (blockIdx.x == 0) {
+            for (int o = threadIdx.x; o < A; o += kThreads) {
+                p.ids_out[o] = ids_sm[o];
+                p.w_out[o] = w_sm[o];
+            }
+        }
+        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_TOPK_DONE);
+        const GroupOut go{n_active, reinterpret_cast<int32_t*>(tabs + dt.active), off_sm, assign_tok, slot_sm,
+                          recs_active};
+        if (A <= 32) {
+            if (warp == 0) group_warp(p.r, go, ids_sm, recs_sm);
+        } else {
+            group_assignments<kThreads>(p.r, go, ids_sm, reinterpret_cast<int32_t*>(tabs + dt.counts),
+                                        reinterpret_cast<int32_t*>(tabs + dt.base), recs_sm);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_END);
+
+    // ---- 4. gate/up then down through one ring ----
+    const int n_e = *n_active;
+    const Tables tgu{recs_active, off_sm, assign_tok, n_e};
+    const Tables tdn{recs_active, off_sm, nullptr, n_e};
+    int gu0, gu1, dn0, dn1;
+    cta_units(n_e, p.gu.gpe, gu0, gu1);
+    cta_units(n_e, p.dn.gpe, dn0, dn1);
+
+    if (warp == kWarps) {
+        if (lane != 0) return;
+        int s = 0;
+        if (stream_copy<2, P, true, true>(p.gu, tgu, rg, gu0, gu1, s))
+            stream_copy<1, P, true, true>(p.dn, tdn, rg, dn0, dn1, s);
+        return;
+    }
+    if (warp == kWarps + 1) {
+        int q = 0;
+        if (stream_meta<2, P, true, true>(p.gu, tgu, rg, gu0, gu1, q))
+            stream_meta<1, P, true, true>(p.dn, tdn, rg, dn0, dn1, q);
+        return;
+    }
+
+    RingPos pos{0, 0, 0};
+    if (!stream_consume<2, TB, P, XBF16, true, BLK, true>(p.gu, tgu, rg, gu0, gu1, pos)) s_fail = 1;
+    consumers_sync();  // the CTA's h rows are written
+    if (threadIdx.x == 0 && !s_fail) {
+        bar_arrive(bars + 32);
+        if (!bar_wait(bars + 32, gridDim.x, p.r.err, ERR_GRID_WAIT)) s_fail = 1;
+    }
+    consumers_sync();
+    if (s_fail) return;
+    if (threadIdx.x == 0) {
+        // every CTA has read the epoch: hand it to the next launch
+        if (blockIdx.x == 0) st_relaxed_u32(p.sync + kSyncEpoch, epoch);
+        tl_mark(TL_DOWN, TL_WAITED);
+    }
+    if (!stream_consume<1, TB, P, false, true, BLK, true>(p.dn, tdn, rg, dn0, dn1, pos)) s_fail = 1;
+    consumers_sync();  // the CTA's y rows are written
+    if (s_fail) return;
+
+    // ---- 5. slot-order combine of the row groups this CTA completes ----
+    for (int i = threadIdx.x; i < dn1 - dn0; i += kWarps * 32) {
+        const int g = (dn0 + i) % p.dn.gpe;
+        fence_acq_rel_gpu();  // release the CTA's y rows before counting the unit
+        const unsigned old = atomicAdd(p.sync + kSyncGroups + g, 1u);
+        if (old == static_cast<unsigned>(n_e - 1)) {
+            p.sync[kSyncGroups + g] = 0u;  // every expert's unit of the group has arrived
+            atomicOr(&cbits[g >> 5], 1u << (g & 31));
+        }
+    }
+    consumers_sync();
+    fence_acq_rel_gpu();  // acquire: the other CTAs' y rows of the completed groups
+    const float* y = static_cast<const float*>(p.dn.y);
+    const int rpp = p.dn.rpp;
+    for (int wd = 0; wd < (p.dn.gpe + 31) / 32; wd++) {
+        unsigned bits = cbits[wd];
+        while (bits) {
+            const int g = wd * 32 + __ffs(bits) - 1;
+            bits &= bits - 1;
+            const int row0 = g * rpp, nr = min(rpp, H - row0);
+            for (int o = threadIdx.x; o < nr * T; o += kWarps * 32) {
+                const int t = o / nr, row = row0 + (o - t * nr);
+                float acc = 0.0f;
+                for (int s0 = 0; s0 < K; s0 += 8) {
+                    float v[8], ws[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const bool ok = s0 + j < K;
+                        ws[j] = ok ? w_sm[t * K + s0 + j] : 0.0f;
+                        v[j] = ok ? __ldcg(y + static_cast<int64_t>(slot_sm[t * K + s0 + j]) * H + row) : 0.0f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (s0 + j < K) acc = fmaf(ws[j], v[j], acc);
+                }
+                const int64_t oi = static_cast<int64_t>(t) * H + row;
+                if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(acc);
+                else static_cast<float*>(p.out)[oi] = acc;
+            }
+        }
+    }
+    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
+}
+
+}  // namespace oomb

@@ -302,28 +302,31 @@ __device__ __forceinline__ void topk_token(const RouteParams& p, int t, int lane
 // 1. Each warp computes the softmax of whole tokens in the canonical order
 //    of topk_token (lane l owns experts l, l+32, ...) into prob[token][E]
 //    (shared memory; NaN stored as -3, below every probability).
-// 2. Every thread takes (token, candidate) pairs and counts the experts that
-//    beat the candidate: e beats i when p_e > p_i, or p_e == p_i and e < i.
-//    The candidate beaten by exactly r others is the r-th pick of k argmax
-//    rounds with ties to the lower id (ops.cu:234-294).
+// 2. Every warp takes candidates of each token and counts, over its lanes, the
+//    experts that beat the candidate: e beats i when p_e > p_i, or p_e == p_i
+//    and e < i.  The candidate beaten by exactly r others is the r-th pick of k
+//    argmax rounds with ties to the lower id (ops.cu:234-294).
 // 3. weights = p / (sum of the picked p in pick order).
-// Writes p.ids, p.weights and, if non-null, ids_sm.  prob: (t1 - t0) * E
-// floats; pick_id / pick_p: (t1 - t0) * K entries.
-__device__ void topk_block(const RouteParams& p, int t0, int t1, float* prob, int32_t* pick_id, float* pick_p,
-                           int32_t* ids_sm) {
+// Writes ids_out / w_out ([T, K], indexed by global token) and, if non-null,
+// ids_sm.  prob: (t1 - t0) * E floats; pick_id / pick_p: (t1 - t0) * K entries.
+// NT: the CTA's threads (all of them call this).  logits: [T, E] in global
+// memory, or in this CTA's shared memory (LSM).
+template <int NT, bool LSM = false>
+__device__ void topk_block(const RouteParams& p, const float* logits, int t0, int t1, float* prob, int32_t* pick_id,
+                           float* pick_p, int32_t* ids_out, float* w_out, int32_t* ids_sm) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int nwarps = kRouteThreads / 32;
+    constexpr int nwarps = NT / 32;
     constexpr int NJ = kRouteSmallE / 32;
     const int nt = t1 - t0, E = p.E;
     const float NEG_INF = -__int_as_float(0x7f800000);
     for (int tl = warp; tl < nt; tl += nwarps) {
-        const float* l = p.logits + static_cast<int64_t>(t0 + tl) * E;
+        const float* l = logits + static_cast<int64_t>(t0 + tl) * E;
         float pe[NJ];
         float mx = NEG_INF;
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
             const int e = lane + 32 * j;
-            pe[j] = e < E ? __ldcg(l + e) : NEG_INF;
+            pe[j] = e < E ? (LSM ? l[e] : __ldcg(l + e)) : NEG_INF;
             mx = fmaxf(mx, pe[j]);
         }
 #pragma unroll
@@ -347,35 +350,152 @@ __device__ void topk_block(const RouteParams& p, int t0, int t1, float* prob, in
         }
     }
     __syncthreads();
-    for (int pr = threadIdx.x; pr < nt * E; pr += kRouteThreads) {
-        const int tl = pr / E, i = pr - tl * E;
+    // Ranks: lane l holds the token's probabilities of experts l + 32 j (absent
+    // experts -5, below every stored value); warp w takes candidates w, w + nwarps,
+    // ... and counts the experts that beat each over the warp.
+    for (int tl = 0; tl < nt; tl++) {
         const float* pt = prob + tl * E;
-        const float pi = pt[i];
-        int beats = 0;
-        for (int e = 0; e < i; e++) beats += pt[e] >= pi ? 1 : 0;
-        for (int e = i + 1; e < E; e++) beats += pt[e] > pi ? 1 : 0;
-        if (beats < p.K) {
-            pick_id[tl * p.K + beats] = i;
-            pick_p[tl * p.K + beats] = pi;
+        float pv[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            pv[j] = e < E ? pt[e] : -5.0f;
+        }
+        // four candidates at a time, so their load-compare-reduce chains overlap
+        for (int i0 = warp; i0 < E; i0 += 4 * nwarps) {
+            float pi[4];
+            unsigned b[4];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int i = i0 + c * nwarps;
+                pi[c] = pt[i < E ? i : 0];
+                b[c] = 0;
+            }
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int i = i0 + c * nwarps;
+#pragma unroll
+                for (int j = 0; j < NJ; j++) b[c] += (pv[j] > pi[c] || (pv[j] == pi[c] && lane + 32 * j < i)) ? 1u : 0u;
+            }
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int i = i0 + c * nwarps;
+                const unsigned beats = __reduce_add_sync(0xffffffffu, b[c]);
+                if (lane == 0 && i < E && beats < static_cast<unsigned>(p.K)) {
+                    pick_id[tl * p.K + beats] = i;
+                    pick_p[tl * p.K + beats] = pi[c];
+                }
+            }
         }
     }
     __syncthreads();
-    for (int o = threadIdx.x; o < nt * p.K; o += kRouteThreads) {
+    for (int o = threadIdx.x; o < nt * p.K; o += NT) {
         const int tl = o / p.K, r = o - tl * p.K;
         float psum = 0.0f;
         for (int q = 0; q < p.K; q++) psum = __fadd_rn(psum, pick_p[tl * p.K + q]);
         const int64_t gi = static_cast<int64_t>(t0 + tl) * p.K + r;
-        p.ids[gi] = pick_id[o];
-        p.weights[gi] = __fdiv_rn(pick_p[o], psum);
+        ids_out[gi] = pick_id[o];
+        w_out[gi] = __fdiv_rn(pick_p[o], psum);
         if (ids_sm) ids_sm[(t0 + tl) * p.K + r] = pick_id[o];
     }
 }
 
+// Softmax top-k of tokens [t0, t1) with one warp per token (E <= kRouteSmallE):
+// the same picks and weights as topk_block.  Each warp computes the token's
+// canonical softmax (NaN stored as -3), then k argmax rounds over (p desc,
+// id asc): exactly the first k of the order topk_block ranks by.  A round is
+// two warp reductions (max of an order key, then min of the ids holding it).  The
+// weights are p / (sum of the picks in pick order).  logits: [T, E] in global
+// memory, or in this CTA's shared memory (LSM).  For a few tokens per warp this
+// is far shorter than the block-wide ranking.
+template <int NT, bool LSM>
+__device__ void topk_warps(const RouteParams& p, const float* logits, int t0, int t1, int32_t* ids_out, float* w_out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int nwarps = NT / 32;
+    constexpr int NJ = kRouteSmallE / 32;
+    const int E = p.E, K = p.K;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    for (int t = t0 + warp; t < t1; t += nwarps) {
+        const float* l = logits + static_cast<int64_t>(t) * E;
+        float pe[NJ];
+        float mx = NEG_INF;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            pe[j] = e < E ? (LSM ? l[e] : __ldcg(l + e)) : NEG_INF;
+            mx = fmaxf(mx, pe[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            if (lane + 32 * j < E) {
+                pe[j] = oomb_expf(__fsub_rn(pe[j], mx));
+                s = __fadd_rn(s, pe[j]);
+            }
+        }
+        const float sum = xor_tree32(s);
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            if (lane + 32 * j < E) {
+                const float v = __fdiv_rn(pe[j], sum);
+                pe[j] = v == v ? v : -3.0f;
+            } else {
+                pe[j] = -5.0f;
+            }
+        }
+        // Order keys: a probability's bits + 2 (non-negative floats order as
+        // their bits), 1 for NaN (-3), 0 for an absent or picked expert.
+        unsigned key[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; j++) key[j] = pe[j] >= 0.0f ? (__float_as_uint(pe[j]) & 0x7fffffffu) + 2u : (pe[j] == -3.0f ? 1u : 0u);
+        int my_id = 0;
+        float my_p = 0.0f, psum = 0.0f;
+        for (int r = 0; r < K; r++) {
+            unsigned bk = 0u, bi = 0xffffffffu;
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if (key[j] > bk) {  // ascending ids within the lane: ties keep the lower
+                    bk = key[j];
+                    bi = static_cast<unsigned>(lane + 32 * j);
+                }
+            const unsigned mk = __reduce_max_sync(0xffffffffu, bk);
+            const unsigned mi = __reduce_min_sync(0xffffffffu, bk == mk ? bi : 0xffffffffu);
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if (static_cast<unsigned>(lane + 32 * j) == mi) key[j] = 0u;
+            const float bv = mk >= 2u ? __uint_as_float(mk - 2u) : -3.0f;
+            if (lane == r) {
+                my_id = static_cast<int>(mi);
+                my_p = bv;
+            }
+            psum = __fadd_rn(psum, bv);
+        }
+        if (lane < K) {
+            ids_out[static_cast<int64_t>(t) * K + lane] = my_id;
+            w_out[static_cast<int64_t>(t) * K + lane] = __fdiv_rn(my_p, psum);
+        }
+    }
+}
+
+// Where grouping writes its tables: the caller's global buffers (route_kernel)
+// or shared memory (decode_kernel).
+struct GroupOut {
+    int32_t* n_active;
+    int32_t* active;
+    int32_t* off;
+    int32_t* assign_tok;
+    int32_t* slot_assign;
+    uint64_t* recs_active;
+};
+
 // Groups the T*K assignments by expert (counting sort, stable in slot order).
-// Runs on one CTA; ids in shared memory.  counts, base: E ints of shared
-// scratch; recs_sm: the layer's record addresses staged in shared memory, or
-// null to read them from p.recs_all.
-__device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, int32_t* counts,
+// Runs on one CTA of NT threads; ids in shared memory.  counts, base: E ints of
+// shared scratch; recs_sm: the layer's record addresses staged in shared
+// memory, or null to read them from p.recs_all.
+template <int NT>
+__device__ void group_assignments(const RouteParams& p, const GroupOut& g, const int32_t* ids_sm, int32_t* counts,
                                   int32_t* base, const uint64_t* recs_sm) {
     const int A = p.T * p.K;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -387,10 +507,10 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
         else record_error(p.err, ERR_BAD_TABLE);
     }
     __syncthreads();
-    if (p.E <= kRouteThreads) {
+    if (p.E <= NT) {
         // One expert per thread: exclusive scans of the assignment counts and of
         // the active flags over the CTA (warp scans, then the warp totals).
-        __shared__ int wtot_a[kRouteThreads / 32], wtot_n[kRouteThreads / 32];
+        __shared__ int wtot_a[NT / 32], wtot_n[NT / 32];
         const int e = threadIdx.x;
         const int c = e < p.E ? counts[e] : 0;
         int inc_a = c, inc_n = c > 0 ? 1 : 0;
@@ -408,13 +528,13 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
         const int idx = pre_n + inc_n - (c > 0 ? 1 : 0);
         if (c > 0) {
             base[e] = start;
-            p.active[idx] = e;
-            p.off[idx] = start;
-            if (p.recs_all) p.recs_active[idx] = recs_sm ? recs_sm[e] : __ldcg(p.recs_all + e);
+            g.active[idx] = e;
+            g.off[idx] = start;
+            if (p.recs_all) g.recs_active[idx] = recs_sm ? recs_sm[e] : __ldcg(p.recs_all + e);
         }
-        if (threadIdx.x == kRouteThreads - 1) {
-            p.off[pre_n + inc_n] = pre_a + inc_a;
-            *p.n_active = pre_n + inc_n;
+        if (threadIdx.x == NT - 1) {
+            g.off[pre_n + inc_n] = pre_a + inc_a;
+            *g.n_active = pre_n + inc_n;
         }
         __syncthreads();
     } else if (threadIdx.x < 32) {
@@ -434,16 +554,16 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
             const int idx = run_n + inc_n - (c > 0 ? 1 : 0);
             if (e < p.E && c > 0) {
                 base[e] = start;
-                p.active[idx] = e;
-                p.off[idx] = start;
-                if (p.recs_all) p.recs_active[idx] = recs_sm ? recs_sm[e] : __ldcg(p.recs_all + e);
+                g.active[idx] = e;
+                g.off[idx] = start;
+                if (p.recs_all) g.recs_active[idx] = recs_sm ? recs_sm[e] : __ldcg(p.recs_all + e);
             }
             run_a += __shfl_sync(0xffffffffu, inc_a, 31);
             run_n += __shfl_sync(0xffffffffu, inc_n, 31);
         }
         if (lane == 0) {
-            p.off[run_n] = run_a;
-            *p.n_active = run_n;
+            g.off[run_n] = run_a;
+            *g.n_active = run_n;
         }
     }
     if (threadIdx.x < 32) {
@@ -455,14 +575,63 @@ __device__ void group_assignments(const RouteParams& p, const int32_t* ids_sm, i
             const int rank = __popc(peers & ((1u << lane) - 1u));
             if (s < A && e >= 0 && e < p.E) {
                 const int a = base[e] + rank;
-                p.assign_tok[a] = s / p.K;
-                p.slot_assign[s] = a;
+                g.assign_tok[a] = s / p.K;
+                g.slot_assign[s] = a;
             }
             __syncwarp();
             // the highest lane of each peer group advances the expert's base
             if (s < A && e >= 0 && e < p.E && (peers >> lane) == 1u) base[e] += rank + 1;
             __syncwarp();
         }
+    }
+}
+
+// The tables of group_assignments for at most 32 assignments, by one warp (all
+// its lanes call this): lane s holds assignment s; its position in (expert,
+// slot) order is the count of assignments of smaller experts plus the earlier
+// slots of its own expert; the first slot of each expert leads the expert's
+// group, whose index is the count of leaders of smaller experts.
+__device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_t* ids_sm, const uint64_t* recs_sm) {
+    const int lane = threadIdx.x & 31;
+    const int A = p.T * p.K;
+    int key = 0x7fffffff;
+    bool valid = false;
+    if (lane < A) {
+        const int e = ids_sm[lane];
+        valid = e >= 0 && e < p.E;
+        if (valid) key = e;
+        else record_error(p.err, ERR_BAD_TABLE);
+    }
+    int lt = 0, before = 0;
+#pragma unroll 8
+    for (int q = 0; q < 32; q++) {
+        const int kq = __shfl_sync(0xffffffffu, key, q);
+        lt += kq < key ? 1 : 0;
+        before += (kq == key && q < lane) ? 1 : 0;
+    }
+    const bool leader = valid && before == 0;
+    const unsigned lead = __ballot_sync(0xffffffffu, leader);
+    const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+    int idx = 0;
+#pragma unroll 8
+    for (int q = 0; q < 32; q++) {
+        const int kq = __shfl_sync(0xffffffffu, key, q);
+        idx += (((lead >> q) & 1u) && kq < key) ? 1 : 0;
+    }
+    if (valid) {
+        const int a = lt + before;
+        g.assign_tok[a] = lane / p.K;
+        g.slot_assign[lane] = a;
+    }
+    if (leader) {
+        g.active[idx] = key;
+        g.off[idx] = lt;
+        if (p.recs_all) g.recs_active[idx] = recs_sm ? recs_sm[key] : __ldcg(p.recs_all + key);
+    }
+    if (lane == 0) {
+        const int n = __popc(lead);
+        g.off[n] = __popc(vmask);
+        *g.n_active = n;
     }
 }
 
@@ -587,17 +756,19 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         }
         // grouping needs every token's picks in one CTA
         if (ranked) {
-            topk_block(p, 0, p.T, prob, pick_id, pick_p, ids_sm);
+            topk_block<kRouteThreads>(p, p.logits, 0, p.T, prob, pick_id, pick_p, p.ids, p.weights, ids_sm);
         } else {
             for (int t = warp; t < p.T; t += nwarps) topk_token(p, t, lane, ids_sm);
         }
         __syncthreads();
         if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_TOPK_DONE);
-        group_assignments(p, ids_sm, ids_sm + p.T * p.K, ids_sm + p.T * p.K + p.E, recs_sm);
+        const GroupOut go{p.n_active, p.active, p.off, p.assign_tok, p.slot_assign, p.recs_active};
+        group_assignments<kRouteThreads>(p, go, ids_sm, ids_sm + p.T * p.K, ids_sm + p.T * p.K + p.E, recs_sm);
         if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_END);
     } else if (ranked) {
         for (int t0 = blockIdx.x * nwarps; t0 < p.T; t0 += gridDim.x * nwarps) {
-            topk_block(p, t0, min(p.T, t0 + nwarps), prob, pick_id, pick_p, nullptr);
+            topk_block<kRouteThreads>(p, p.logits, t0, min(p.T, t0 + nwarps), prob, pick_id, pick_p, p.ids, p.weights,
+                                      nullptr);
             __syncthreads();
         }
     } else {

@@ -128,10 +128,6 @@ struct StreamParams {
     unsigned* err;
 };
 
-__device__ __forceinline__ const uint8_t* rec_at(const uint64_t* recs, int i) {
-    return reinterpret_cast<const uint8_t*>(__ldcg(reinterpret_cast<const unsigned long long*>(recs) + i));
-}
-
 // ---- activation slices in registers ----------------------------------------------------
 
 // 16 bf16 activations as f16 pairs scaled by 2^-s (s from the largest
@@ -237,12 +233,41 @@ struct XSlice<false> {
     __device__ __forceinline__ float scale() const { return 1.0f; }
 };
 
-// ---- units ----------------------------------------------------------------------------------
+// ---- units and routing tables ---------------------------------------------------------------
 
-// The CTA's slice [u0, u1) of the flat unit list.
-__device__ __forceinline__ void cta_units(const StreamParams& p, bool moe, int& u0, int& u1) {
-    const int n_e = moe ? (p.n_e_dev ? __ldcg(p.n_e_dev) : p.n_e_host) : 1;
-    const int units = n_e * p.gpe;
+// The routing tables a MoE launch streams from: record address of each expert
+// group, assignment ranges off[n_e + 1], token of each assignment, group count.
+// They live in global memory (written by an earlier kernel) or, in the fused
+// decode kernel, in this CTA's shared memory (TSMEM).
+struct Tables {
+    const uint64_t* recs;
+    const int32_t* off;
+    const int32_t* assign_tok;
+    int n_e;
+};
+
+template <bool TSMEM>
+__device__ __forceinline__ int tab_i32(const int32_t* a) {
+    if constexpr (TSMEM) return *a;
+    else return __ldcg(a);
+}
+
+template <bool TSMEM>
+__device__ __forceinline__ unsigned long long tab_u64(const uint64_t* a) {
+    if constexpr (TSMEM) return *reinterpret_cast<const unsigned long long*>(a);
+    else return __ldcg(reinterpret_cast<const unsigned long long*>(a));
+}
+
+// The tables of a stand-alone launch (dense launches: one group, no tables).
+__device__ __forceinline__ Tables global_tables(const StreamParams& p, bool moe) {
+    Tables tb{p.recs, p.off, p.assign_tok, 1};
+    if (moe) tb.n_e = p.n_e_dev ? __ldcg(p.n_e_dev) : p.n_e_host;
+    return tb;
+}
+
+// The CTA's slice [u0, u1) of the flat list of n_e * gpe units.
+__device__ __forceinline__ void cta_units(int n_e, int gpe, int& u0, int& u1) {
+    const int units = n_e * gpe;
     u0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * units) / gridDim.x);
     u1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * units) / gridDim.x);
 }
@@ -254,6 +279,33 @@ template <int PARTS>
 __device__ __forceinline__ int slot_row(int rpi, int rp, int j) {
     constexpr int H = kRows / 2;
     return PARTS == 2 ? (j / H) * (H * rp) + H * rpi + (j % H) : rpi + j * rp;
+}
+
+// The shared-memory rings of a streaming CTA: weight stages with their
+// full/empty mbarriers, per-pass unit tables with theirs, the reduction
+// buffers and the chunk headers.  `meta_stride` (ints) holds the largest pass
+// table of any phase the CTA runs.
+struct Ring {
+    uint8_t* stage_buf;
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* mfull;
+    uint64_t* mempty;
+    float* red;      // [2][kWarps][kRedV]
+    int* meta;       // [kMetaBufs][meta_stride]
+    int* chunk_hdr;  // [2][4]
+    int stages, slot_bytes, meta_stride;
+};
+
+// Positions in the rings, carried from one phase to the next within a launch:
+// s counts stages, q pass tables, rparity the reduction buffer in use.
+struct RingPos {
+    int s, q, rparity;
+};
+
+template <int PARTS, bool MOE>
+__host__ __device__ constexpr unsigned timeline_kind() {
+    return !MOE ? TL_GEMV : (PARTS == 2 ? TL_GATE_UP : TL_DOWN);
 }
 
 // ---- per-pass reduction and output ----------------------------------------------------------
@@ -316,213 +368,175 @@ __device__ __forceinline__ void reduce_write(const StreamParams& p, const float 
     }
 }
 
-// ---- the kernel ---------------------------------------------------------------------------
+// ---- the three roles --------------------------------------------------------------------
 
-// PARTS: 2 = fused gate/up + SwiGLU (expert records), 1 = one matrix.
-// TB: token slots per unit.  P: units per reduction pass (kRows * P * TB <= 16).
-//   With P > 1 every unit has at most TB assignments (the host guarantees it);
-//   with P == 1 a unit may have more, processed in chunks of TB against the
-//   stage held in shared memory.
-// MOE: units come from expert groups (recs/off); else from the dense q.
-// EARLY: the copy producer reads the routing tables before griddepcontrol.wait
-//   (valid only two launches after the kernel that wrote them, see capi.cu).
-// BLK: 128x128 scale blocks (p.layout == 1), else 1x128.
-template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool EARLY, bool BLK>
-__global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kernel(const StreamParams p) {
-    static_assert(kRows * P * TB <= kRedV, "too many partials per lane");
-    constexpr unsigned TLK = !MOE ? TL_GEMV : (PARTS == 2 ? TL_GATE_UP : TL_DOWN);
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int S = p.stages;
-    uint8_t* stage_buf = smem;
-    const int slot_bytes = p.slot_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * slot_bytes);
-    uint64_t* empty = full + kMaxStages;
-    uint64_t* mfull = empty + kMaxStages;
-    uint64_t* mempty = mfull + kMetaBufs;
-    float* red = reinterpret_cast<float*>(mempty + kMetaBufs);  // [2][kWarps][kRedV]
+// Copy producer (one lane): streams units [u0, u1) into the stage ring,
+// continuing at ring position s.  After a wait that ran out it drains its
+// copies in flight and returns false.
+template <int PARTS, int P, bool MOE, bool TSMEM>
+__device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1, int& s) {
+    constexpr unsigned TLK = timeline_kind<PARTS, MOE>();
+    if (u1 <= u0) return true;
+    const int S = rg.stages, KS = p.ks;
+    const int kcs = min(p.kc, p.k);  // shared-memory row stride
+    const uint64_t pol = make_evict_first_policy();
+    int ei = u0 / p.gpe;
+    const uint8_t* rec = MOE ? reinterpret_cast<const uint8_t*>(tab_u64<TSMEM>(tb.recs + ei)) : p.q;
+    const uint8_t* rec_next =
+        (MOE && ei + 1 < tb.n_e) ? reinterpret_cast<const uint8_t*>(tab_u64<TSMEM>(tb.recs + ei + 1)) : rec;
+    int rec_ei = ei;
+    bool ok = true, first = true;
+    const int s_begin = s;
+    for (int pf = u0; pf < u1 && ok; pf += P) {
+        const int pn = min(P, u1 - pf);
+        for (int ks = 0; ks < KS && ok; ks++) {
+            for (int pi = 0; pi < pn; pi++, s++) {
+                const int slot = s % S;
+                ok = mbar_wait(&rg.empty[slot], ((s / S) & 1) ^ 1, p.err, ERR_EMPTY_WAIT);
+                if (!ok) break;
+                const int u = pf + pi;
+                const int uei = u / p.gpe, g = u - uei * p.gpe;
+                if (MOE && uei != rec_ei) {
+                    rec = uei == rec_ei + 1 ? rec_next : reinterpret_cast<const uint8_t*>(tab_u64<TSMEM>(tb.recs + uei));
+                    rec_ei = uei;
+                    if (uei + 1 < tb.n_e) rec_next = reinterpret_cast<const uint8_t*>(tab_u64<TSMEM>(tb.recs + uei + 1));
+                }
+                const int row0 = g * p.rpp;
+                const int nr = min(p.rpp, p.nrows - row0);
+                const int kc0 = ks * p.kc;
+                const int kcl = min(p.kc, p.k - kc0);
+                uint8_t* dst = rg.stage_buf + slot * rg.slot_bytes;
+                mbar_arrive_expect_tx(&rg.full[slot], static_cast<unsigned>(PARTS * nr * kcl));
+                if (first) {
+                    tl_mark(TLK, TL_FIRST_COPY);
+                    first = false;
+                }
+#pragma unroll
+                for (int part = 0; part < PARTS; part++) {
+                    const uint8_t* src = (MOE ? rec + (part ? p.w_off[1] : p.w_off[0]) : rec) +
+                                         static_cast<int64_t>(row0) * p.k + kc0;
+                    uint8_t* d = dst + part * p.rpp * kcs;
+                    if (kcl == p.k) {
+                        bulk_g2s(d, src, static_cast<unsigned>(nr * kcl), &rg.full[slot], pol);
+                    } else {
+                        for (int r = 0; r < nr; r++)
+                            bulk_g2s(d + r * kcs, src + static_cast<int64_t>(r) * p.k, static_cast<unsigned>(kcl),
+                                     &rg.full[slot], pol);
+                    }
+                }
+            }
+        }
+    }
+    tl_mark(TLK, TL_LAST_COPY);
+    if (!ok) {
+        // copies issued from this phase's stages that may still be in flight
+        for (int d = max(s_begin, s - S); d < s; d++) mbar_wait(&rg.full[d % S], (d / S) & 1, p.err, ERR_DRAIN_WAIT);
+    }
+    return ok;
+}
+
+// Metadata producer (one warp): for every pass of P units of [u0, u1) loads
+// the unit headers and block-scale rows into the table ring, continuing at
+// table position q.
+template <int PARTS, int P, bool MOE, bool TSMEM>
+__device__ bool stream_meta(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1, int& q) {
+    const int lane = threadIdx.x & 31;
     const int meta_ints = P * 4;
     const int pair_floats = p.sr * p.nb;  // scale table of one (unit, part)
-    int* meta = reinterpret_cast<int*>(red + 2 * kWarps * kRedV);  // [kMetaBufs][P*4 ints | P*PARTS*SR*NB floats]
-    const int meta_stride = meta_ints + P * PARTS * pair_floats;
-    int* chunk_hdr = meta + kMetaBufs * meta_stride;  // [2][4]
+    for (int pf = u0; pf < u1; pf += P, q++) {
+        const int buf = q % kMetaBufs;
+        if (!mbar_wait(&rg.mempty[buf], ((q / kMetaBufs) & 1) ^ 1, p.err, ERR_EMPTY_WAIT)) return false;
+        const int pn = min(P, u1 - pf);
+        int* hdr = rg.meta + buf * rg.meta_stride;
+        float* sc = reinterpret_cast<float*>(hdr + meta_ints);
+        // unit headers and record addresses: lane pi holds unit pi's
+        unsigned long long urec = reinterpret_cast<unsigned long long>(p.q);
+        int urow0 = 0;
+        if (lane < pn) {
+            const int u = pf + lane;
+            const int ei = u / p.gpe, g = u - ei * p.gpe;
+            urow0 = g * p.rpp;
+            if (MOE) urec = tab_u64<TSMEM>(tb.recs + ei);
+            hdr[lane * 4 + 0] = MOE ? tab_i32<TSMEM>(tb.off + ei) : 0;
+            hdr[lane * 4 + 1] = MOE ? tab_i32<TSMEM>(tb.off + ei + 1) : p.t;
+            hdr[lane * 4 + 2] = urow0;
+            hdr[lane * 4 + 3] = min(p.rpp, p.nrows - urow0);
+        }
+        // scale tables, one per (unit, part): 128x128 keeps the unit's block row
+        // (unit sizes divide 128), 1x128 its RPP rows; NB blocks per row.  All loads
+        // of a batch (8 per lane, across every (unit, part) of the pass) are
+        // issued before any store, so a pass costs one L2 round trip.
+        const int total = pn * PARTS * pair_floats;
+        for (int e0 = 0; e0 < total; e0 += 8 * 32) {
+            float v[8];
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                const int e = e0 + m * 32 + lane;
+                const int ec = e < total ? e : 0;
+                const int pair = ec / pair_floats, ep = ec - pair * pair_floats;
+                const int pi = pair / PARTS, part = pair - pi * PARTS;
+                const unsigned long long rb = __shfl_sync(0xffffffffu, urec, pi);
+                const int row0 = __shfl_sync(0xffffffffu, urow0, pi);
+                v[m] = 0.0f;
+                if (e < total) {
+                    const float* sp = MOE ? reinterpret_cast<const float*>(
+                                                reinterpret_cast<const uint8_t*>(rb) + (part ? p.s_off[1] : p.s_off[0]))
+                                          : p.scale;
+                    const int r = ep / p.nb, kb = ep - r * p.nb;
+                    const int srow = p.layout ? (row0 >> 7) + r : row0 + r;
+                    if ((p.layout ? srow * 128 : srow) < p.nrows) v[m] = __ldg(sp + static_cast<int64_t>(srow) * p.nb + kb);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                const int e = e0 + m * 32 + lane;
+                if (e < total) sc[e] = v[m];
+            }
+        }
+        mbar_arrive(&rg.mfull[buf]);  // release: this lane's header and table writes
+    }
+    return true;
+}
 
+// Consumer warps: the arithmetic of units [u0, u1) from the rings, continuing
+// at ring positions `pos`.  Returns false when a wait ran out.
+template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool BLK, bool TSMEM>
+__device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1,
+                               RingPos& pos) {
+    static_assert(kRows * P * TB <= kRedV, "too many partials per lane");
+    constexpr unsigned TLK = timeline_kind<PARTS, MOE>();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int KS = p.ks;
+    const int S = rg.stages, KS = p.ks;
     const int kcs = min(p.kc, p.k);  // shared-memory row stride
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < S; i++) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kWarps);
-        }
-        for (int i = 0; i < kMetaBufs; i++) {
-            mbar_init(&mfull[i], 32);
-            mbar_init(&mempty[i], kWarps);
-        }
-        fence_barrier_init();
-        tl_mark(TLK, TL_ENTRY);
-    }
-    __syncthreads();
-
-    if (warp == kWarps) {
-        // ================= copy producer =================
-        // weights and (dense, or tables written two launches back) unit tables do
-        // not depend on the previous kernel
-        if (MOE && !EARLY) pdl_wait();
-        pdl_launch_dependents();
-        if (lane != 0) return;
-        int u0, u1;
-        cta_units(p, MOE, u0, u1);
-        if (u1 <= u0) return;
-        const int n_e = MOE ? (p.n_e_dev ? __ldcg(p.n_e_dev) : p.n_e_host) : 1;
-        const uint64_t pol = make_evict_first_policy();
-        int ei = u0 / p.gpe;
-        const uint8_t* rec = MOE ? rec_at(p.recs, ei) : p.q;
-        const uint8_t* rec_next = (MOE && ei + 1 < n_e) ? rec_at(p.recs, ei + 1) : rec;
-        int rec_ei = ei;
-        bool ok = true;
-        int s = 0;
-        for (int pf = u0; pf < u1 && ok; pf += P) {
-            const int pn = min(P, u1 - pf);
-            for (int ks = 0; ks < KS && ok; ks++) {
-                for (int pi = 0; pi < pn; pi++, s++) {
-                    const int slot = s % S;
-                    ok = mbar_wait(&empty[slot], ((s / S) & 1) ^ 1, p.err, ERR_EMPTY_WAIT);
-                    if (!ok) break;
-                    const int u = pf + pi;
-                    const int uei = u / p.gpe, g = u - uei * p.gpe;
-                    if (MOE && uei != rec_ei) {
-                        rec = uei == rec_ei + 1 ? rec_next : rec_at(p.recs, uei);
-                        rec_ei = uei;
-                        if (uei + 1 < n_e) rec_next = rec_at(p.recs, uei + 1);
-                    }
-                    const int row0 = g * p.rpp;
-                    const int nr = min(p.rpp, p.nrows - row0);
-                    const int kc0 = ks * p.kc;
-                    const int kcl = min(p.kc, p.k - kc0);
-                    uint8_t* dst = stage_buf + slot * slot_bytes;
-                    mbar_arrive_expect_tx(&full[slot], static_cast<unsigned>(PARTS * nr * kcl));
-                    if (s == 0) tl_mark(TLK, TL_FIRST_COPY);
-#pragma unroll
-                    for (int part = 0; part < PARTS; part++) {
-                        const uint8_t* src = (MOE ? rec + (part ? p.w_off[1] : p.w_off[0]) : rec) +
-                                             static_cast<int64_t>(row0) * p.k + kc0;
-                        uint8_t* d = dst + part * p.rpp * kcs;
-                        if (kcl == p.k) {
-                            bulk_g2s(d, src, static_cast<unsigned>(nr * kcl), &full[slot], pol);
-                        } else {
-                            for (int r = 0; r < nr; r++)
-                                bulk_g2s(d + r * kcs, src + static_cast<int64_t>(r) * p.k,
-                                         static_cast<unsigned>(kcl), &full[slot], pol);
-                        }
-                    }
-                }
-            }
-        }
-        tl_mark(TLK, TL_LAST_COPY);
-        if (!ok) {
-            for (int d = (s > S ? s - S : 0); d < s; d++)
-                mbar_wait(&full[d % S], (d / S) & 1, p.err, ERR_DRAIN_WAIT);
-        }
-        return;
-    }
-
-    if (warp == kWarps + 1) {
-        // ================= metadata producer =================
-        // block scales are weights; the unit tables are as ready as for the copy producer
-        if (MOE && !EARLY) pdl_wait();
-        pdl_launch_dependents();
-        int u0, u1;
-        cta_units(p, MOE, u0, u1);
-        int q = 0;
-        for (int pf = u0; pf < u1; pf += P, q++) {
-            const int buf = q % kMetaBufs;
-            if (!mbar_wait(&mempty[buf], ((q / kMetaBufs) & 1) ^ 1, p.err, ERR_EMPTY_WAIT)) return;
-            const int pn = min(P, u1 - pf);
-            int* hdr = meta + buf * meta_stride;
-            float* sc = reinterpret_cast<float*>(hdr + meta_ints);
-            // unit headers and record addresses: lane pi holds unit pi's
-            unsigned long long urec = reinterpret_cast<unsigned long long>(p.q);
-            int urow0 = 0;
-            if (lane < pn) {
-                const int u = pf + lane;
-                const int ei = u / p.gpe, g = u - ei * p.gpe;
-                urow0 = g * p.rpp;
-                if (MOE) urec = __ldcg(reinterpret_cast<const unsigned long long*>(p.recs) + ei);
-                hdr[lane * 4 + 0] = MOE ? __ldcg(p.off + ei) : 0;
-                hdr[lane * 4 + 1] = MOE ? __ldcg(p.off + ei + 1) : p.t;
-                hdr[lane * 4 + 2] = urow0;
-                hdr[lane * 4 + 3] = min(p.rpp, p.nrows - urow0);
-            }
-            // scale tables, one per (unit, part): 128x128 keeps the unit's block row
-            // (unit sizes divide 128), 1x128 its RPP rows; NB blocks per row.  All loads
-            // of a batch (8 per lane, across every (unit, part) of the pass) are
-            // issued before any store, so a pass costs one L2 round trip.
-            const int total = pn * PARTS * pair_floats;
-            for (int e0 = 0; e0 < total; e0 += 8 * 32) {
-                float v[8];
-#pragma unroll
-                for (int m = 0; m < 8; m++) {
-                    const int e = e0 + m * 32 + lane;
-                    const int ec = e < total ? e : 0;
-                    const int pair = ec / pair_floats, ep = ec - pair * pair_floats;
-                    const int pi = pair / PARTS, part = pair - pi * PARTS;
-                    const unsigned long long rb = __shfl_sync(0xffffffffu, urec, pi);
-                    const int row0 = __shfl_sync(0xffffffffu, urow0, pi);
-                    v[m] = 0.0f;
-                    if (e < total) {
-                        const float* sp = MOE ? reinterpret_cast<const float*>(
-                                                    reinterpret_cast<const uint8_t*>(rb) + (part ? p.s_off[1] : p.s_off[0]))
-                                              : p.scale;
-                        const int r = ep / p.nb, kb = ep - r * p.nb;
-                        const int srow = p.layout ? (row0 >> 7) + r : row0 + r;
-                        if ((p.layout ? srow * 128 : srow) < p.nrows)
-                            v[m] = __ldg(sp + static_cast<int64_t>(srow) * p.nb + kb);
-                    }
-                }
-#pragma unroll
-                for (int m = 0; m < 8; m++) {
-                    const int e = e0 + m * 32 + lane;
-                    if (e < total) sc[e] = v[m];
-                }
-            }
-            mbar_arrive(&mfull[buf]);  // release: this lane's header and table writes
-        }
-        return;
-    }
-
-    // ================= consumers =================
-    pdl_wait();
-    pdl_launch_dependents();
-    if (threadIdx.x == 0) tl_mark(TLK, TL_WAITED);
-    int u0, u1;
-    cta_units(p, MOE, u0, u1);
-    if (u1 <= u0) return;
+    const int meta_ints = P * 4;
+    const int pair_floats = p.sr * p.nb;
 
     const bool active = warp < p.rp * p.nsl;  // warp-uniform
     const int sl = active ? warp % p.nsl : 0;
     const int rpi = active ? warp / p.nsl : 0;
     const int col = sl * 512 + lane * 16;
-    const int kc = p.kc, kdim = p.k, nb_k = p.nb, rpp = p.rpp;
+    const int kc = p.kc, kdim = p.k, nb_k = p.nb;
     // byte offset of each of the warp's rows in a stage and its row within its part
     int roff[kRows], rin[kRows];
 #pragma unroll
     for (int j = 0; j < kRows; j++) {
         const int srow = slot_row<PARTS>(rpi, p.rp, j);
         roff[j] = srow * kcs;
-        rin[j] = PARTS == 2 ? srow - (j / (kRows / 2)) * rpp : srow;
+        rin[j] = PARTS == 2 ? srow - (j / (kRows / 2)) * p.rpp : srow;
     }
 
     XSlice<XBF16> xs[TB];
     int x_key0 = -1, x_key1 = -1;  // (expert or K-stage, first assignment) the slices hold
-    int s = 0, q = 0, rparity = 0;
+    int s = pos.s, q = pos.q, rparity = pos.rparity;
+    bool first_meta = true, first_stage = true;
 
     for (int pf = u0; pf < u1; pf += P, q++) {
         const int pn = min(P, u1 - pf);
         const int buf = q % kMetaBufs;
-        if (!mbar_wait(&mfull[buf], (q / kMetaBufs) & 1, p.err, ERR_FULL_WAIT)) return;
-        if (q == 0 && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_META);
-        const int* hdr = meta + buf * meta_stride;
+        if (!mbar_wait(&rg.mfull[buf], (q / kMetaBufs) & 1, p.err, ERR_FULL_WAIT)) return false;
+        if (first_meta && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_META);
+        first_meta = false;
+        const int* hdr = rg.meta + buf * rg.meta_stride;
         const float* sct = reinterpret_cast<const float*>(hdr + meta_ints);
         float acc[P][kRows][TB];
 #pragma unroll
@@ -568,9 +582,10 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
                     // activations of a MoE unit depend only on its first assignment
                     const int key0 = MOE ? 0 : ks;
                     const int slot = s % S;
-                    if (!mbar_wait(&full[slot], (s / S) & 1, p.err, ERR_FULL_WAIT)) return;
-                    if (s == 0 && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_STAGE);
-                    const uint8_t* base = stage_buf + slot * slot_bytes + ccol;
+                    if (!mbar_wait(&rg.full[slot], (s / S) & 1, p.err, ERR_FULL_WAIT)) return false;
+                    if (first_stage && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_STAGE);
+                    first_stage = false;
+                    const uint8_t* base = rg.stage_buf + slot * rg.slot_bytes + ccol;
                     for (int a0 = a_begin; a0 < a_end; a0 += TB) {
                         const int nb = min(TB, a_end - a0);
                         if (x_key0 != key0 || x_key1 != a0) {
@@ -580,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
                                     int64_t xr;
                                     // gate/up: the assignment's token; down: the
                                     // assignment's h row; dense: the token
-                                    if (MOE && PARTS == 2) xr = __ldcg(p.assign_tok + a0 + b);
+                                    if (MOE && PARTS == 2) xr = tab_i32<TSMEM>(tb.assign_tok + a0 + b);
                                     else xr = a0 + b;
                                     xs[b].load(p.x, xr * kdim + kc0 + col);
                                 } else {
@@ -605,20 +620,19 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
                                 WDec<XBF16> w;
                                 w.decode(raw[j]);
 #pragma unroll
-                                for (int b = 0; b < TB; b++)
-                                    acc[pi][j][b] = fmaf(xs[b].dot(w), sx[j][b], acc[pi][j][b]);
+                                for (int b = 0; b < TB; b++) acc[pi][j][b] = fmaf(xs[b].dot(w), sx[j][b], acc[pi][j][b]);
                             }
                         }
                         if (chunked) {
                             // more assignments than token slots: reduce and write this chunk now
-                            int* ch = chunk_hdr + rparity * 4;
+                            int* ch = rg.chunk_hdr + rparity * 4;
                             if (threadIdx.x == 0) {
                                 ch[0] = a0;
                                 ch[1] = a0 + nb;
                                 ch[2] = hdr[pi * 4 + 2];
                                 ch[3] = nr;
                             }
-                            reduce_write<PARTS, TB, P, MOE>(p, acc, red + rparity * kWarps * kRedV, ch, 1, warp,
+                            reduce_write<PARTS, TB, P, MOE>(p, acc, rg.red + rparity * kWarps * kRedV, ch, 1, warp,
                                                             lane);
                             rparity ^= 1;
 #pragma unroll
@@ -628,20 +642,116 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
                         }
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[slot]);
+                    if (lane == 0) mbar_arrive(&rg.empty[slot]);
                     s++;
                 }
             }
         }
         if (!chunked_any) {
-            reduce_write<PARTS, TB, P, MOE>(p, acc, red + rparity * kWarps * kRedV, hdr, pn, warp, lane);
+            reduce_write<PARTS, TB, P, MOE>(p, acc, rg.red + rparity * kWarps * kRedV, hdr, pn, warp, lane);
             rparity ^= 1;
         }
         // this warp is done with the pass's table: hand it back
         __syncwarp();
-        if (lane == 0) mbar_arrive(&mempty[buf]);
+        if (lane == 0) mbar_arrive(&rg.mempty[buf]);
     }
+    pos.s = s;
+    pos.q = q;
+    pos.rparity = rparity;
     if (threadIdx.x == 0) tl_mark(TLK, TL_END);
+    return true;
+}
+
+// Initialises the ring's mbarriers (one thread).
+__device__ __forceinline__ void ring_init(const Ring& rg) {
+    for (int i = 0; i < rg.stages; i++) {
+        mbar_init(&rg.full[i], 1);
+        mbar_init(&rg.empty[i], kWarps);
+    }
+    for (int i = 0; i < kMetaBufs; i++) {
+        mbar_init(&rg.mfull[i], 32);
+        mbar_init(&rg.mempty[i], kWarps);
+    }
+}
+
+// ---- the stand-alone kernel -----------------------------------------------------------------
+
+// PARTS: 2 = fused gate/up + SwiGLU (expert records), 1 = one matrix.
+// TB: token slots per unit.  P: units per reduction pass (kRows * P * TB <= 16).
+//   With P > 1 every unit has at most TB assignments (the host guarantees it);
+//   with P == 1 a unit may have more, processed in chunks of TB against the
+//   stage held in shared memory.
+// MOE: units come from expert groups (recs/off); else from the dense q.
+// EARLY: the copy producer reads the routing tables before griddepcontrol.wait
+//   (valid only two launches after the kernel that wrote them, see capi.cu).
+// BLK: 128x128 scale blocks (p.layout == 1), else 1x128.
+//
+// Shared-memory layout: [stages x slot_bytes][full][empty][meta_full][meta_empty]
+// [red 2 x kWarps x kRedV][meta kMetaBufs x (P x 4 ints + P x PARTS x SR x NB floats)]
+// [chunk headers 2 x 4 ints]
+template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool EARLY, bool BLK>
+__global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kernel(const StreamParams p) {
+    constexpr unsigned TLK = timeline_kind<PARTS, MOE>();
+    extern __shared__ __align__(128) uint8_t smem[];
+    Ring rg;
+    rg.stages = p.stages;
+    rg.slot_bytes = p.slot_bytes;
+    rg.stage_buf = smem;
+    rg.full = reinterpret_cast<uint64_t*>(smem + p.stages * p.slot_bytes);
+    rg.empty = rg.full + kMaxStages;
+    rg.mfull = rg.empty + kMaxStages;
+    rg.mempty = rg.mfull + kMetaBufs;
+    rg.red = reinterpret_cast<float*>(rg.mempty + kMetaBufs);
+    rg.meta = reinterpret_cast<int*>(rg.red + 2 * kWarps * kRedV);
+    rg.meta_stride = P * 4 + P * PARTS * p.sr * p.nb;
+    rg.chunk_hdr = rg.meta + kMetaBufs * rg.meta_stride;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        ring_init(rg);
+        fence_barrier_init();
+        tl_mark(TLK, TL_ENTRY);
+    }
+    __syncthreads();
+
+    if (warp == kWarps) {
+        // ================= copy producer =================
+        // weights and (dense, or tables written two launches back) unit tables do
+        // not depend on the previous kernel
+        if (MOE && !EARLY) pdl_wait();
+        pdl_launch_dependents();
+        if (lane != 0) return;
+        const Tables tb = global_tables(p, MOE);
+        int u0, u1;
+        cta_units(tb.n_e, p.gpe, u0, u1);
+        int s = 0;
+        stream_copy<PARTS, P, MOE, false>(p, tb, rg, u0, u1, s);
+        return;
+    }
+
+    if (warp == kWarps + 1) {
+        // ================= metadata producer =================
+        // block scales are weights; the unit tables are as ready as for the copy producer
+        if (MOE && !EARLY) pdl_wait();
+        pdl_launch_dependents();
+        const Tables tb = global_tables(p, MOE);
+        int u0, u1;
+        cta_units(tb.n_e, p.gpe, u0, u1);
+        int q = 0;
+        stream_meta<PARTS, P, MOE, false>(p, tb, rg, u0, u1, q);
+        return;
+    }
+
+    // ================= consumers =================
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) tl_mark(TLK, TL_WAITED);
+    const Tables tb = global_tables(p, MOE);
+    int u0, u1;
+    cta_units(tb.n_e, p.gpe, u0, u1);
+    if (u1 <= u0) return;
+    RingPos pos{0, 0, 0};
+    stream_consume<PARTS, TB, P, XBF16, MOE, BLK, false>(p, tb, rg, u0, u1, pos);
 }
 
 }  // namespace oomb

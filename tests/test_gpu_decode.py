@@ -1,0 +1,171 @@
+"""The one-launch decode step (decode_kernel) against the chain of kernels.
+
+oomb_moe_decode_fp8 runs the whole routed step of a resident layer in one
+persistent launch for up to 16 tokens and routers of at most 256 experts;
+OOMB_DECODE_CHAIN=1 makes it run the chain route -> gate/up -> down -> combine
+instead (each of those kernels is checked against the oracle in
+test_gpu_parity.py).  The two must agree bit for bit on every output (ids,
+weights, out) across activation dtypes, scale layouts, output dtypes, batch
+sizes (one token, two, and the chunked path) and layer shapes; repeated
+launches on one workspace (grid-barrier and row-group counters reset
+themselves), launches of different batch sizes on one workspace and CUDA graph
+replays must keep giving the same bits; and the one-launch result must meet
+the float64 bound on its own.
+"""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import oracle as O  # noqa: E402
+import homelab_b200 as hb  # noqa: E402
+from homelab_b200 import SCALE_128X128, SCALE_1X128  # noqa: E402
+from homelab_b200.backend import Gpu  # noqa: E402
+from homelab_b200.records import ExpertBank  # noqa: E402
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a GPU", allow_module_level=True)
+
+DEV = torch.device("cuda", 0)
+
+# hidden, experts, top_k, inter, scale layout
+LAYERS = {
+    "config2": (2048, 128, 8, 768, SCALE_128X128),
+    "small": (1024, 64, 6, 512, SCALE_1X128),
+    "wide": (4096, 256, 8, 256, SCALE_128X128),
+    "odd": (528, 40, 5, 272, SCALE_1X128),
+}
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    g = Gpu(0)
+    yield g
+    torch.cuda.synchronize()
+    assert g.device_error() == 0, "a bounded device wait ran out"
+
+
+_layers = {}
+
+
+def get_layer(gpu, name):
+    if name not in _layers:
+        H, E, K, I, layout = LAYERS[name]
+        b = ExpertBank(E, H, I, layout, DEV)
+        b.fill_random(gpu, seed=sum(map(ord, name)))
+        router = O.normal_bf16(7 + E, E * H, 0.0, 0.02)
+        router_d = torch.from_numpy(router.view(np.int16)).to(DEV).view(torch.bfloat16)
+        L = hb.MoeLayer(hidden=H, experts=E, top_k=K, router_w=router_d.data_ptr(), recs=b.addrs.data_ptr())
+        L.geo = b.geo
+        torch.cuda.synchronize()
+        _layers[name] = dict(bank=b, router=router, router_d=router_d, L=L)
+    return _layers[name]
+
+
+def make_x(H, t, xbf16, seed):
+    xb = O.normal_bf16(seed, t * H)
+    x = torch.from_numpy(xb.view(np.int16)).to(DEV).view(torch.bfloat16).view(t, H)
+    return x if xbf16 else x.float()
+
+
+def run(gpu, lay, x, t, out_dtype, chain, ws=None):
+    H, K = lay["L"].hidden, lay["L"].top_k
+    if ws is None:
+        ws = gpu.moe_decode_workspace(lay["L"], t)
+    out = torch.full((t, H), float("nan"), dtype=out_dtype, device=DEV)
+    ids = torch.full((t, K), -1, dtype=torch.int32, device=DEV)
+    wts = torch.full((t, K), float("nan"), dtype=torch.float32, device=DEV)
+    if chain:
+        os.environ["OOMB_DECODE_CHAIN"] = "1"
+    try:
+        gpu.moe_decode(lay["L"], x, t, out, ws, ids, wts)
+    finally:
+        os.environ.pop("OOMB_DECODE_CHAIN", None)
+    return out, ids, wts
+
+
+def same(a, b):
+    return a.shape == b.shape and torch.equal(a.view(torch.int32) if a.dtype == torch.float32 else a,
+                                              b.view(torch.int32) if b.dtype == torch.float32 else b)
+
+
+@pytest.mark.parametrize("name", list(LAYERS))
+@pytest.mark.parametrize("xbf16", [True, False])
+@pytest.mark.parametrize("t", [1, 2, 5, 16])
+def test_one_launch_equals_chain(gpu, name, xbf16, t):
+    lay = get_layer(gpu, name)
+    H = lay["L"].hidden
+    out_dtype = torch.bfloat16 if (t % 2 == 1) else torch.float32
+    x = make_x(H, t, xbf16, 500 + t)
+    got = run(gpu, lay, x, t, out_dtype, chain=False)
+    want = run(gpu, lay, x, t, out_dtype, chain=True)
+    torch.cuda.synchronize()
+    for g, w, what in zip(got, want, ("out", "ids", "weights")):
+        assert same(g, w), f"{what} differs from the chain of kernels"
+
+
+def test_repeated_launches_and_batch_sizes_share_a_workspace(gpu):
+    lay = get_layer(gpu, "config2")
+    H = lay["L"].hidden
+    ws = gpu.moe_decode_workspace(lay["L"], 16)
+    xs = {t: make_x(H, t, True, 900 + t) for t in (1, 3, 16)}
+    want = {t: run(gpu, lay, xs[t], t, torch.float32, chain=True) for t in xs}
+    for i, t in enumerate((1, 1, 16, 3, 1, 16, 16, 3)):
+        got = run(gpu, lay, xs[t], t, torch.float32, chain=False, ws=ws)
+        if i % 3 == 2:  # the chain of kernels on the same workspace in between
+            run(gpu, lay, xs[t], t, torch.float32, chain=True, ws=ws)
+        torch.cuda.synchronize()
+        for g, w in zip(got, want[t]):
+            assert same(g, w)
+
+
+def test_graph_replays_give_the_same_bits(gpu):
+    lay = get_layer(gpu, "config2")
+    L, H, K = lay["L"], lay["L"].hidden, lay["L"].top_k
+    t = 1
+    ws = gpu.moe_decode_workspace(L, t)
+    xs = [make_x(H, t, True, 1000 + i) for i in range(3)]
+    outs = [torch.empty((t, H), dtype=torch.bfloat16, device=DEV) for _ in xs]
+    ids = torch.empty((t, K), dtype=torch.int32, device=DEV)
+    wts = torch.empty((t, K), dtype=torch.float32, device=DEV)
+    want = [run(gpu, lay, x, t, torch.bfloat16, chain=True)[0] for x in xs]
+    s = torch.cuda.Stream(DEV)
+    s.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(s):
+        gpu.moe_decode(L, xs[0], t, outs[0], ws, ids, wts)  # warm-up outside the capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for x, o in zip(xs, outs):
+                gpu.moe_decode(L, x, t, o, ws, ids, wts)
+    torch.cuda.current_stream(DEV).wait_stream(s)
+    for _ in range(3):
+        for o in outs:
+            o.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        for o, w in zip(outs, want):
+            assert torch.equal(o, w)
+    del g
+
+
+@pytest.mark.parametrize("name,xbf16,t", [("small", False, 3), ("odd", True, 7), ("wide", True, 2)])
+def test_one_launch_meets_the_float64_bound(gpu, name, xbf16, t):
+    lay = get_layer(gpu, name)
+    L = lay["L"]
+    H, E, K = L.hidden, L.experts, L.top_k
+    x = make_x(H, t, xbf16, 1200 + t)
+    out, ids, wts = run(gpu, lay, x, t, torch.float32, chain=False)
+    torch.cuda.synchronize()
+    x32 = x.float().cpu().numpy()
+    want_ids, want_w = O.router_topk(O.router_logits(x32, lay["router"].reshape(E, H)), K)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert np.array_equal(wts.cpu().numpy().view(np.uint32), want_w.view(np.uint32))
+    active, off, tok, slot = O.group_assignments(want_ids, E)
+    host = lay["bank"].host_records()
+    y = O.moe_experts_f64([host[e] for e in active], L.geo, off, tok, x32)
+    truth = O.combine_slots_f64(y, slot, want_w, t, H, K)
+    got = out.cpu().numpy()
+    assert np.abs(got - truth).max() / np.abs(truth).max() <= 1e-4
