@@ -135,6 +135,7 @@ int stream_launch_tp(const DeviceState* d, int groups, StreamParams sp, cudaStre
     sp.gpe = (sp.nrows + pl.rpp - 1) / pl.rpp;
     const int64_t units = static_cast<int64_t>(groups) * sp.gpe;
     const int grid = units < d->sms ? static_cast<int>(units > 0 ? units : 1) : d->sms;
+    if (units * (grid + 1) >= (int64_t{1} << 32)) return OOMB_E_SHAPE;  // the kernel splits units in 32 bits
     if (sp.layout == OOMB_SCALE_128X128)
         return launch(stream_kernel<PARTS, TB, P, XB, MOE, EARLY, true>, dim3(grid), dim3(kThreads), pl.smem, s, sp);
     return launch(stream_kernel<PARTS, TB, P, XB, MOE, EARLY, false>, dim3(grid), dim3(kThreads), pl.smem, s, sp);
@@ -358,7 +359,8 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     const StreamPlan pg = stream_plan(H, 2, f.p, layout), pd = stream_plan(I, 1, f.p, layout);
     if (pg.stage_bytes > kStageBytes || pd.stage_bytes > kStageBytes) return false;
     const int gpe_g = (I + pg.rpp - 1) / pg.rpp, gpe_d = (H + pd.rpp - 1) / pd.rpp;
-    if (gpe_d > kDecodeMaxGroups) return false;
+    if (gpe_d > kDecodeMaxGroups || static_cast<int64_t>(E) * (gpe_g > gpe_d ? gpe_g : gpe_d) * 1025 >= (int64_t{1} << 32))
+        return false;
     const int slot = pg.slot_bytes > pd.slot_bytes ? pg.slot_bytes : pd.slot_bytes;
     const int ms_g = f.p * 4 + f.p * 2 * pg.sr * pg.nb, ms_d = f.p * 4 + f.p * pd.sr * pd.nb;
     const int meta_stride = ms_g > ms_d ? ms_g : ms_d;
@@ -378,8 +380,9 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
                           : (layout ? fused_resident<false, true>(f.tb, f.smem) : fused_resident<false, false>(f.tb, f.smem));
     if (occ < 1) return false;
     f.grid = d->sms * (occ < OOMB_STREAM_CTAS_PER_SM ? occ : OOMB_STREAM_CTAS_PER_SM);
-    const int rows_per_cta = (E + f.grid - 1) / f.grid;
-    if (rows_per_cta > kWarps || ring < decode_ring_borrow(t, H, E, K, rows_per_cta, 0)) return false;
+    // router rows: kWarps per CTA (one per consumer warp) on the first ceil(E / kWarps) CTAs
+    const int rows_per_cta = E < kWarps ? E : kWarps;
+    if ((E + kWarps - 1) / kWarps > f.grid || ring < decode_ring_borrow(t, H, E, K, rows_per_cta, 0)) return false;
     // the activations are staged in the ring after the router rows when they fit
     const size_t x_bytes = static_cast<size_t>(t) * H * (xbf16 ? 2 : 4);
     const bool x_staged = ring >= decode_ring_borrow(t, H, E, K, rows_per_cta, x_bytes);

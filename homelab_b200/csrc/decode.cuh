@@ -10,10 +10,11 @@
 // Every CTA of the grid (one or two per SM, all resident at once) runs:
 //   1. before the dependency wait: its router rows land in shared memory by
 //      bulk copy, and the layer's record table is fetched;
-//   2. CTA c computes the logits of router rows c, c + grid, ... for every
-//      token (activations staged by one bulk copy after the wait, when they
-//      fit), writes them to global memory; a grid barrier, then every CTA
-//      loads all T x E logits into shared memory;
+//   2. CTA c < ceil(E / 8) computes the logits of router rows 8c .. 8c + 7 (a
+//      warp each) for every token (activations staged by one bulk copy after
+//      the wait, when they fit; few CTAs read them, so their lines are not a
+//      hot spot), writes them to global memory; a grid barrier, then every
+//      CTA loads all T x E logits into shared memory;
 //   3. softmax top-k and grouping of all tokens from the logits, the same in
 //      every CTA (deterministic), into shared-memory routing tables: no
 //      second hand-off through global memory;
@@ -152,59 +153,45 @@ __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;
 // the canonical order of router_row_dot (per lane one fmaf chain over columns
 // 256*i + 8*lane + j, i ascending, then the xor tree).  Activations from
 // global memory, or staged in shared memory (XSM, rows of p.H).  The logits go
-// to p.logits.
+// to p.logits.  Written as short loops (one token at a time): this code runs
+// once per launch, so its instruction fetch costs more than its arithmetic.
 template <bool XBF16, bool XSM>
 __device__ __forceinline__ void logits_row(const RouteParams& p, const uint8_t* wrow, const uint8_t* xsm, int e, int t0,
                                            int nt, int lane) {
-    float acc[kRouteTT];
-#pragma unroll
-    for (int j = 0; j < kRouteTT; j++) acc[j] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kRouteMaxH / 256; i++) {
-        const int base = i * 256 + lane * 8;
-        if (base < p.H) {
+#pragma unroll 1
+    for (int t = t0; t < t0 + nt; t++) {
+        float acc = 0.0f;
+#pragma unroll 2
+        for (int base = lane * 8; base < p.H; base += 256) {
             const uint4 wv = *reinterpret_cast<const uint4*>(wrow + static_cast<size_t>(base) * 2);
             const unsigned ww[4] = {wv.x, wv.y, wv.z, wv.w};
-            float wf[8];
+            const int64_t xi = static_cast<int64_t>(t) * p.H + base;
+            float xv[8];
+            if (XBF16) {
+                const uint4* xp = XSM ? reinterpret_cast<const uint4*>(xsm + xi * 2)
+                                      : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi);
+                const uint4 a = XSM ? *xp : __ldcg(xp);
+                const unsigned aa[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    xv[2 * q] = __uint_as_float(aa[q] << 16);
+                    xv[2 * q + 1] = __uint_as_float(aa[q] & 0xffff0000u);
+                }
+            } else {
+                const float4* xp = XSM ? reinterpret_cast<const float4*>(xsm + xi * 4)
+                                       : reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi);
+                const float4 a = XSM ? xp[0] : __ldcg(xp), b = XSM ? xp[1] : __ldcg(xp + 1);
+                xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+                xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+            }
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-                wf[2 * q] = __uint_as_float(ww[q] << 16);
-                wf[2 * q + 1] = __uint_as_float(ww[q] & 0xffff0000u);
-            }
-#pragma unroll
-            for (int j = 0; j < kRouteTT; j++) {
-                if (j < nt) {
-                    float xv[8];
-                    const int64_t xi = static_cast<int64_t>(t0 + j) * p.H + base;
-                    if (XBF16) {
-                        const uint4* xp = XSM ? reinterpret_cast<const uint4*>(xsm + xi * 2)
-                                              : reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xi);
-                        const uint4 a = XSM ? *xp : __ldcg(xp);
-                        const unsigned aa[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            xv[2 * q] = __uint_as_float(aa[q] << 16);
-                            xv[2 * q + 1] = __uint_as_float(aa[q] & 0xffff0000u);
-                        }
-                    } else {
-                        const float4* xp = XSM ? reinterpret_cast<const float4*>(xsm + xi * 4)
-                                               : reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + xi);
-                        const float4 a = XSM ? xp[0] : __ldcg(xp), b = XSM ? xp[1] : __ldcg(xp + 1);
-                        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
-                        xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
-                    }
-#pragma unroll
-                    for (int q = 0; q < 8; q++) acc[j] = __fmaf_rn(xv[q], wf[q], acc[j]);
-                }
+                acc = __fmaf_rn(xv[2 * q], __uint_as_float(ww[q] << 16), acc);
+                acc = __fmaf_rn(xv[2 * q + 1], __uint_as_float(ww[q] & 0xffff0000u), acc);
             }
         }
-    }
-#pragma unroll
-    for (int j = 0; j < kRouteTT; j++) {
-        if (j < nt) {
-            const float v = xor_tree32(acc[j]);
-            if (lane == 0) p.logits[static_cast<int64_t>(t0 + j) * p.E + e] = v;
-        }
+        const float v = xor_tree32(acc);
+        if (lane == 0) p.logits[static_cast<int64_t>(t) * p.E + e] = v;
     }
 }
 
@@ -246,9 +233,9 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
 
     uint64_t* xbar = reinterpret_cast<uint64_t*>(tabs + dt.xbar);
     float* lg = reinterpret_cast<float*>(tabs + dt.lg);
-    // This CTA's router rows blockIdx.x + i * grid, i < nrow; row i lands at i * H * 2.
-    int nrow = 0;
-    while (nrow < kWarps && static_cast<int>(blockIdx.x + gridDim.x * nrow) < E) nrow++;
+    // This CTA's router rows: [kWarps * blockIdx.x, + nrow), row i landing at i * H * 2.
+    const int row0 = kWarps * static_cast<int>(blockIdx.x);
+    const int nrow = max(0, min(kWarps, E - row0));
     const unsigned x_bytes = static_cast<unsigned>(T * H * (XBF16 ? 2 : 4));
     const bool xsm = p.x_off >= 0;
 
@@ -262,10 +249,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         tl_mark(TL_ROUTE, TL_ENTRY);
         if (nrow > 0) {
             mbar_arrive_expect_tx(rbar, static_cast<unsigned>(nrow * H * 2));
-            for (int i = 0; i < nrow; i++)
-                bulk_g2s_plain(smem + static_cast<size_t>(i) * H * 2,
-                               p.r.w + static_cast<int64_t>(blockIdx.x + gridDim.x * i) * H,
-                               static_cast<unsigned>(H * 2), rbar);
+            bulk_g2s_plain(smem, p.r.w + static_cast<int64_t>(row0) * H, static_cast<unsigned>(nrow * H * 2), rbar);
         }
     }
     const unsigned long long rec_pre =
@@ -299,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         const bool ok = mbar_wait(rbar, 0, p.r.err, ERR_ROUTER_WAIT) &&
                         (!xsm || mbar_wait(xbar, 0, p.r.err, ERR_ROUTER_WAIT));
         if (ok) {
-            const int e = static_cast<int>(blockIdx.x + gridDim.x * warp);
+            const int e = row0 + warp;
             const uint8_t* wrow = smem + static_cast<size_t>(warp) * H * 2;
             for (int t0 = 0; t0 < T; t0 += kRouteTT) {
                 if (xsm) logits_row<XBF16, true>(p.r, wrow, smem + p.x_off, e, t0, min(kRouteTT, T - t0), lane);
@@ -315,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     if (threadIdx.x == 0) {
         tl_mark(TL_ROUTE, TL_LOGITS_DONE);
         if (nrow > 0 && !s_fail) bar_arrive(bars);
-        const unsigned writers = static_cast<unsigned>(min(E, static_cast<int>(gridDim.x)));
+        const unsigned writers = static_cast<unsigned>((E + kWarps - 1) / kWarps);
         if (!s_fail && !bar_wait(bars, writers, p.r.err, ERR_GRID_WAIT)) s_fail = 1;
         tl_mark(TL_ROUTE, TL_LAST_CTA);
     }
@@ -326,7 +310,8 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
 
     // ---- 3. top-k and grouping of every token, in every CTA ----
     {
-        topk_warps<kThreads, true>(p.r, lg, 0, T, ids_sm, w_sm);
+        if (E <= 128) topk_warps<kThreads, true, 4>(p.r, lg, 0, T, ids_sm, w_sm);
+        else topk_warps<kThreads, true, kRouteSmallE / 32>(p.r, lg, 0, T, ids_sm, w_sm);
         __syncthreads();
         if (blockIdx.x == 0) {
             for (int o = threadIdx.x; o < A; o += kThreads) {

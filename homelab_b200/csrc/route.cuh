@@ -408,11 +408,11 @@ __device__ void topk_block(const RouteParams& p, const float* logits, int t0, in
 // weights are p / (sum of the picks in pick order).  logits: [T, E] in global
 // memory, or in this CTA's shared memory (LSM).  For a few tokens per warp this
 // is far shorter than the block-wide ranking.
-template <int NT, bool LSM>
+// NJ: probabilities per lane (E <= 32 NJ).
+template <int NT, bool LSM, int NJ>
 __device__ void topk_warps(const RouteParams& p, const float* logits, int t0, int t1, int32_t* ids_out, float* w_out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int nwarps = NT / 32;
-    constexpr int NJ = kRouteSmallE / 32;
     const int E = p.E, K = p.K;
     const float NEG_INF = -__int_as_float(0x7f800000);
     for (int t = t0 + warp; t < t1; t += nwarps) {
@@ -603,7 +603,7 @@ __device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_
         else record_error(p.err, ERR_BAD_TABLE);
     }
     int lt = 0, before = 0;
-#pragma unroll 8
+#pragma unroll 4
     for (int q = 0; q < 32; q++) {
         const int kq = __shfl_sync(0xffffffffu, key, q);
         lt += kq < key ? 1 : 0;
@@ -613,7 +613,7 @@ __device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_
     const unsigned lead = __ballot_sync(0xffffffffu, leader);
     const unsigned vmask = __ballot_sync(0xffffffffu, valid);
     int idx = 0;
-#pragma unroll 8
+#pragma unroll 4
     for (int q = 0; q < 32; q++) {
         const int kq = __shfl_sync(0xffffffffu, key, q);
         idx += (((lead >> q) & 1u) && kq < key) ? 1 : 0;

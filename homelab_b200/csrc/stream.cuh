@@ -265,11 +265,12 @@ __device__ __forceinline__ Tables global_tables(const StreamParams& p, bool moe)
     return tb;
 }
 
-// The CTA's slice [u0, u1) of the flat list of n_e * gpe units.
+// The CTA's slice [u0, u1) of the flat list of n_e * gpe units (32-bit
+// arithmetic: units * (grid + 1) < 2^32 for every launch the host plans).
 __device__ __forceinline__ void cta_units(int n_e, int gpe, int& u0, int& u1) {
-    const int units = n_e * gpe;
-    u0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * units) / gridDim.x);
-    u1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * units) / gridDim.x);
+    const unsigned units = static_cast<unsigned>(n_e * gpe);
+    u0 = static_cast<int>((blockIdx.x * units) / gridDim.x);
+    u1 = static_cast<int>(((blockIdx.x + 1) * units) / gridDim.x);
 }
 
 // Stage row (part-major) of the warp's slot j: for PARTS == 2 the first half

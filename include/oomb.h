@@ -191,8 +191,11 @@ int oomb_moe_combine(const float* routed, const float* shared, const float* gate
  *   x: [t, hidden] (x_dtype); out: [t, hidden] (out_dtype);
  *   ids, weights: optional [t, top_k] copies of the routing (NULL to skip).
  * The workspace must hold oomb_moe_decode_workspace_bytes(t, layer) bytes and
- * be zeroed once before first use (oomb_workspace_clear); calls that share a
- * workspace must be ordered on one stream. */
+ * be zeroed once before first use (oomb_workspace_clear), and again after a
+ * device error (oomb_device_error); calls that share a workspace must be
+ * ordered on one stream.  Up to 16 tokens and 256 experts the step is one
+ * persistent launch; setting the environment variable OOMB_DECODE_CHAIN=1
+ * selects the chain of separate kernels instead (same results). */
 size_t oomb_moe_decode_workspace_bytes(int t, const oomb_moe_layer* layer);
 int oomb_moe_decode_fp8(const oomb_moe_layer* layer, const void* x, int x_dtype, int t, void* out,
                         int out_dtype, int32_t* ids, float* weights, void* workspace,
