@@ -604,7 +604,7 @@ __device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_
     }
     int lt = 0, before = 0;
 #pragma unroll 4
-    for (int q = 0; q < 32; q++) {
+    for (int q = 0; q < A; q++) {
         const int kq = __shfl_sync(0xffffffffu, key, q);
         lt += kq < key ? 1 : 0;
         before += (kq == key && q < lane) ? 1 : 0;
@@ -614,7 +614,7 @@ __device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_
     const unsigned vmask = __ballot_sync(0xffffffffu, valid);
     int idx = 0;
 #pragma unroll 4
-    for (int q = 0; q < 32; q++) {
+    for (int q = 0; q < A; q++) {
         const int kq = __shfl_sync(0xffffffffu, key, q);
         idx += (((lead >> q) & 1u) && kq < key) ? 1 : 0;
     }

@@ -580,8 +580,30 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
                         for (int j = 0; j < kRows; j++)
                             sc[j] = st[(PARTS == 2 ? j / (kRows / 2) : 0) * pair_floats + rin[j] * nb_k];
                     }
-                    // activations of a MoE unit depend only on its first assignment
+                    // Activation slices: gate/up the assignment's token, down the
+                    // assignment's h row, dense the token.  They are reloaded only when
+                    // their key changes: (K stage, first assignment of the chunk), or
+                    // with one token slot in gate/up the token itself, which every
+                    // expert of that token shares.
                     const int key0 = MOE ? 0 : ks;
+                    auto ensure_x = [&](int a0, int nb) {
+                        const int key1 = (MOE && PARTS == 2 && TB == 1) ? tab_i32<TSMEM>(tb.assign_tok + a0) : a0;
+                        if (x_key0 == key0 && x_key1 == key1) return;
+#pragma unroll
+                        for (int b = 0; b < TB; b++) {
+                            if (b < nb && col_ok) {
+                                const int64_t xr = (MOE && PARTS == 2) ? tab_i32<TSMEM>(tb.assign_tok + a0 + b) : a0 + b;
+                                xs[b].load(p.x, xr * kdim + kc0 + col);
+                            } else {
+                                xs[b].zero();
+                            }
+                        }
+                        x_key0 = key0;
+                        x_key1 = key1;
+                    };
+                    // the first chunk's activations are requested before the stage wait,
+                    // so their latency overlaps the stage's
+                    if (a_begin < a_end) ensure_x(a_begin, min(TB, a_end - a_begin));
                     const int slot = s % S;
                     if (!mbar_wait(&rg.full[slot], (s / S) & 1, p.err, ERR_FULL_WAIT)) return false;
                     if (first_stage && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_STAGE);
@@ -589,23 +611,7 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
                     const uint8_t* base = rg.stage_buf + slot * rg.slot_bytes + ccol;
                     for (int a0 = a_begin; a0 < a_end; a0 += TB) {
                         const int nb = min(TB, a_end - a0);
-                        if (x_key0 != key0 || x_key1 != a0) {
-#pragma unroll
-                            for (int b = 0; b < TB; b++) {
-                                if (b < nb && col_ok) {
-                                    int64_t xr;
-                                    // gate/up: the assignment's token; down: the
-                                    // assignment's h row; dense: the token
-                                    if (MOE && PARTS == 2) xr = tab_i32<TSMEM>(tb.assign_tok + a0 + b);
-                                    else xr = a0 + b;
-                                    xs[b].load(p.x, xr * kdim + kc0 + col);
-                                } else {
-                                    xs[b].zero();
-                                }
-                            }
-                            x_key0 = key0;
-                            x_key1 = a0;
-                        }
+                        if (a0 != a_begin) ensure_x(a0, nb);
                         if (active) {
                             float sx[kRows][TB];
 #pragma unroll
