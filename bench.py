@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=8,
                     help="layer replicas rotated through (8 x 604 MB keeps every step out of L2)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
+                    help="expert-parallel all-to-alls: kernels storing into peer mailboxes over NVLink, or NCCL")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU work of the cpu_baseline / reference sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
@@ -254,10 +256,15 @@ def run_ours(args, rank, world, local_rank):
             gpu.moe_decode(layers[i % LAYERS][2], xs[i % NX] if x is None else x, B, out if o is None else o, ws)
     else:
         # expert parallelism: route locally, all-to-all dispatch, local experts, all-to-all return, combine
-        from homelab_b200.ep import EpGpuOps, EpMoeLayer
+        from homelab_b200.ep import EpGpuOps, EpMoeLayer, EpPeerMailboxes, EpPeerMoeLayer
         ops = EpGpuOps(dev)
-        ep_layers = [EpMoeLayer(ops, dist.group.WORLD, H, E, K_TOP, I, router, bank.addrs, bank.geo, B)
-                     for (bank, router, _) in layers]
+        if args.ep_transport == "peer":
+            mailboxes = EpPeerMailboxes(dist.group.WORLD, H, K_TOP, B, torch.bfloat16, dev)
+            ep_layers = [EpPeerMoeLayer(ops, mailboxes, rank, H, E, K_TOP, I, router, bank.addrs, bank.geo, B)
+                         for (bank, router, _) in layers]
+        else:
+            ep_layers = [EpMoeLayer(ops, dist.group.WORLD, H, E, K_TOP, I, router, bank.addrs, bank.geo, B)
+                         for (bank, router, _) in layers]
 
         def step(i, x=None, o=None):
             ep_layers[i % LAYERS].forward(xs[i % NX] if x is None else x, B, out if o is None else o)
@@ -408,7 +415,9 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": dict(config_dict(B, LAYERS), parallelism=f"ep{world}" if world > 1 else "single",
-                           **({"expert_parallel": f"{E // world} experts per GPU, NCCL all-to-all dispatch and combine",
+                           **({"expert_parallel": f"{E // world} experts per GPU, " + (
+                               "dispatch and return stored by the kernels into peer mailboxes over NVLink (CUDA IPC)"
+                               if args.ep_transport == "peer" else "NCCL all-to-all dispatch and combine"),
                                "step_capture": "cuda graph" if graphs_ok else "eager"} if world > 1 else {})),
             "roofline": roofline_line(fused, step_bytes, ms / K, roof, peak, peak_kind, traffic),
             "gate_up_kernel": {"kernel": "stream_kernel<2> (gate/up+SiLU over the 8 experts of a step, "
@@ -424,8 +433,10 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
             # per step: one decode_kernel (the chain route, gate/up, down, combine when
-            # OOMB_DECODE_CHAIN=1 or B > 16); expert-parallel: router logits, top-k, meta,
-            # group, gate/up, down, scatter, combine (NCCL's own kernels not counted)
+            # OOMB_DECODE_CHAIN=1 or B > 16); expert-parallel over peer memory: router
+            # logits, top-k, dispatch, group, gate/up, down, return, combine; over NCCL:
+            # logits, top-k, meta, group, gate/up, down, scatter, combine (NCCL's own
+            # kernels not counted)
             "gpu_launches": (1 if fused else (4 if world == 1 else 8)) * K,
             "clocks": clocks,
         }

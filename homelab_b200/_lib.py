@@ -53,6 +53,18 @@ class MoeLayer(C.Structure):
     ]
 
 
+class EpPeer(C.Structure):
+    """oomb_ep_peer: a rank's view of the expert-parallel mailboxes."""
+
+    _fields_ = [
+        ("peers", C.c_void_p), ("mailbox", C.c_void_p),
+        ("ranks", C.c_int32), ("rank", C.c_int32), ("t_max", C.c_int32),
+        ("top_k", C.c_int32), ("hidden", C.c_int32), ("x_dtype", C.c_int32),
+    ]
+
+
+IPC_HANDLE_BYTES = 64
+
 # (name, restype, argtypes) of every entry point in include/oomb.h
 P, I, Z, S = C.c_void_p, C.c_int, C.c_size_t, C.c_void_p
 SIGNATURES = [
@@ -69,6 +81,17 @@ SIGNATURES = [
     ("oomb_ep_group", I, [P, I, I, I, I, P, P, P, P, P, P, S]),
     ("oomb_ep_scatter", I, [P, P, P, P, I, I, P, S]),
     ("oomb_ep_combine", I, [P, P, P, I, I, I, I, I, P, I, S]),
+    ("oomb_ep_mailbox_bytes", Z, [I, I, I, I, I]),
+    ("oomb_ep_mailbox_x_offset", Z, [I, I, I, I, I]),
+    ("oomb_ep_mailbox_alloc", I, [Z, C.POINTER(C.c_void_p)]),
+    ("oomb_ep_mailbox_free", I, [P]),
+    ("oomb_ipc_handle", I, [P, P]),
+    ("oomb_ipc_open", I, [P, C.POINTER(C.c_void_p)]),
+    ("oomb_ipc_close", I, [P]),
+    ("oomb_ep_dispatch_peer", I, [C.POINTER(EpPeer), P, I, I, P, S]),
+    ("oomb_ep_group_peer", I, [C.POINTER(EpPeer), I, I, P, P, P, P, P, P, S]),
+    ("oomb_ep_return_peer", I, [C.POINTER(EpPeer), P, P, P, P, I, I, S]),
+    ("oomb_ep_combine_peer", I, [C.POINTER(EpPeer), P, P, I, I, P, I, S]),
     ("oomb_copy_queue_create", I, [C.POINTER(C.c_void_p)]),
     ("oomb_copy_queue_destroy", I, [P]),
     ("oomb_pin_host", I, [P, Z]),

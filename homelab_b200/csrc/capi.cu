@@ -934,6 +934,141 @@ int oomb_ep_combine(const float* back, const int32_t* ids, const float* w, int t
                         ranks, out);
 }
 
+// ---- expert parallelism through peer memory ------------------------------------
+
+namespace {
+int ep_xb(int x_dtype) { return x_dtype == OOMB_BF16 ? 2 : (x_dtype == OOMB_F32 ? 4 : 0); }
+
+bool ep_peer_of(const oomb_ep_peer* q, EpPeer& p) {
+    if (!q || !q->peers || !q->mailbox || q->ranks <= 0 || q->rank < 0 || q->rank >= q->ranks || q->t_max <= 0 ||
+        q->top_k <= 0 || q->hidden <= 0 || q->hidden % 16 || ep_xb(q->x_dtype) == 0 || !aligned16(q->mailbox))
+        return false;
+    p.peers = reinterpret_cast<const unsigned long long*>(q->peers);
+    p.mailbox = static_cast<uint8_t*>(q->mailbox);
+    p.ranks = q->ranks;
+    p.rank = q->rank;
+    p.t_max = q->t_max;
+    p.k = q->top_k;
+    p.h = q->hidden;
+    p.xb = ep_xb(q->x_dtype);
+    p.err = nullptr;
+    return true;
+}
+}  // namespace
+
+size_t oomb_ep_mailbox_bytes(int ranks, int t_max, int top_k, int hidden, int x_dtype) {
+    if (ranks <= 0 || t_max <= 0 || top_k <= 0 || hidden <= 0 || ep_xb(x_dtype) == 0) return 0;
+    return ep_mailbox(ranks, t_max, top_k, hidden, ep_xb(x_dtype)).total;
+}
+
+size_t oomb_ep_mailbox_x_offset(int ranks, int t_max, int top_k, int hidden, int x_dtype) {
+    if (ranks <= 0 || t_max <= 0 || top_k <= 0 || hidden <= 0 || ep_xb(x_dtype) == 0) return 0;
+    return ep_mailbox(ranks, t_max, top_k, hidden, ep_xb(x_dtype)).x;
+}
+
+int oomb_ep_mailbox_alloc(size_t bytes, void** mailbox) {
+    if (!mailbox || bytes == 0) return OOMB_E_ARG;
+    *mailbox = nullptr;
+    if (cudaMalloc(mailbox, bytes) != cudaSuccess) return OOMB_E_DEVICE;
+    if (cudaMemset(*mailbox, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(*mailbox);
+        *mailbox = nullptr;
+        return OOMB_E_DEVICE;
+    }
+    return OOMB_OK;
+}
+
+int oomb_ep_mailbox_free(void* mailbox) {
+    if (!mailbox) return OOMB_E_ARG;
+    return cudaFree(mailbox) == cudaSuccess ? OOMB_OK : OOMB_E_DEVICE;
+}
+
+int oomb_ipc_handle(const void* dev_ptr, void* handle) {
+    if (!dev_ptr || !handle) return OOMB_E_ARG;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)) != cudaSuccess) return OOMB_E_DEVICE;
+    static_assert(sizeof(h) <= OOMB_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    return OOMB_OK;
+}
+
+int oomb_ipc_open(const void* handle, void** dev_ptr) {
+    if (!handle || !dev_ptr) return OOMB_E_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *dev_ptr = nullptr;
+    return cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? OOMB_OK : OOMB_E_DEVICE;
+}
+
+int oomb_ipc_close(void* dev_ptr) {
+    if (!dev_ptr) return OOMB_E_ARG;
+    return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? OOMB_OK : OOMB_E_DEVICE;
+}
+
+int oomb_ep_dispatch_peer(const oomb_ep_peer* q, const int32_t* ids, int t, int experts_per_rank, const void* x,
+                          oomb_stream stream) {
+    EpPeer p;
+    if (!ep_peer_of(q, p) || !ids || !x || experts_per_rank <= 0) return OOMB_E_ARG;
+    if (t <= 0 || t > q->t_max) return OOMB_E_SHAPE;
+    if (!aligned16(x)) return OOMB_E_ALIGN;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    p.err = d->err;
+    return launch(ep_dispatch_kernel, dim3(q->ranks), dim3(kEpThreads), 0, stream, p, ids, t, experts_per_rank, x);
+}
+
+int oomb_ep_group_peer(const oomb_ep_peer* q, int t, int experts_per_rank, const uint64_t* recs_local,
+                       int32_t* n_active, int32_t* off, int32_t* assign_row, int32_t* assign_ret,
+                       uint64_t* recs_active, oomb_stream stream) {
+    EpPeer p;
+    if (!ep_peer_of(q, p) || !recs_local || !n_active || !off || !assign_row || !assign_ret || !recs_active ||
+        experts_per_rank <= 0)
+        return OOMB_E_ARG;
+    if (t <= 0 || t > q->t_max) return OOMB_E_SHAPE;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    p.err = d->err;
+    const size_t smem = 2 * static_cast<size_t>(experts_per_rank) * sizeof(int32_t);
+    if (smem > 200 * 1024) return OOMB_E_SHAPE;
+    return launch(ep_group_peer_kernel, dim3(1), dim3(kEpThreads), smem, stream, p, t, experts_per_rank, recs_local,
+                  n_active, off, assign_row, assign_ret, recs_active);
+}
+
+int oomb_ep_return_peer(const oomb_ep_peer* q, const float* y, const int32_t* n_active, const int32_t* off,
+                        const int32_t* assign_ret, int t, int max_rows, oomb_stream stream) {
+    EpPeer p;
+    if (!ep_peer_of(q, p) || !y || !n_active || !off || !assign_ret) return OOMB_E_ARG;
+    if (t <= 0 || t > q->t_max || max_rows <= 0) return OOMB_E_SHAPE;
+    if (!aligned16(y)) return OOMB_E_ALIGN;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    p.err = d->err;
+    const int64_t quads = static_cast<int64_t>(max_rows) * (q->hidden / 4);
+    int grid = static_cast<int>((quads + 255) / 256);
+    if (grid > 2 * d->sms) grid = 2 * d->sms;
+    return launch(ep_return_kernel, dim3(grid > 0 ? grid : 1), dim3(256), 0, stream, p, y, n_active, off, assign_ret, t);
+}
+
+int oomb_ep_combine_peer(const oomb_ep_peer* q, const int32_t* ids, const float* w, int t, int experts_per_rank,
+                         void* out, int out_dtype, oomb_stream stream) {
+    EpPeer p;
+    if (!ep_peer_of(q, p) || !ids || !w || !out || experts_per_rank <= 0) return OOMB_E_ARG;
+    if (out_dtype != OOMB_F32 && out_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (t <= 0 || t > q->t_max) return OOMB_E_SHAPE;
+    if (!aligned16(out)) return OOMB_E_ALIGN;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    p.err = d->err;
+    const int64_t quads = static_cast<int64_t>(t) * q->hidden / 4;
+    int grid = static_cast<int>((quads + 255) / 256);
+    if (grid > 2 * d->sms) grid = 2 * d->sms;
+    return out_dtype == OOMB_BF16
+               ? launch(ep_combine_peer_kernel<true>, dim3(grid), dim3(256), 0, stream, p, ids, w, t, experts_per_rank,
+                        out)
+               : launch(ep_combine_peer_kernel<false>, dim3(grid), dim3(256), 0, stream, p, ids, w, t,
+                        experts_per_rank, out);
+}
+
 // ---- offload staging (Transfer, crates/oominf-core/src/backend.rs:945-1018) --------
 
 int oomb_copy_queue_create(oomb_copy_queue* queue) {

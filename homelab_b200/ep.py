@@ -175,3 +175,160 @@ def exchange_local(sends, recvs):
     for g in range(G):
         for src in range(G):
             recvs[g][src].copy_(sends[src][g])
+
+
+# ---- the exchanges through peer memory ---------------------------------------------------
+
+class _DeviceBytes:
+    """A raw device allocation seen through __cuda_array_interface__ (no ownership)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+def _bytes_view(ptr: int, nbytes: int, device) -> torch.Tensor:
+    return torch.as_tensor(_DeviceBytes(ptr, nbytes), device=device)
+
+
+class EpPeerMailboxes:
+    """The mailboxes of the peer-memory exchange (oomb_ep_peer).  With a process
+    group: this process's mailbox (cudaMalloc'd by the library) mapped into every
+    peer through CUDA IPC, the handles exchanged over the group.  With `ranks`
+    given: virtual ranks in this process, one mailbox each (tests)."""
+
+    def __init__(self, group, hidden, top_k, t_max, x_dtype, device, ranks=None):
+        self.L = L = _lib.lib()
+        self.device = torch.device(device)
+        self.virtual = ranks is not None
+        self.G = ranks if self.virtual else dist.get_world_size(group)
+        self.rank = None if self.virtual else dist.get_rank(group)
+        self.hidden, self.top_k, self.t_max = hidden, top_k, t_max
+        self.x_dtype = x_dtype
+        self.xd = BF16 if x_dtype == torch.bfloat16 else F32
+        self.nbytes = int(L.oomb_ep_mailbox_bytes(self.G, t_max, top_k, hidden, self.xd))
+        if self.nbytes == 0:
+            raise ValueError("unsupported mailbox shape")
+        self.x_off = int(L.oomb_ep_mailbox_x_offset(self.G, t_max, top_k, hidden, self.xd))
+        self.owned, self.opened = [], []
+        with torch.cuda.device(self.device):
+            if self.virtual:
+                bases = [self._alloc() for _ in range(self.G)]
+            else:
+                own = self._alloc()
+                h = (C.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+                check(L.oomb_ipc_handle(own, h), "ipc_handle")
+                handles = [None] * self.G
+                dist.all_gather_object(handles, bytes(h), group=group)
+                bases = []
+                for g, hb in enumerate(handles):
+                    if g == self.rank:
+                        bases.append(own)
+                        continue
+                    buf = (C.c_ubyte * _lib.IPC_HANDLE_BYTES).from_buffer_copy(hb)
+                    p = C.c_void_p()
+                    check(L.oomb_ipc_open(buf, C.byref(p)), "ipc_open")
+                    self.opened.append(p.value)
+                    bases.append(p.value)
+        self.bases = bases
+        self.peers = torch.tensor(bases, dtype=torch.int64, device=self.device)
+
+    def _alloc(self) -> int:
+        p = C.c_void_p()
+        check(self.L.oomb_ep_mailbox_alloc(self.nbytes, C.byref(p)), "mailbox_alloc")
+        self.owned.append(p.value)
+        return p.value
+
+    def view(self, rank: int) -> _lib.EpPeer:
+        """The oomb_ep_peer of `rank` (this process's rank for a real group)."""
+        return _lib.EpPeer(self.peers.data_ptr(), self.bases[rank], self.G, rank, self.t_max, self.top_k,
+                           self.hidden, self.xd)
+
+    def recv_x(self, rank: int, t: int) -> torch.Tensor:
+        """The received activations [G * t, hidden] in `rank`'s mailbox."""
+        xb = 2 if self.x_dtype == torch.bfloat16 else 4
+        raw = _bytes_view(self.bases[rank] + self.x_off, self.G * t * self.hidden * xb, self.device)
+        return raw.view(self.x_dtype).view(self.G * t, self.hidden)
+
+    def close(self):
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            for p in self.opened:
+                self.L.oomb_ipc_close(p)
+            for p in self.owned:
+                self.L.oomb_ep_mailbox_free(p)
+        self.opened, self.owned = [], []
+
+
+class EpPeerMoeLayer:
+    """EpMoeLayer with its three all-to-alls done by the kernels over peer memory
+    (oomb_ep_dispatch_peer / _group_peer / _return_peer / _combine_peer): no
+    collective library on the data path, and the whole step stream-ordered on
+    the device, so it captures into a CUDA graph.  Buffers as EpMoeLayer's."""
+
+    def __init__(self, ops, mailboxes: EpPeerMailboxes, rank, hidden, experts, top_k, inter, router_w, recs_local,
+                 geo, t_max):
+        self.ops, self.mb = ops, mailboxes
+        self.L = _lib.lib()
+        self.G, self.rank = mailboxes.G, rank
+        if experts % self.G:
+            raise ValueError("experts must divide evenly over the ranks")
+        if t_max > mailboxes.t_max:
+            raise ValueError("more tokens than the mailboxes hold")
+        self.H, self.E, self.K, self.I = hidden, experts, top_k, inter
+        self.epr = experts // self.G
+        self.router_w, self.recs_local, self.geo = router_w, recs_local, geo
+        self.t_max = t_max
+        self.q = mailboxes.view(rank)
+        dev = router_w.device
+        G, T, K = self.G, t_max, top_k
+        i32 = dict(dtype=torch.int32, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.logits = torch.empty((T, experts), **f32)
+        self.ids = torch.empty((T, K), **i32)
+        self.weights = torch.empty((T, K), **f32)
+        A = G * T * K
+        self.n_active = torch.zeros(1, **i32)
+        self.off = torch.zeros(self.epr + 1, **i32)
+        self.assign_row = torch.zeros(A, **i32)
+        self.assign_ret = torch.zeros(A, **i32)
+        self.recs_active = torch.zeros(self.epr, dtype=torch.int64, device=dev)
+        self.h = torch.empty((A, inter), **f32)
+        self.y = torch.empty((A, hidden), **f32)
+
+    def _s(self):
+        return torch.cuda.current_stream(self.router_w.device).cuda_stream
+
+    def phase_route(self, x, t: int):
+        """Route this rank's t tokens and dispatch them to every rank's mailbox."""
+        if t > self.t_max:
+            raise ValueError("more tokens than the layer's buffers hold")
+        self.ops.route(x, self.router_w, self.logits, self.ids, self.weights, t, self.E, self.K, self.H)
+        check(self.L.oomb_ep_dispatch_peer(C.byref(self.q), self.ids.data_ptr(), t, self.epr, x.data_ptr(), self._s()),
+              "ep_dispatch_peer")
+
+    def phase_experts(self, t: int):
+        """Group what every rank dispatched here, run the local experts, return the rows."""
+        check(self.L.oomb_ep_group_peer(C.byref(self.q), t, self.epr, self.recs_local.data_ptr(),
+                                        self.n_active.data_ptr(), self.off.data_ptr(), self.assign_row.data_ptr(),
+                                        self.assign_ret.data_ptr(), self.recs_active.data_ptr(), self._s()),
+              "ep_group_peer")
+        G, K = self.G, self.K
+        max_active = min(self.epr, G * t * K)
+        self.ops.experts(self.recs_active, self.off, self.assign_row, self.n_active, max_active,
+                         self.mb.recv_x(self.rank, t), self.h, self.y, self.geo, G * t)
+        check(self.L.oomb_ep_return_peer(C.byref(self.q), self.y.data_ptr(), self.n_active.data_ptr(),
+                                         self.off.data_ptr(), self.assign_ret.data_ptr(), t, G * t * K, self._s()),
+              "ep_return_peer")
+
+    def phase_combine(self, t: int, out):
+        od = BF16 if out.dtype == torch.bfloat16 else F32
+        check(self.L.oomb_ep_combine_peer(C.byref(self.q), self.ids.data_ptr(), self.weights.data_ptr(), t, self.epr,
+                                          out.data_ptr(), od, self._s()), "ep_combine_peer")
+        return self.ids[:t], self.weights[:t]
+
+    def forward(self, x, t: int, out):
+        """out[t, hidden] = the routed experts' combined output for this rank's t tokens."""
+        self.phase_route(x, t)
+        self.phase_experts(t)
+        return self.phase_combine(t, out)

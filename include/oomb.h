@@ -269,6 +269,49 @@ int oomb_ep_scatter(const float* y, const int32_t* n_active, const int32_t* off,
 int oomb_ep_combine(const float* back, const int32_t* ids, const float* w, int t, int k, int h, int experts_per_rank,
                     int ranks, void* out, int out_dtype, oomb_stream stream);
 
+/* Expert parallelism with the all-to-alls done by the kernels over NVLink:
+ * every rank owns a mailbox (cudaMalloc'd by oomb_ep_mailbox_alloc, zeroed;
+ * mapped into every peer through CUDA IPC), and the dispatch and return
+ * kernels store straight into the destination rank's mailbox, then raise a
+ * per-source flag there carrying the step's epoch (the mailbox's step counter
+ * + 1); the grouping and combine kernels wait for every source's flag (bounded
+ * waits; a wait that runs out records OOMB device error 0x700 / 0x710).  A step:
+ * route; oomb_ep_dispatch_peer; oomb_ep_group_peer; oomb_moe_experts_fp8 over
+ * the mailbox's received activations; oomb_ep_return_peer; oomb_ep_combine_peer
+ * (which advances the step counter).  Every rank runs the same steps with the
+ * same t; the arithmetic is the NCCL path's, bit-identical to one GPU. */
+typedef struct oomb_ep_peer {
+    const uint64_t* peers; /* device array [ranks]: every rank's mailbox in this process (own rank: mailbox) */
+    void* mailbox;         /* this rank's mailbox */
+    int ranks, rank;
+    int t_max;             /* tokens per rank the mailbox holds */
+    int top_k, hidden;
+    int x_dtype;           /* OOMB_BF16 or OOMB_F32 activations */
+} oomb_ep_peer;
+
+#define OOMB_IPC_HANDLE_BYTES 64
+size_t oomb_ep_mailbox_bytes(int ranks, int t_max, int top_k, int hidden, int x_dtype);
+/* Byte offset of the received activations [ranks * t, hidden] in a mailbox. */
+size_t oomb_ep_mailbox_x_offset(int ranks, int t_max, int top_k, int hidden, int x_dtype);
+int oomb_ep_mailbox_alloc(size_t bytes, void** mailbox);  /* cudaMalloc + zero */
+int oomb_ep_mailbox_free(void* mailbox);
+int oomb_ipc_handle(const void* dev_ptr, void* handle);    /* cudaIpcGetMemHandle of an allocation base */
+int oomb_ipc_open(const void* handle, void** dev_ptr);     /* cudaIpcOpenMemHandle (lazy peer access) */
+int oomb_ipc_close(void* dev_ptr);
+/* ids [t, k] (experts of this rank's tokens), x [t, hidden]. */
+int oomb_ep_dispatch_peer(const oomb_ep_peer* q, const int32_t* ids, int t, int experts_per_rank, const void* x,
+                          oomb_stream stream);
+/* As oomb_ep_group over the mailbox's received meta. */
+int oomb_ep_group_peer(const oomb_ep_peer* q, int t, int experts_per_rank, const uint64_t* recs_local,
+                       int32_t* n_active, int32_t* off, int32_t* assign_row, int32_t* assign_ret,
+                       uint64_t* recs_active, oomb_stream stream);
+/* Sends y[a] to its source rank's mailbox (row (this rank, slot)); max_rows bounds A. */
+int oomb_ep_return_peer(const oomb_ep_peer* q, const float* y, const int32_t* n_active, const int32_t* off,
+                        const int32_t* assign_ret, int t, int max_rows, oomb_stream stream);
+/* As oomb_ep_combine over the mailbox's returned rows; out fp32 or bf16 [t, hidden]. */
+int oomb_ep_combine_peer(const oomb_ep_peer* q, const int32_t* ids, const float* w, int t, int experts_per_rank,
+                         void* out, int out_dtype, oomb_stream stream);
+
 /* ---- offload staging ---------------------------------------------------- */
 /* Copies that run beside compute, from pinned host memory or within the
  * device, ordered against compute with events: the Transfer trait

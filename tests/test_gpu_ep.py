@@ -98,3 +98,48 @@ def test_expert_outputs_do_not_depend_on_grouping(layer):
     assert torch.equal(big[4], alone[0])  # expert 20, token 1
     pair = run([9, 41], [[1], [2]])
     assert torch.equal(big[2], pair[0]) and torch.equal(big[6], pair[1])
+
+
+def run_virtual_peer(layer, xs, G, t):
+    """Steps of the peer-memory expert-parallel path over G virtual ranks (one
+    mailbox each, in this process); every phase runs for all ranks before the
+    next, so each wait finds its flags already raised by finished kernels."""
+    from homelab_b200.ep import EpPeerMailboxes, EpPeerMoeLayer
+    bank, router = layer["bank"], layer["router"]
+    ops = EpGpuOps(DEV)
+    epr = E // G
+    mb = EpPeerMailboxes(None, H, K, t, torch.bfloat16, DEV, ranks=G)
+    ranks = [EpPeerMoeLayer(ops, mb, g, H, E, K, I, router, bank.addrs[g * epr:(g + 1) * epr].contiguous(), bank.geo, t)
+             for g in range(G)]
+    results = []
+    for x in xs:
+        outs = [torch.full((t, H), float("nan"), dtype=torch.float32, device=DEV) for _ in range(G)]
+        for g, r in enumerate(ranks):
+            r.phase_route(x[g * t:(g + 1) * t], t)
+        for r in ranks:
+            r.phase_experts(t)
+        routing = [r.phase_combine(t, outs[g]) for g, r in enumerate(ranks)]
+        torch.cuda.synchronize()
+        results.append((outs, [(i.clone(), w.clone()) for i, w in routing]))
+    mb.close()
+    return results
+
+
+@pytest.mark.parametrize("G,t", [(2, 1), (4, 2), (8, 1)])
+def test_peer_expert_parallel_equals_single_gpu(layer, G, t):
+    """Three consecutive steps (the mailbox epochs advance) equal the single-GPU decode."""
+    gpu, L = layer["gpu"], layer["L"]
+    T = G * t
+    xs = [torch.from_numpy(O.normal_bf16(60 + 7 * G + t + i, T * H).view(np.int16)).to(DEV).view(torch.bfloat16)
+          .view(T, H) for i in range(3)]
+    ws = gpu.moe_decode_workspace(L, T)
+    results = run_virtual_peer(layer, xs, G, t)
+    for x, (outs, routing) in zip(xs, results):
+        want = torch.empty((T, H), dtype=torch.float32, device=DEV)
+        ids = torch.empty((T, K), dtype=torch.int32, device=DEV)
+        wts = torch.empty((T, K), dtype=torch.float32, device=DEV)
+        gpu.moe_decode(L, x, T, want, ws, ids, wts)
+        torch.cuda.synchronize()
+        for g in range(G):
+            assert torch.equal(routing[g][0], ids[g * t:(g + 1) * t])
+            assert torch.equal(outs[g], want[g * t:(g + 1) * t]), f"rank {g} differs from one GPU"
