@@ -256,12 +256,16 @@ def run_ours(args, rank, world, local_rank):
             gpu.moe_decode(layers[i % LAYERS][2], xs[i % NX] if x is None else x, B, out if o is None else o, ws)
     else:
         # expert parallelism: route locally, all-to-all dispatch, local experts, all-to-all return, combine
-        from homelab_b200.ep import EpGpuOps, EpMoeLayer, EpPeerMailboxes, EpPeerMoeLayer
+        from homelab_b200.ep import EpDecodeLayer, EpGpuOps, EpMoeLayer, EpPeerMailboxes, EpPeerMoeLayer
         ops = EpGpuOps(dev)
         if args.ep_transport == "peer":
             mailboxes = EpPeerMailboxes(dist.group.WORLD, H, K_TOP, B, torch.bfloat16, dev)
-            ep_layers = [EpPeerMoeLayer(ops, mailboxes, rank, H, E, K_TOP, I, router, bank.addrs, bank.geo, B)
-                         for (bank, router, _) in layers]
+            if B <= 16:  # the one-launch step per rank
+                ep_layers = [EpDecodeLayer(mailboxes, rank, H, E, K_TOP, router, bank.addrs, bank.geo, B)
+                             for (bank, router, _) in layers]
+            else:
+                ep_layers = [EpPeerMoeLayer(ops, mailboxes, rank, H, E, K_TOP, I, router, bank.addrs, bank.geo, B)
+                             for (bank, router, _) in layers]
         else:
             ep_layers = [EpMoeLayer(ops, dist.group.WORLD, H, E, K_TOP, I, router, bank.addrs, bank.geo, B)
                          for (bank, router, _) in layers]
@@ -416,7 +420,8 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": dict(config_dict(B, LAYERS), parallelism=f"ep{world}" if world > 1 else "single",
                            **({"expert_parallel": f"{E // world} experts per GPU, " + (
-                               "dispatch and return stored by the kernels into peer mailboxes over NVLink (CUDA IPC)"
+                               "one launch per rank and step: dispatch and return stored by the kernel into peer "
+                               "mailboxes over NVLink (CUDA IPC)"
                                if args.ep_transport == "peer" else "NCCL all-to-all dispatch and combine"),
                                "step_capture": "cuda graph" if graphs_ok else "eager"} if world > 1 else {})),
             "roofline": roofline_line(fused, step_bytes, ms / K, roof, peak, peak_kind, traffic),
@@ -437,7 +442,8 @@ def run_ours(args, rank, world, local_rank):
             # logits, top-k, dispatch, group, gate/up, down, return, combine; over NCCL:
             # logits, top-k, meta, group, gate/up, down, scatter, combine (NCCL's own
             # kernels not counted)
-            "gpu_launches": (1 if fused else (4 if world == 1 else 8)) * K,
+            "gpu_launches": (1 if fused or (world > 1 and args.ep_transport == "peer" and B <= 16)
+                             else (4 if world == 1 else 8)) * K,
             "clocks": clocks,
         }
     return result, roof

@@ -81,6 +81,8 @@ SIGNATURES = [
     ("oomb_ep_group", I, [P, I, I, I, I, P, P, P, P, P, P, S]),
     ("oomb_ep_scatter", I, [P, P, P, P, I, I, P, S]),
     ("oomb_ep_combine", I, [P, P, P, I, I, I, I, I, P, I, S]),
+    ("oomb_moe_decode_ep_workspace_bytes", Z, [I, I, C.POINTER(MoeLayer)]),
+    ("oomb_moe_decode_ep_fp8", I, [C.POINTER(MoeLayer), C.POINTER(EpPeer), P, I, I, P, I, P, P, P, Z, S]),
     ("oomb_ep_mailbox_bytes", Z, [I, I, I, I, I]),
     ("oomb_ep_mailbox_x_offset", Z, [I, I, I, I, I]),
     ("oomb_ep_mailbox_alloc", I, [Z, C.POINTER(C.c_void_p)]),

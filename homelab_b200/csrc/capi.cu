@@ -336,24 +336,34 @@ int resident_ctas(Kernel kernel, size_t smem) {
     return n;
 }
 
-template <bool XB, bool BLK, int TB, int P>
+template <bool XB, bool BLK, int TB, int P, bool EP>
 auto decode_kernel_ptr() {
-    return decode_kernel<XB, BLK, TB, P>;
+    return decode_kernel<XB, BLK, TB, P, EP>;
 }
 
-template <bool XB, bool BLK>
+template <bool XB, bool BLK, bool EP>
 int fused_resident(int tb, size_t smem) {
-    return tb == 1 ? resident_ctas(decode_kernel_ptr<XB, BLK, 1, pass_len<1>()>(), smem)
-                   : resident_ctas(decode_kernel_ptr<XB, BLK, 2, 1>(), smem);
+    return tb == 1 ? resident_ctas(decode_kernel_ptr<XB, BLK, 1, pass_len<1>(), EP>(), smem)
+                   : resident_ctas(decode_kernel_ptr<XB, BLK, 2, 1, EP>(), smem);
 }
 
-bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, bool xbf16, FusedDecode& f) {
+template <bool EP>
+int fused_resident_any(bool xbf16, int layout, int tb, size_t smem) {
+    return xbf16 ? (layout ? fused_resident<true, true, EP>(tb, smem) : fused_resident<true, false, EP>(tb, smem))
+                 : (layout ? fused_resident<false, true, EP>(tb, smem) : fused_resident<false, false, EP>(tb, smem));
+}
+
+// ranks > 0: the expert-parallel kernel, this rank's experts E / ranks of them.
+bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, bool xbf16, FusedDecode& f,
+                       int ranks = 0) {
     const char* env = getenv("OOMB_DECODE_CHAIN");
-    if (env && env[0] == '1') return false;
+    if (ranks == 0 && env && env[0] == '1') return false;
     const int E = L->experts, K = L->top_k, H = static_cast<int>(L->geo.hidden), I = static_cast<int>(L->geo.inter);
     const int layout = L->geo.layout;
     if (t < 1 || t > kDecodeMaxT || E > kRouteSmallE || H > kRouteMaxH) return false;
-    const TbP tp = tb_p(t);
+    const int TA = ranks > 0 ? ranks * t : t;  // tokens whose slots this rank groups
+    if (ranks > 0 && (E % ranks || E / ranks > kThreads)) return false;
+    const TbP tp = tb_p(TA);
     f.tb = tp.chunked ? 2 : tp.tb;
     f.p = f.tb == 1 ? pass_len<1>() : 1;
     const StreamPlan pg = stream_plan(H, 2, f.p, layout), pd = stream_plan(I, 1, f.p, layout);
@@ -364,7 +374,7 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     const int slot = pg.slot_bytes > pd.slot_bytes ? pg.slot_bytes : pd.slot_bytes;
     const int ms_g = f.p * 4 + f.p * 2 * pg.sr * pg.nb, ms_d = f.p * 4 + f.p * pd.sr * pd.nb;
     const int meta_stride = ms_g > ms_d ? ms_g : ms_d;
-    const DecodeTabs dt = decode_tabs(t, K, E);
+    const DecodeTabs dt = decode_tabs(t, K, E, TA);
     // [ring][bars][red][meta][chunk][tables]
     const size_t bars = (2 * kMaxStages + 2 * kMetaBufs) * sizeof(uint64_t);
     const size_t red = 2 * kWarps * kRedV * sizeof(float);
@@ -376,8 +386,8 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     if (ring + fixed > static_cast<size_t>(kSmemLimit)) return false;
     f.smem = ring + fixed;
     // every CTA must be resident at once (grid barriers)
-    const int occ = xbf16 ? (layout ? fused_resident<true, true>(f.tb, f.smem) : fused_resident<true, false>(f.tb, f.smem))
-                          : (layout ? fused_resident<false, true>(f.tb, f.smem) : fused_resident<false, false>(f.tb, f.smem));
+    const int occ = ranks > 0 ? fused_resident_any<true>(xbf16, layout, f.tb, f.smem)
+                              : fused_resident_any<false>(xbf16, layout, f.tb, f.smem);
     if (occ < 1) return false;
     f.grid = d->sms * (occ < OOMB_STREAM_CTAS_PER_SM ? occ : OOMB_STREAM_CTAS_PER_SM);
     // router rows: kWarps per CTA (one per consumer warp) on the first ceil(E / kWarps) CTAs
@@ -425,11 +435,17 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     return true;
 }
 
-template <bool XB, bool BLK>
+template <bool XB, bool BLK, bool EP>
 int fused_launch(const FusedDecode& f, cudaStream_t s) {
     if (f.tb == 1)
-        return launch(decode_kernel<XB, BLK, 1, pass_len<1>()>, dim3(f.grid), dim3(kThreads), f.smem, s, f.prm);
-    return launch(decode_kernel<XB, BLK, 2, 1>, dim3(f.grid), dim3(kThreads), f.smem, s, f.prm);
+        return launch(decode_kernel<XB, BLK, 1, pass_len<1>(), EP>, dim3(f.grid), dim3(kThreads), f.smem, s, f.prm);
+    return launch(decode_kernel<XB, BLK, 2, 1, EP>, dim3(f.grid), dim3(kThreads), f.smem, s, f.prm);
+}
+
+template <bool EP>
+int fused_launch_any(bool xbf16, int layout, const FusedDecode& f, cudaStream_t s) {
+    if (xbf16) return layout ? fused_launch<true, true, EP>(f, s) : fused_launch<true, false, EP>(f, s);
+    return layout ? fused_launch<false, true, EP>(f, s) : fused_launch<false, false, EP>(f, s);
 }
 
 }  // namespace
@@ -709,9 +725,10 @@ struct DecodeLayout {
 
 size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-DecodeLayout decode_layout(int t, const oomb_moe_layer* L) {
+// ranks > 1: the expert-parallel kernel, whose h holds the slots of every rank's tokens.
+DecodeLayout decode_layout(int t, const oomb_moe_layer* L, int ranks = 1) {
     DecodeLayout d{};
-    const size_t T = t, E = L->experts, K = L->top_k, A = T * K;
+    const size_t T = t, E = L->experts, K = L->top_k, A = T * K, AH = static_cast<size_t>(ranks) * A;
     const size_t H = L->geo.hidden, I = L->geo.inter;
     size_t o = 0;
     d.ticket = o; o += 256;
@@ -725,7 +742,7 @@ DecodeLayout decode_layout(int t, const oomb_moe_layer* L) {
     d.assign_tok = o; o = up256(o + A * 4);
     d.slot_assign = o; o = up256(o + A * 4);
     d.recs_active = o; o = up256(o + E * 8);
-    d.h = o; o = up256(o + A * I * 4);
+    d.h = o; o = up256(o + AH * I * 4);
     d.y = o; o = up256(o + A * H * 4);
     d.total = o;
     return d;
@@ -799,9 +816,7 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
         q.w_out = weights ? weights : reinterpret_cast<float*>(ws + lay.weights);
         q.out = out;
         q.out_bf16 = out_dtype == OOMB_BF16;
-        if (x_dtype == OOMB_BF16)
-            return L->geo.layout ? fused_launch<true, true>(f, stream) : fused_launch<true, false>(f, stream);
-        return L->geo.layout ? fused_launch<false, true>(f, stream) : fused_launch<false, false>(f, stream);
+        return fused_launch_any<false>(x_dtype == OOMB_BF16, L->geo.layout, f, stream);
     }
 
     // 1. router logits + top-k + grouping (one launch; the last CTA groups)
@@ -854,6 +869,82 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K)
                : launch(combine_slots_kernel<false>, cgrid, dim3(256), 0, stream, static_cast<const float*>(y),
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K);
+}
+
+namespace {
+int ep_xb(int x_dtype) { return x_dtype == OOMB_BF16 ? 2 : (x_dtype == OOMB_F32 ? 4 : 0); }
+
+bool ep_peer_of(const oomb_ep_peer* q, EpPeer& p) {
+    if (!q || !q->peers || !q->mailbox || q->ranks <= 0 || q->rank < 0 || q->rank >= q->ranks || q->t_max <= 0 ||
+        q->top_k <= 0 || q->hidden <= 0 || q->hidden % 16 || ep_xb(q->x_dtype) == 0 || !aligned16(q->mailbox))
+        return false;
+    p.peers = reinterpret_cast<const unsigned long long*>(q->peers);
+    p.mailbox = static_cast<uint8_t*>(q->mailbox);
+    p.ranks = q->ranks;
+    p.rank = q->rank;
+    p.t_max = q->t_max;
+    p.k = q->top_k;
+    p.h = q->hidden;
+    p.xb = ep_xb(q->x_dtype);
+    p.err = nullptr;
+    return true;
+}
+}  // namespace
+
+size_t oomb_moe_decode_ep_workspace_bytes(int t, int ranks, const oomb_moe_layer* layer) {
+    if (t <= 0 || ranks <= 0 || check_layer(layer) != OOMB_OK) return 0;
+    return decode_layout(t, layer, ranks).total;
+}
+
+int oomb_moe_decode_ep_fp8(const oomb_moe_layer* L, const oomb_ep_peer* q, const void* x, int x_dtype, int t,
+                           void* out, int out_dtype, int32_t* ids, float* weights, void* workspace,
+                           size_t workspace_bytes, oomb_stream stream) {
+    int rc = check_layer(L);
+    if (rc) return rc;
+    EpPeer ep;
+    if (!ep_peer_of(q, ep) || !x || !out || !workspace) return OOMB_E_ARG;
+    if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) || (out_dtype != OOMB_F32 && out_dtype != OOMB_BF16) ||
+        x_dtype != q->x_dtype)
+        return OOMB_E_ARG;
+    if (q->hidden != L->hidden || q->top_k != L->top_k || L->experts % q->ranks) return OOMB_E_SHAPE;
+    if (t <= 0 || t > q->t_max) return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(out) || !aligned16(workspace) || !aligned16(L->router_w)) return OOMB_E_ALIGN;
+    const DecodeLayout lay = decode_layout(t, L, q->ranks);
+    if (workspace_bytes < lay.total) return OOMB_E_WORKSPACE;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    ep.err = d->err;
+    FusedDecode f;
+    if (!fused_decode_plan(d, L, t, x_dtype == OOMB_BF16, f, q->ranks)) return OOMB_E_SHAPE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const EpMailbox mb = ep_mailbox(q->ranks, q->t_max, q->top_k, q->hidden, ep.xb);
+    DecodeParams& p = f.prm;
+    p.r.x = x;
+    p.r.x_bf16 = x_dtype == OOMB_BF16;
+    p.r.w = L->router_w;
+    p.r.logits = reinterpret_cast<float*>(ws + lay.logits);
+    p.r.T = t;
+    p.r.H = L->hidden;
+    p.r.E = L->experts;
+    p.r.K = L->top_k;
+    p.r.recs_all = L->recs;  // this rank's records
+    p.r.err = d->err;
+    p.gu.x = static_cast<uint8_t*>(q->mailbox) + mb.x;  // every rank's activations, as received
+    p.gu.y = ws + lay.h;
+    p.dn.x = ws + lay.h;
+    p.dn.y = nullptr;
+    p.dn.ep_peers = reinterpret_cast<const unsigned long long*>(q->peers);
+    p.dn.ep_back_off = static_cast<int64_t>(mb.back);
+    p.dn.ep_rank = q->rank;
+    p.dn.ep_tk = t * L->top_k;
+    p.sync = reinterpret_cast<unsigned*>(ws + lay.sync);
+    p.ids_out = ids ? ids : reinterpret_cast<int32_t*>(ws + lay.ids);
+    p.w_out = weights ? weights : reinterpret_cast<float*>(ws + lay.weights);
+    p.out = out;
+    p.out_bf16 = out_dtype == OOMB_BF16;
+    p.ep = ep;
+    p.epr = L->experts / q->ranks;
+    return fused_launch_any<true>(x_dtype == OOMB_BF16, L->geo.layout, f, stream);
 }
 
 // ---- expert parallelism -------------------------------------------------------
@@ -936,25 +1027,7 @@ int oomb_ep_combine(const float* back, const int32_t* ids, const float* w, int t
 
 // ---- expert parallelism through peer memory ------------------------------------
 
-namespace {
-int ep_xb(int x_dtype) { return x_dtype == OOMB_BF16 ? 2 : (x_dtype == OOMB_F32 ? 4 : 0); }
 
-bool ep_peer_of(const oomb_ep_peer* q, EpPeer& p) {
-    if (!q || !q->peers || !q->mailbox || q->ranks <= 0 || q->rank < 0 || q->rank >= q->ranks || q->t_max <= 0 ||
-        q->top_k <= 0 || q->hidden <= 0 || q->hidden % 16 || ep_xb(q->x_dtype) == 0 || !aligned16(q->mailbox))
-        return false;
-    p.peers = reinterpret_cast<const unsigned long long*>(q->peers);
-    p.mailbox = static_cast<uint8_t*>(q->mailbox);
-    p.ranks = q->ranks;
-    p.rank = q->rank;
-    p.t_max = q->t_max;
-    p.k = q->top_k;
-    p.h = q->hidden;
-    p.xb = ep_xb(q->x_dtype);
-    p.err = nullptr;
-    return true;
-}
-}  // namespace
 
 size_t oomb_ep_mailbox_bytes(int ranks, int t_max, int top_k, int hidden, int x_dtype) {
     if (ranks <= 0 || t_max <= 0 || top_k <= 0 || hidden <= 0 || ep_xb(x_dtype) == 0) return 0;

@@ -40,6 +40,7 @@
 // once.
 #pragma once
 
+#include "ep.cuh"
 #include "route.cuh"
 #include "stream.cuh"
 
@@ -47,9 +48,10 @@ namespace oomb {
 
 constexpr int kDecodeMaxT = 16;         // tokens per launch
 constexpr int kDecodeMaxGroups = 512;   // down row groups (combine counters, bitmap bits)
-// sync-area words: the launch epoch; a ring of 4 slots of the two barriers'
-// arrival counts (slot epoch % 4, counts 32 words apart); the row-group counters
-constexpr int kSyncEpoch = 0, kSyncBars = 32, kSyncGroups = kSyncBars + 4 * 2 * 32;
+// sync-area words: the launch epoch; a ring of 4 slots of the grid barriers'
+// arrival counts (slot epoch % 4, three counts 32 words apart); the row-group counters
+constexpr int kSyncSlot = 3 * 32;
+constexpr int kSyncEpoch = 0, kSyncBars = 32, kSyncGroups = kSyncBars + 4 * kSyncSlot;
 constexpr int kSyncWords = kSyncGroups + kDecodeMaxGroups;
 
 enum : unsigned {
@@ -68,23 +70,31 @@ struct DecodeParams {
     int stages, slot_bytes, meta_stride;
     int off_bars, off_red, off_meta, off_chunk, off_tabs;  // shared-memory layout (bytes)
     int x_off;  // ring offset (bytes) of the staged activations, or -1 to read them from global memory
+    // expert parallelism (EP kernels): the mailboxes, experts per rank; r.recs_all
+    // then holds this rank's epr records, gu.x the mailbox's received activations
+    EpPeer ep;
+    int epr;
 };
 
 // Routing tables in shared memory (byte offsets from the table area).
 struct DecodeTabs {
     int recs, recs_active, rbar, xbar, lg, ids, w, counts, base, active, off, assign_tok, slot_assign, n_active, cbits,
-        total;
+        rmeta, aret, total;
 };
 
-__host__ __device__ inline DecodeTabs decode_tabs(int T, int K, int E) {
+// T: this rank's tokens; TA: tokens whose slots are grouped (T, or ranks * T
+// with expert parallelism).
+__host__ __device__ inline DecodeTabs decode_tabs(int T, int K, int E, int TA) {
     DecodeTabs d{};
-    const int A = T * K;
+    const int A = TA * K;
     int o = 0;
     d.recs = o; o += E * 8;
     d.recs_active = o; o += E * 8;
     d.rbar = o; o += 8;
     d.xbar = o; o += 8;
     d.lg = o; o += T * E * 4;
+    d.rmeta = o; o += A * 4;
+    d.aret = o; o += A * 4;
     d.ids = o; o += A * 4;
     d.w = o; o += A * 4;
     d.counts = o; o += E * 4;
@@ -197,12 +207,21 @@ __device__ __forceinline__ void logits_row(const RouteParams& p, const uint8_t* 
 
 // XBF16: activations bf16 (else fp32).  BLK: 128x128 block scales.  TB, P: the
 // token slots and units per pass of both streaming phases (as the stand-alone
-// kernels would take them for at most T assignments per expert).
-template <bool XBF16, bool BLK, int TB, int P>
+// kernels would take them for at most T assignments per expert).  EP: expert
+// parallelism, this rank holding experts [rank * epr, (rank + 1) * epr):
+//   after top-k, CTA g < ranks dispatches this rank's meta and activations into
+//   rank g's mailbox and raises the flag there; every CTA waits for all
+//   sources' flags and groups the received slots (local expert ids, -1 for
+//   another rank's) in (source, token, slot) order; the streaming phases run
+//   over the local experts, down's reduction storing each output row straight
+//   into its source rank's mailbox; a grid barrier, CTA g raises the return
+//   flag on rank g, and every CTA, once all ranks' flags are up, combines its
+//   share of this rank's outputs in slot order from the mailbox.
+template <bool XBF16, bool BLK, int TB, int P, bool EP>
 __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_fail;
-    __shared__ unsigned s_epoch;
+    __shared__ unsigned s_epoch, s_ep_epoch;
     Ring rg;
     rg.stages = p.stages;
     rg.slot_bytes = p.slot_bytes;
@@ -217,7 +236,9 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     rg.chunk_hdr = reinterpret_cast<int*>(smem + p.off_chunk);
 
     const int T = p.r.T, H = p.r.H, E = p.r.E, K = p.r.K, A = T * K;
-    const DecodeTabs dt = decode_tabs(T, K, E);
+    const int G = EP ? p.ep.ranks : 1;
+    const int nrec = EP ? p.epr : E;  // entries of the record table r.recs_all
+    const DecodeTabs dt = decode_tabs(T, K, E, G * T);
     uint8_t* tabs = smem + p.off_tabs;
     uint64_t* recs_sm = reinterpret_cast<uint64_t*>(tabs + dt.recs);
     uint64_t* recs_active = reinterpret_cast<uint64_t*>(tabs + dt.recs_active);
@@ -253,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         }
     }
     const unsigned long long rec_pre =
-        static_cast<int>(threadIdx.x) < E
+        static_cast<int>(threadIdx.x) < nrec
             ? ld_prefetch_u64(reinterpret_cast<const unsigned long long*>(p.r.recs_all) + threadIdx.x)
             : 0ull;
     pdl_wait();
@@ -263,17 +284,19 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         // every launch on this workspace before this one has completed
         s_epoch = ld_relaxed_u32(p.sync + kSyncEpoch) + 1u;
         if (blockIdx.x == 0) {
-            unsigned* ahead = p.sync + kSyncBars + ((s_epoch + 2u) & 3u) * 64;
+            unsigned* ahead = p.sync + kSyncBars + ((s_epoch + 2u) & 3u) * kSyncSlot;
             ahead[0] = 0u;
             ahead[32] = 0u;
+            ahead[64] = 0u;
         }
+        if (EP) s_ep_epoch = ep_epoch(p.ep);
         if (xsm && nrow > 0) {
             // the activations may come from the previous kernel: staged after the wait
             mbar_arrive_expect_tx(xbar, x_bytes);
             bulk_g2s_plain(smem + p.x_off, p.r.x, x_bytes, xbar);
         }
     }
-    if (static_cast<int>(threadIdx.x) < E) recs_sm[threadIdx.x] = rec_pre;
+    if (static_cast<int>(threadIdx.x) < nrec) recs_sm[threadIdx.x] = rec_pre;
     if (threadIdx.x < kDecodeMaxGroups / 32) cbits[threadIdx.x] = 0u;
     __syncthreads();
     const unsigned epoch = s_epoch;
@@ -295,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     }
     __syncthreads();
     // the CTAs with router rows publish their logits; every CTA waits for all of them
-    unsigned* bars = p.sync + kSyncBars + (epoch & 3u) * 64;
+    unsigned* bars = p.sync + kSyncBars + (epoch & 3u) * kSyncSlot;
     if (threadIdx.x == 0) {
         tl_mark(TL_ROUTE, TL_LOGITS_DONE);
         if (nrow > 0 && !s_fail) bar_arrive(bars);
@@ -320,13 +343,56 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
             }
         }
         if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_TOPK_DONE);
-        const GroupOut go{n_active, reinterpret_cast<int32_t*>(tabs + dt.active), off_sm, assign_tok, slot_sm,
-                          recs_active};
-        if (A <= 32) {
-            if (warp == 0) group_warp(p.r, go, ids_sm, recs_sm);
+        if constexpr (EP) {
+            const EpMailbox mb = ep_mailbox(p.ep.ranks, p.ep.t_max, p.ep.k, p.ep.h, p.ep.xb);
+            const unsigned ep_ep = s_ep_epoch;
+            // every CTA read the mailbox epoch before the logits barrier: hand it to the next step
+            if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<unsigned*>(p.ep.mailbox + mb.counter) = ep_ep;
+            if (static_cast<int>(blockIdx.x) < G) {
+                // dispatch to rank g: meta (local expert ids on g, -1 elsewhere) and activations
+                const int g = blockIdx.x;
+                uint8_t* dst = reinterpret_cast<uint8_t*>(p.ep.peers[g]);
+                int32_t* meta = reinterpret_cast<int32_t*>(dst + mb.meta) + static_cast<size_t>(p.ep.rank) * A;
+                for (int i = threadIdx.x; i < A; i += kThreads) {
+                    const int e = ids_sm[i];
+                    meta[i] = e / p.epr == g ? e - g * p.epr : -1;
+                }
+                ep_copy16(dst + mb.x + static_cast<size_t>(p.ep.rank) * T * H * p.ep.xb,
+                          static_cast<const uint8_t*>(p.r.x), static_cast<size_t>(T) * H * p.ep.xb);
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    __threadfence_system();
+                    ep_st_relaxed_sys(reinterpret_cast<unsigned*>(dst + mb.flags_dispatch) + p.ep.rank, ep_ep);
+                }
+            }
+            // every source rank's slots for this rank's experts
+            if (!ep_wait_flags(reinterpret_cast<const unsigned*>(p.ep.mailbox + mb.flags_dispatch), G, ep_ep, p.r.err,
+                               ERR_EP_DISPATCH_WAIT))
+                return;
+            int32_t* rmeta = reinterpret_cast<int32_t*>(tabs + dt.rmeta);
+            for (int i = threadIdx.x; i < G * A; i += kThreads)
+                rmeta[i] = __ldcg(reinterpret_cast<const int32_t*>(p.ep.mailbox + mb.meta) + i);
+            __syncthreads();
+            RouteParams rq = p.r;
+            rq.T = G * T;
+            rq.E = p.epr;
+            const GroupOut go{n_active, reinterpret_cast<int32_t*>(tabs + dt.active), off_sm, assign_tok, slot_sm,
+                              recs_active, reinterpret_cast<int32_t*>(tabs + dt.aret)};
+            if (G * A <= 32) {
+                if (warp == 0) group_warp<true>(rq, go, rmeta, recs_sm);
+            } else {
+                group_assignments<kThreads, true>(rq, go, rmeta, reinterpret_cast<int32_t*>(tabs + dt.counts),
+                                                  reinterpret_cast<int32_t*>(tabs + dt.base), recs_sm);
+            }
         } else {
-            group_assignments<kThreads>(p.r, go, ids_sm, reinterpret_cast<int32_t*>(tabs + dt.counts),
-                                        reinterpret_cast<int32_t*>(tabs + dt.base), recs_sm);
+            const GroupOut go{n_active, reinterpret_cast<int32_t*>(tabs + dt.active), off_sm, assign_tok, slot_sm,
+                              recs_active, nullptr};
+            if (A <= 32) {
+                if (warp == 0) group_warp(p.r, go, ids_sm, recs_sm);
+            } else {
+                group_assignments<kThreads>(p.r, go, ids_sm, reinterpret_cast<int32_t*>(tabs + dt.counts),
+                                            reinterpret_cast<int32_t*>(tabs + dt.base), recs_sm);
+            }
         }
         __syncthreads();
     }
@@ -334,8 +400,8 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
 
     // ---- 4. gate/up then down through one ring ----
     const int n_e = *n_active;
-    const Tables tgu{recs_active, off_sm, assign_tok, n_e};
-    const Tables tdn{recs_active, off_sm, nullptr, n_e};
+    const Tables tgu{recs_active, off_sm, assign_tok, n_e, nullptr};
+    const Tables tdn{recs_active, off_sm, nullptr, n_e, EP ? reinterpret_cast<const int32_t*>(tabs + dt.aret) : nullptr};
     int gu0, gu1, dn0, dn1;
     cta_units(n_e, p.gu.gpe, gu0, gu1);
     cta_units(n_e, p.dn.gpe, dn0, dn1);
@@ -368,52 +434,101 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         if (blockIdx.x == 0) st_relaxed_u32(p.sync + kSyncEpoch, epoch);
         tl_mark(TL_DOWN, TL_WAITED);
     }
-    if (!stream_consume<1, TB, P, false, true, BLK, true>(p.dn, tdn, rg, dn0, dn1, pos)) s_fail = 1;
+    if (!stream_consume<1, TB, P, false, true, BLK, true, EP>(p.dn, tdn, rg, dn0, dn1, pos)) s_fail = 1;
     consumers_sync();  // the CTA's y rows are written
     if (s_fail) return;
 
-    // ---- 5. slot-order combine of the row groups this CTA completes ----
-    for (int i = threadIdx.x; i < dn1 - dn0; i += kWarps * 32) {
-        const int g = (dn0 + i) % p.dn.gpe;
-        fence_acq_rel_gpu();  // release the CTA's y rows before counting the unit
-        const unsigned old = atomicAdd(p.sync + kSyncGroups + g, 1u);
-        if (old == static_cast<unsigned>(n_e - 1)) {
-            p.sync[kSyncGroups + g] = 0u;  // every expert's unit of the group has arrived
-            atomicOr(&cbits[g >> 5], 1u << (g & 31));
-        }
-    }
-    consumers_sync();
-    fence_acq_rel_gpu();  // acquire: the other CTAs' y rows of the completed groups
-    const float* y = static_cast<const float*>(p.dn.y);
-    const int rpp = p.dn.rpp;
-    for (int wd = 0; wd < (p.dn.gpe + 31) / 32; wd++) {
-        unsigned bits = cbits[wd];
-        while (bits) {
-            const int g = wd * 32 + __ffs(bits) - 1;
-            bits &= bits - 1;
-            const int row0 = g * rpp, nr = min(rpp, H - row0);
-            for (int o = threadIdx.x; o < nr * T; o += kWarps * 32) {
-                const int t = o / nr, row = row0 + (o - t * nr);
-                float acc = 0.0f;
-                for (int s0 = 0; s0 < K; s0 += 8) {
-                    float v[8], ws[8];
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const bool ok = s0 + j < K;
-                        ws[j] = ok ? w_sm[t * K + s0 + j] : 0.0f;
-                        v[j] = ok ? __ldcg(y + static_cast<int64_t>(slot_sm[t * K + s0 + j]) * H + row) : 0.0f;
+    if constexpr (EP) {
+        // ---- 5 (expert parallel). the output rows are in their source ranks' mailboxes:
+        // a grid barrier, the return flags, and once every rank's are up, the combine ----
+        const EpMailbox mb = ep_mailbox(p.ep.ranks, p.ep.t_max, p.ep.k, p.ep.h, p.ep.xb);
+        const unsigned ep_ep = s_ep_epoch;
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            bar_arrive(bars + 64);
+            if (!bar_wait(bars + 64, gridDim.x, p.r.err, ERR_GRID_WAIT)) s_fail = 1;
+            if (!s_fail && static_cast<int>(blockIdx.x) < G) {
+                __threadfence_system();
+                ep_st_relaxed_sys(reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(p.ep.peers[blockIdx.x]) +
+                                                              mb.flags_return) +
+                                      p.ep.rank,
+                                  ep_ep);
+            }
+            const unsigned* flags = reinterpret_cast<const unsigned*>(p.ep.mailbox + mb.flags_return);
+            for (int g = 0; g < G && !s_fail; g++) {
+                if (ep_ld_acquire_sys(flags + g) == ep_ep) continue;
+                const unsigned long long t0 = global_ns();
+                while (ep_ld_acquire_sys(flags + g) != ep_ep) {
+                    if (global_ns() - t0 > kWaitLimitNs) {
+                        record_error(p.r.err, ERR_EP_RETURN_WAIT);
+                        s_fail = 1;
+                        break;
                     }
-#pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        if (s0 + j < K) acc = fmaf(ws[j], v[j], acc);
                 }
-                const int64_t oi = static_cast<int64_t>(t) * H + row;
-                if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(acc);
-                else static_cast<float*>(p.out)[oi] = acc;
             }
         }
+        consumers_sync();
+        if (s_fail) return;
+        const float* back = reinterpret_cast<const float*>(p.ep.mailbox + mb.back);
+        for (int o = blockIdx.x * (kWarps * 32) + threadIdx.x; o < T * H; o += gridDim.x * (kWarps * 32)) {
+            const int t = o / H, c = o - t * H;
+            float acc = 0.0f;
+            for (int s = 0; s < K; s++) {
+                const int e = ids_sm[t * K + s];
+                const int g = min(max(e / p.epr, 0), G - 1);
+                acc = fmaf(w_sm[t * K + s],
+                           __ldcg(back + (static_cast<int64_t>(g) * A + static_cast<int64_t>(t) * K + s) * H + c), acc);
+            }
+            if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(acc);
+            else static_cast<float*>(p.out)[o] = acc;
+        }
+        if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
     }
-    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
+
+    if constexpr (!EP) {
+        // ---- 5. slot-order combine of the row groups this CTA completes ----
+        for (int i = threadIdx.x; i < dn1 - dn0; i += kWarps * 32) {
+            const int g = (dn0 + i) % p.dn.gpe;
+            fence_acq_rel_gpu();  // release the CTA's y rows before counting the unit
+            const unsigned old = atomicAdd(p.sync + kSyncGroups + g, 1u);
+            if (old == static_cast<unsigned>(n_e - 1)) {
+                p.sync[kSyncGroups + g] = 0u;  // every expert's unit of the group has arrived
+                atomicOr(&cbits[g >> 5], 1u << (g & 31));
+            }
+        }
+        consumers_sync();
+        fence_acq_rel_gpu();  // acquire: the other CTAs' y rows of the completed groups
+        const float* y = static_cast<const float*>(p.dn.y);
+        const int rpp = p.dn.rpp;
+        for (int wd = 0; wd < (p.dn.gpe + 31) / 32; wd++) {
+            unsigned bits = cbits[wd];
+            while (bits) {
+                const int g = wd * 32 + __ffs(bits) - 1;
+                bits &= bits - 1;
+                const int row0 = g * rpp, nr = min(rpp, H - row0);
+                for (int o = threadIdx.x; o < nr * T; o += kWarps * 32) {
+                    const int t = o / nr, row = row0 + (o - t * nr);
+                    float acc = 0.0f;
+                    for (int s0 = 0; s0 < K; s0 += 8) {
+                        float v[8], ws[8];
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const bool ok = s0 + j < K;
+                            ws[j] = ok ? w_sm[t * K + s0 + j] : 0.0f;
+                            v[j] = ok ? __ldcg(y + static_cast<int64_t>(slot_sm[t * K + s0 + j]) * H + row) : 0.0f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            if (s0 + j < K) acc = fmaf(ws[j], v[j], acc);
+                    }
+                    const int64_t oi = static_cast<int64_t>(t) * H + row;
+                    if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(acc);
+                    else static_cast<float*>(p.out)[oi] = acc;
+                }
+            }
+        }
+        if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
+    }
 }
 
 }  // namespace oomb

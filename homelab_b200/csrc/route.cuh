@@ -488,13 +488,15 @@ struct GroupOut {
     int32_t* assign_tok;
     int32_t* slot_assign;
     uint64_t* recs_active;
+    int32_t* assign_ret;  // optional: the slot (flat index) of each assignment
 };
 
 // Groups the T*K assignments by expert (counting sort, stable in slot order).
-// Runs on one CTA of NT threads; ids in shared memory.  counts, base: E ints of
+// SKIP_NEG: entries of -1 are another rank's (expert parallelism) and are
+// skipped without an error.  Runs on one CTA of NT threads; ids in shared memory.  counts, base: E ints of
 // shared scratch; recs_sm: the layer's record addresses staged in shared
 // memory, or null to read them from p.recs_all.
-template <int NT>
+template <int NT, bool SKIP_NEG = false>
 __device__ void group_assignments(const RouteParams& p, const GroupOut& g, const int32_t* ids_sm, int32_t* counts,
                                   int32_t* base, const uint64_t* recs_sm) {
     const int A = p.T * p.K;
@@ -504,7 +506,7 @@ __device__ void group_assignments(const RouteParams& p, const GroupOut& g, const
     for (int s = threadIdx.x; s < A; s += blockDim.x) {
         const int e = ids_sm[s];
         if (e >= 0 && e < p.E) atomicAdd(&counts[e], 1);
-        else record_error(p.err, ERR_BAD_TABLE);
+        else if (!(SKIP_NEG && e < 0)) record_error(p.err, ERR_BAD_TABLE);
     }
     __syncthreads();
     if (p.E <= NT) {
@@ -577,6 +579,7 @@ __device__ void group_assignments(const RouteParams& p, const GroupOut& g, const
                 const int a = base[e] + rank;
                 g.assign_tok[a] = s / p.K;
                 g.slot_assign[s] = a;
+                if (g.assign_ret) g.assign_ret[a] = s;
             }
             __syncwarp();
             // the highest lane of each peer group advances the expert's base
@@ -591,6 +594,7 @@ __device__ void group_assignments(const RouteParams& p, const GroupOut& g, const
 // slot) order is the count of assignments of smaller experts plus the earlier
 // slots of its own expert; the first slot of each expert leads the expert's
 // group, whose index is the count of leaders of smaller experts.
+template <bool SKIP_NEG = false>
 __device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_t* ids_sm, const uint64_t* recs_sm) {
     const int lane = threadIdx.x & 31;
     const int A = p.T * p.K;
@@ -600,7 +604,7 @@ __device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_
         const int e = ids_sm[lane];
         valid = e >= 0 && e < p.E;
         if (valid) key = e;
-        else record_error(p.err, ERR_BAD_TABLE);
+        else if (!(SKIP_NEG && e < 0)) record_error(p.err, ERR_BAD_TABLE);
     }
     int lt = 0, before = 0;
 #pragma unroll 4
@@ -622,6 +626,7 @@ __device__ void group_warp(const RouteParams& p, const GroupOut& g, const int32_
         const int a = lt + before;
         g.assign_tok[a] = lane / p.K;
         g.slot_assign[lane] = a;
+        if (g.assign_ret) g.assign_ret[a] = lane;
     }
     if (leader) {
         g.active[idx] = key;
@@ -762,7 +767,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         }
         __syncthreads();
         if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_TOPK_DONE);
-        const GroupOut go{p.n_active, p.active, p.off, p.assign_tok, p.slot_assign, p.recs_active};
+        const GroupOut go{p.n_active, p.active, p.off, p.assign_tok, p.slot_assign, p.recs_active, nullptr};
         group_assignments<kRouteThreads>(p, go, ids_sm, ids_sm + p.T * p.K, ids_sm + p.T * p.K + p.E, recs_sm);
         if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_END);
     } else if (ranked) {

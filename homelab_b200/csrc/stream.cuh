@@ -126,6 +126,12 @@ struct StreamParams {
     void* y;        // dense: [t, nrows] (y_bf16 ? bf16 : fp32); MoE: [A, nrows] fp32
     int y_bf16;
     unsigned* err;
+    // expert-parallel outputs (decode kernel): output row a goes to rank g's
+    // mailbox at ep_back_off, row (ep_rank * ep_tk + ts) of [*, nrows] fp32,
+    // where g * ep_tk + ts is the assignment's return index
+    const unsigned long long* ep_peers;
+    int64_t ep_back_off;
+    int ep_rank, ep_tk;
 };
 
 // ---- activation slices in registers ----------------------------------------------------
@@ -244,6 +250,7 @@ struct Tables {
     const int32_t* off;
     const int32_t* assign_tok;
     int n_e;
+    const int32_t* assign_ret;  // expert-parallel outputs: return index of each assignment
 };
 
 template <bool TSMEM>
@@ -260,7 +267,7 @@ __device__ __forceinline__ unsigned long long tab_u64(const uint64_t* a) {
 
 // The tables of a stand-alone launch (dense launches: one group, no tables).
 __device__ __forceinline__ Tables global_tables(const StreamParams& p, bool moe) {
-    Tables tb{p.recs, p.off, p.assign_tok, 1};
+    Tables tb{p.recs, p.off, p.assign_tok, 1, nullptr};
     if (moe) tb.n_e = p.n_e_dev ? __ldcg(p.n_e_dev) : p.n_e_host;
     return tb;
 }
@@ -312,9 +319,11 @@ __host__ __device__ constexpr unsigned timeline_kind() {
 // ---- per-pass reduction and output ----------------------------------------------------------
 
 // hdr[pi] = {a_begin, a_end, row0, nr} of the pass's units (shared memory).
-template <int PARTS, int TB, int P, bool MOE>
+// EPOUT: MoE outputs go to the ranks whose assignments they are (aret: return
+// index of each assignment), else to p.y.
+template <int PARTS, int TB, int P, bool MOE, bool EPOUT = false>
 __device__ __forceinline__ void reduce_write(const StreamParams& p, const float (&acc)[P][kRows][TB], float* rb,
-                                             const int* hdr, int pn, int warp, int lane) {
+                                             const int* hdr, int pn, int warp, int lane, const int32_t* aret = nullptr) {
     // The multi-value butterfly sums every partial over the 32 lanes by the same
     // tree (pairs at lane distance 16, then 8, 4, 2, 1; addition commutes), so
     // an output's arithmetic does not depend on its position in the pass: results
@@ -360,7 +369,14 @@ __device__ __forceinline__ void reduce_write(const StreamParams& p, const float 
         const int row = row0 + r;
         if (MOE) {
             const float val = PARTS == 2 ? res[0] / (1.0f + expf(-res[0])) * res[PARTS - 1] : res[0];
-            static_cast<float*>(p.y)[static_cast<int64_t>(a_begin + b) * p.nrows + row] = val;
+            if (EPOUT) {
+                const int r = aret[a_begin + b];
+                const int g = r / p.ep_tk, ts = r - g * p.ep_tk;
+                float* dst = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peers[g]) + p.ep_back_off);
+                dst[(static_cast<int64_t>(p.ep_rank) * p.ep_tk + ts) * p.nrows + row] = val;
+            } else {
+                static_cast<float*>(p.y)[static_cast<int64_t>(a_begin + b) * p.nrows + row] = val;
+            }
         } else {
             const int64_t yi = static_cast<int64_t>(a_begin + b) * p.nrows + row;
             if (p.y_bf16) static_cast<__nv_bfloat16*>(p.y)[yi] = __float2bfloat16_rn(res[0]);
@@ -501,7 +517,7 @@ __device__ bool stream_meta(const StreamParams& p, const Tables& tb, const Ring&
 
 // Consumer warps: the arithmetic of units [u0, u1) from the rings, continuing
 // at ring positions `pos`.  Returns false when a wait ran out.
-template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool BLK, bool TSMEM>
+template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool BLK, bool TSMEM, bool EPOUT = false>
 __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1,
                                RingPos& pos) {
     static_assert(kRows * P * TB <= kRedV, "too many partials per lane");
@@ -639,8 +655,8 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
                                 ch[2] = hdr[pi * 4 + 2];
                                 ch[3] = nr;
                             }
-                            reduce_write<PARTS, TB, P, MOE>(p, acc, rg.red + rparity * kWarps * kRedV, ch, 1, warp,
-                                                            lane);
+                            reduce_write<PARTS, TB, P, MOE, EPOUT>(p, acc, rg.red + rparity * kWarps * kRedV, ch, 1,
+                                                                   warp, lane, tb.assign_ret);
                             rparity ^= 1;
 #pragma unroll
                             for (int j = 0; j < kRows; j++)
@@ -655,7 +671,8 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
             }
         }
         if (!chunked_any) {
-            reduce_write<PARTS, TB, P, MOE>(p, acc, rg.red + rparity * kWarps * kRedV, hdr, pn, warp, lane);
+            reduce_write<PARTS, TB, P, MOE, EPOUT>(p, acc, rg.red + rparity * kWarps * kRedV, hdr, pn, warp, lane,
+                                                   tb.assign_ret);
             rparity ^= 1;
         }
         // this warp is done with the pass's table: hand it back

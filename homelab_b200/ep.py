@@ -332,3 +332,39 @@ class EpPeerMoeLayer:
         self.phase_route(x, t)
         self.phase_experts(t)
         return self.phase_combine(t, out)
+
+
+class EpDecodeLayer:
+    """The expert-parallel decode step in one launch per rank
+    (oomb_moe_decode_ep_fp8): route, dispatch into the mailboxes, the local
+    experts with each output row stored into its source rank's mailbox, and the
+    slot-order combine, for up to 16 tokens per rank and 256 experts.  Every
+    rank runs each step with the same t; the kernels of the ranks wait on one
+    another (bounded waits), so each rank's runs on its own GPU."""
+
+    def __init__(self, mailboxes: EpPeerMailboxes, rank, hidden, experts, top_k, router_w, recs_local, geo, t_max):
+        self.L = L = _lib.lib()
+        self.mb = mailboxes
+        self.q = mailboxes.view(rank)
+        self.layer = _lib.MoeLayer(hidden=hidden, experts=experts, top_k=top_k, router_w=router_w.data_ptr(),
+                                   recs=recs_local.data_ptr())
+        self.layer.geo = geo
+        self._keep = (router_w, recs_local)
+        dev = router_w.device
+        self.t_max = t_max
+        n = int(L.oomb_moe_decode_ep_workspace_bytes(t_max, mailboxes.G, C.byref(self.layer)))
+        if n == 0:
+            raise ValueError("unsupported expert-parallel layer shape")
+        self.ws = torch.zeros(n, dtype=torch.uint8, device=dev)
+        self.ids = torch.empty((t_max, top_k), dtype=torch.int32, device=dev)
+        self.weights = torch.empty((t_max, top_k), dtype=torch.float32, device=dev)
+
+    def forward(self, x, t: int, out):
+        """out[t, hidden] = the routed experts' combined output for this rank's t tokens."""
+        xd = BF16 if x.dtype == torch.bfloat16 else F32
+        od = BF16 if out.dtype == torch.bfloat16 else F32
+        s = torch.cuda.current_stream(x.device).cuda_stream
+        check(self.L.oomb_moe_decode_ep_fp8(C.byref(self.layer), C.byref(self.q), x.data_ptr(), xd, t, out.data_ptr(),
+                                            od, self.ids.data_ptr(), self.weights.data_ptr(), self.ws.data_ptr(),
+                                            self.ws.numel(), s), "moe_decode_ep")
+        return self.ids[:t], self.weights[:t]

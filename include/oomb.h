@@ -289,6 +289,18 @@ typedef struct oomb_ep_peer {
     int x_dtype;           /* OOMB_BF16 or OOMB_F32 activations */
 } oomb_ep_peer;
 
+/* The one-launch decode step (as oomb_moe_decode_fp8, up to 16 tokens per rank
+ * and 256 experts) with expert parallelism: layer->recs holds this rank's
+ * experts [rank * E/ranks, (rank + 1) * E/ranks), layer->router_w the whole
+ * router.  Route, dispatch to the mailboxes, grouping of the received slots,
+ * gate/up and down over the local experts with each output row stored into its
+ * source rank's mailbox, and the slot-order combine, in one kernel per rank;
+ * every rank runs the step with the same t.  Bit-identical to one GPU. */
+size_t oomb_moe_decode_ep_workspace_bytes(int t, int ranks, const oomb_moe_layer* layer);
+int oomb_moe_decode_ep_fp8(const oomb_moe_layer* layer, const oomb_ep_peer* peer, const void* x, int x_dtype, int t,
+                           void* out, int out_dtype, int32_t* ids, float* weights, void* workspace,
+                           size_t workspace_bytes, oomb_stream stream);
+
 #define OOMB_IPC_HANDLE_BYTES 64
 size_t oomb_ep_mailbox_bytes(int ranks, int t_max, int top_k, int hidden, int x_dtype);
 /* Byte offset of the received activations [ranks * t, hidden] in a mailbox. */

@@ -105,3 +105,34 @@ def test_no_gpu_fails_loudly():
     L = hb.lib()
     fake = 0x10000
     assert L.oomb_gemm_fp8(fake, 0, fake, fake, 1, fake, 0, 1, 64, 32, None, 0, None) == _lib.E_DEVICE
+
+
+def test_expert_parallel_peer_entry_points_check_arguments():
+    L = hb.lib()
+    fake = 0x10000  # never dereferenced: every call below fails its checks first
+    assert L.oomb_ep_mailbox_bytes(2, 1, 8, 2048, _lib.BF16) > 0
+    assert L.oomb_ep_mailbox_bytes(0, 1, 8, 2048, _lib.BF16) == 0
+    assert L.oomb_ep_mailbox_bytes(2, 1, 8, 2048, 9) == 0  # unknown activation type
+    assert L.oomb_ep_mailbox_x_offset(2, 1, 8, 2048, _lib.BF16) % 256 == 0
+    # the x region grows with the ranks, and the later regions after it
+    assert L.oomb_ep_mailbox_bytes(4, 2, 8, 2048, _lib.BF16) > L.oomb_ep_mailbox_bytes(2, 2, 8, 2048, _lib.BF16)
+    q = _lib.EpPeer(fake, fake, 2, 0, 4, 8, 2048, _lib.BF16)
+    assert L.oomb_ep_dispatch_peer(None, fake, 1, 32, fake, None) == _lib.E_ARG
+    assert L.oomb_ep_dispatch_peer(C.byref(q), fake, 5, 32, fake, None) == _lib.E_SHAPE  # t > t_max
+    assert L.oomb_ep_dispatch_peer(C.byref(q), fake, 1, 32, fake + 4, None) == _lib.E_ALIGN
+    bad = _lib.EpPeer(fake, fake, 2, 2, 4, 8, 2048, _lib.BF16)  # rank out of range
+    assert L.oomb_ep_dispatch_peer(C.byref(bad), fake, 1, 32, fake, None) == _lib.E_ARG
+    assert L.oomb_ep_group_peer(C.byref(q), 0, 32, fake, fake, fake, fake, fake, fake, None) == _lib.E_SHAPE
+    assert L.oomb_ep_return_peer(C.byref(q), fake, fake, fake, fake, 1, 0, None) == _lib.E_SHAPE
+    assert L.oomb_ep_combine_peer(C.byref(q), fake, fake, 1, 32, fake, 7, None) == _lib.E_ARG  # out dtype
+    layer = hb.MoeLayer(hidden=2048, experts=64, top_k=8, router_w=fake, recs=fake)
+    layer.geo = hb.Fp8Record(hidden=2048, inter=768, layout=1, gate_weight=0, up_weight=768 * 2048,
+                             down_weight=2 * 768 * 2048, gate_scale=3 * 768 * 2048, up_scale=3 * 768 * 2048 + 512,
+                             down_scale=3 * 768 * 2048 + 1024)
+    assert L.oomb_moe_decode_ep_workspace_bytes(1, 2, C.byref(layer)) > L.oomb_moe_decode_workspace_bytes(1, C.byref(layer))
+    # activation dtype must match the mailboxes'; hidden must match the layer's
+    assert L.oomb_moe_decode_ep_fp8(C.byref(layer), C.byref(q), fake, _lib.F32, 1, fake, 0, None, None, fake, 1 << 30,
+                                    None) == _lib.E_ARG
+    q2 = _lib.EpPeer(fake, fake, 2, 0, 4, 8, 1024, _lib.BF16)
+    assert L.oomb_moe_decode_ep_fp8(C.byref(layer), C.byref(q2), fake, _lib.BF16, 1, fake, 0, None, None, fake,
+                                    1 << 30, None) == _lib.E_SHAPE

@@ -2,9 +2,11 @@
 through peer memory (CUDA IPC mailboxes, NVLink stores and epoch flags).
 
 Two spawned processes, one per GPU, shard a 64-expert layer; each runs several
-steps of EpPeerMoeLayer and compares its tokens' outputs, bit for bit, with the
-single-GPU fused decode of the whole batch on its own GPU (which holds the full
-layer too).  Skipped on a box with fewer than two GPUs.
+steps of the chain of kernels (EpPeerMoeLayer) or of the one-launch step
+(EpDecodeLayer, whose kernels on the two GPUs wait on each other) and compares
+its tokens' outputs, bit for bit, with the single-GPU fused decode of the whole
+batch on its own GPU (which holds the full layer too).  Skipped on a box with
+fewer than two GPUs.
 """
 import datetime
 import os
@@ -34,7 +36,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, t, result_dir):
+def _worker(rank, world, port, t, result_dir, fused):
     sys.path.insert(0, ROOT)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -47,7 +49,7 @@ def _worker(rank, world, port, t, result_dir):
         import oracle as O
         import homelab_b200 as hb
         from homelab_b200.backend import Gpu
-        from homelab_b200.ep import EpGpuOps, EpPeerMailboxes, EpPeerMoeLayer
+        from homelab_b200.ep import EpDecodeLayer, EpGpuOps, EpPeerMailboxes, EpPeerMoeLayer
         from homelab_b200.records import ExpertBank
         gpu = Gpu(rank)
         bank = ExpertBank(E, H, I, hb.SCALE_128X128, dev)
@@ -58,8 +60,11 @@ def _worker(rank, world, port, t, result_dir):
         full.geo = bank.geo
         epr = E // world
         mb = EpPeerMailboxes(dist.group.WORLD, H, K, t, torch.bfloat16, dev)
-        layer = EpPeerMoeLayer(EpGpuOps(dev), mb, rank, H, E, K, I, router,
-                               bank.addrs[rank * epr:(rank + 1) * epr].contiguous(), bank.geo, t)
+        recs_local = bank.addrs[rank * epr:(rank + 1) * epr].contiguous()
+        if fused:
+            layer = EpDecodeLayer(mb, rank, H, E, K, router, recs_local, bank.geo, t)
+        else:
+            layer = EpPeerMoeLayer(EpGpuOps(dev), mb, rank, H, E, K, I, router, recs_local, bank.geo, t)
         ws = gpu.moe_decode_workspace(full, world * t)
         same = True
         for step in range(STEPS):
@@ -83,9 +88,10 @@ def _worker(rank, world, port, t, result_dir):
             pass
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("t", [1, 3])
-def test_two_gpu_peer_expert_parallel_equals_one_gpu(tmp_path, t):
+def test_two_gpu_peer_expert_parallel_equals_one_gpu(tmp_path, t, fused):
     world = 2
-    mp.spawn(_worker, args=(world, _free_port(), t, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), t, str(tmp_path), fused), nprocs=world, join=True)
     for r in range(world):
         assert open(os.path.join(tmp_path, f"rank{r}.txt")).read() == "ok", f"rank {r}"
