@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel all-to-alls: kernels storing into peer mailboxes over NVLink, or NCCL")
+    ap.add_argument("--ep-step", choices=["chain", "fused"], default="chain",
+                    help="with peer transport: the chain of kernels, or one launch per rank and step")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU work of the cpu_baseline / reference sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
@@ -260,7 +262,7 @@ def run_ours(args, rank, world, local_rank):
         ops = EpGpuOps(dev)
         if args.ep_transport == "peer":
             mailboxes = EpPeerMailboxes(dist.group.WORLD, H, K_TOP, B, torch.bfloat16, dev)
-            if B <= 16:  # the one-launch step per rank
+            if args.ep_step == "fused" and B <= 16:  # the one-launch step per rank
                 ep_layers = [EpDecodeLayer(mailboxes, rank, H, E, K_TOP, router, bank.addrs, bank.geo, B)
                              for (bank, router, _) in layers]
             else:
@@ -420,7 +422,8 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": dict(config_dict(B, LAYERS), parallelism=f"ep{world}" if world > 1 else "single",
                            **({"expert_parallel": f"{E // world} experts per GPU, " + (
-                               "one launch per rank and step: dispatch and return stored by the kernel into peer "
+                               ("one launch per rank and step: " if args.ep_step == "fused" and B <= 16 else
+                                "chain of kernels: ") + "dispatch and return stored by the kernels into peer "
                                "mailboxes over NVLink (CUDA IPC)"
                                if args.ep_transport == "peer" else "NCCL all-to-all dispatch and combine"),
                                "step_capture": "cuda graph" if graphs_ok else "eager"} if world > 1 else {})),
@@ -442,7 +445,8 @@ def run_ours(args, rank, world, local_rank):
             # logits, top-k, dispatch, group, gate/up, down, return, combine; over NCCL:
             # logits, top-k, meta, group, gate/up, down, scatter, combine (NCCL's own
             # kernels not counted)
-            "gpu_launches": (1 if fused or (world > 1 and args.ep_transport == "peer" and B <= 16)
+            "gpu_launches": (1 if fused or (world > 1 and args.ep_transport == "peer" and args.ep_step == "fused"
+                                           and B <= 16)
                              else (4 if world == 1 else 8)) * K,
             "clocks": clocks,
         }

@@ -143,3 +143,25 @@ def test_peer_expert_parallel_equals_single_gpu(layer, G, t):
         for g in range(G):
             assert torch.equal(routing[g][0], ids[g * t:(g + 1) * t])
             assert torch.equal(outs[g], want[g * t:(g + 1) * t]), f"rank {g} differs from one GPU"
+
+
+def test_one_launch_expert_parallel_single_rank_equals_single_gpu(layer):
+    """The expert-parallel one-launch kernel with one rank: it dispatches to and
+    returns into its own mailbox (the waits are on flags that CTAs of the same,
+    fully resident launch raise), and its output equals the single-GPU decode."""
+    from homelab_b200.ep import EpDecodeLayer, EpPeerMailboxes
+    gpu, L, bank, router = layer["gpu"], layer["L"], layer["bank"], layer["router"]
+    for t in (1, 3):
+        mb = EpPeerMailboxes(None, H, K, t, torch.bfloat16, DEV, ranks=1)
+        ep = EpDecodeLayer(mb, 0, H, E, K, router, bank.addrs, bank.geo, t)
+        ws = gpu.moe_decode_workspace(L, t)
+        for step in range(3):
+            x = torch.from_numpy(O.normal_bf16(400 + 10 * t + step, t * H).view(np.int16)).to(DEV).view(torch.bfloat16)
+            x = x.view(t, H)
+            out = torch.full((t, H), float("nan"), dtype=torch.float32, device=DEV)
+            ep.forward(x, t, out)
+            want = torch.empty((t, H), dtype=torch.float32, device=DEV)
+            gpu.moe_decode(L, x, t, want, ws)
+            torch.cuda.synchronize()
+            assert torch.equal(out, want), f"t={t} step {step}"
+        mb.close()
