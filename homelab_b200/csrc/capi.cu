@@ -1276,8 +1276,10 @@ NoallocState g_noalloc[kMaxDevices];
 std::mutex g_noalloc_mu;
 
 // One-time set-up per device, with that device current: look up the array's
-// address and zero its first 256 bytes (the arrival counter, which the route
-// kernel resets after every call).  Returns nullptr if set-up failed.
+// address and zero the pieces that must start at zero and that the kernels keep
+// consistent from call to call: the chain's arrival counter (first 256 bytes)
+// and the one-launch kernel's sync words after it (launch epoch, barrier
+// counts, row-group counters).  Returns nullptr if set-up failed.
 uint8_t* noalloc_scratch(oomb_stream stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
@@ -1287,7 +1289,7 @@ uint8_t* noalloc_scratch(oomb_stream stream) {
         s.init = true;
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) == cudaSuccess &&
-            cudaMemsetAsync(p, 0, 256, stream) == cudaSuccess) {
+            cudaMemsetAsync(p, 0, 256 + up256(kSyncWords * 4), stream) == cudaSuccess) {
             s.scratch = static_cast<uint8_t*>(p);
             s.ok = true;
         }
