@@ -15,9 +15,12 @@ experts), so every step streams its weights from HBM.
 
 value   tokens/s over all ranks, device-timed (CUDA events around a CUDA graph of
         exactly K steps, inputs resident in HBM).
-e2e     the same through the public C ABI with host buffers: every step copies
-        its input from pinned host memory and its output back, inside the
-        timed region.
+e2e     the same through the public C ABI with host buffers, inside the timed
+        region: every step's input comes from pinned host memory and its output
+        goes back to pinned host memory.  At N = 1 the decode entry point takes
+        the host buffers itself (a staging kernel reads x over the bus after the
+        previous step, the step stores out into host memory); expert-parallel
+        ranks copy in and out with stream-ordered copies.
 roofline  the dominant kernel (gate/up+SiLU), timed in its own loop of
         back-to-back launches with CUDA events, against the measured HBM copy
         bandwidth of MEASURED_PEAKS.json.
@@ -297,11 +300,15 @@ def run_ours(args, rank, world, local_rank):
     reps, rem = divmod(K, G)
     s = torch.cuda.Stream(dev)
 
+    host_io = world == 1  # the single-GPU entry point reads and writes pinned host buffers itself
+
     def capture(n, e2e=False, xh=None, oh=None, xdev=None):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             for i in range(n):
-                if e2e:
+                if e2e and host_io:
+                    step(i, xh[i % NX], oh[i % NX])
+                elif e2e:
                     xdev.copy_(xh[i % NX], non_blocking=True)
                     step(i, xdev, out)
                     oh[i % NX].copy_(out, non_blocking=True)
@@ -318,7 +325,9 @@ def run_ours(args, rank, world, local_rank):
         def replay(self):
             with torch.cuda.stream(s):
                 for i in range(self.n):
-                    if self.e2e:
+                    if self.e2e and host_io:
+                        step(i, self.xh[i % NX], self.oh[i % NX])
+                    elif self.e2e:
                         self.xdev.copy_(self.xh[i % NX], non_blocking=True)
                         step(i, self.xdev, out)
                         self.oh[i % NX].copy_(out, non_blocking=True)

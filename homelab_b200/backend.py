@@ -37,6 +37,16 @@ def _ptr(t) -> int:
     return t.data_ptr()
 
 
+def _ptr_or_host(t) -> int:
+    """A device tensor's address, or a host tensor's (the library takes pinned
+    host memory where its entry points say so and refuses pageable memory)."""
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
 class Gpu:
     """One device's backend (the counterpart of `oominf_cuda::Gpu`)."""
 
@@ -128,8 +138,9 @@ class Gpu:
         return ws
 
     def moe_decode(self, layer: MoeLayer, x, t: int, out, workspace, ids=None, weights=None):
-        """One resident MoE layer step: route, group, gate/up, down, combine."""
-        check(self.L.oomb_moe_decode_fp8(C.byref(layer), _ptr(x), _dtype_code(x), t, _ptr(out),
+        """One resident MoE layer step: route, group, gate/up, down, combine.
+        x and out may be pinned host tensors (read and written by the kernels over the bus)."""
+        check(self.L.oomb_moe_decode_fp8(C.byref(layer), _ptr_or_host(x), _dtype_code(x), t, _ptr_or_host(out),
                                          _dtype_code(out), _ptr(ids), _ptr(weights), _ptr(workspace),
                                          workspace.numel(), self._stream()), "moe_decode")
 

@@ -101,6 +101,27 @@ int launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t strea
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Where a caller's buffer lives.  Pinned host memory (cudaHostAlloc,
+// cudaHostRegister) is reachable from kernels at its mapped device address;
+// pageable host memory and unknown pointers are reachable by no kernel.
+enum class Mem { none, device, host };
+Mem mem_kind(const void* p, const void** dev) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return Mem::none;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+        *dev = p;
+        return Mem::device;
+    }
+    if (a.type == cudaMemoryTypeHost && a.devicePointer) {
+        *dev = a.devicePointer;
+        return Mem::host;
+    }
+    return Mem::none;
+}
+
 // ---- streaming kernels ----------------------------------------------------------
 
 // Token slots for units with at most `maxn` assignments (0: unknown), and
@@ -726,6 +747,8 @@ struct DecodeLayout {
 size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 // ranks > 1: the expert-parallel kernel, whose h holds the slots of every rank's tokens.
+// y [A, H] fp32 also holds the device copy of activations passed in host memory
+// (T x H, at most 4 bytes each): a step writes y only after its last read of x.
 DecodeLayout decode_layout(int t, const oomb_moe_layer* L, int ranks = 1) {
     DecodeLayout d{};
     const size_t T = t, E = L->experts, K = L->top_k, A = T * K, AH = static_cast<size_t>(ranks) * A;
@@ -792,6 +815,26 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const int E = L->experts, K = L->top_k, H = L->hidden;
     const int A = t * K;
+    // x and out may be pinned host memory; the workspace, ids and weights are device memory
+    const void* xv = nullptr;
+    const void* ov = nullptr;
+    const void* unused = nullptr;
+    const Mem xk = mem_kind(x, &xv), ok = mem_kind(out, &ov);
+    if (xk == Mem::none || ok == Mem::none || mem_kind(workspace, &unused) != Mem::device ||
+        (ids && mem_kind(ids, &unused) != Mem::device) || (weights && mem_kind(weights, &unused) != Mem::device))
+        return OOMB_E_ARG;
+    out = const_cast<void*>(ov);
+    if (xk == Mem::host) {
+        // staged into the y region, which the step writes only after its last read of x
+        const int64_t n16 = static_cast<int64_t>(t) * H * (x_dtype == OOMB_BF16 ? 2 : 4) / 16;
+        const int64_t blocks = (n16 + 255) / 256;
+        rc = launch(stage_host_kernel, dim3(static_cast<unsigned>(blocks < d->sms ? blocks : d->sms)), dim3(256), 0,
+                    stream, reinterpret_cast<uint4*>(ws + lay.y), static_cast<const uint4*>(xv), n16);
+        if (rc) return rc;
+        x = ws + lay.y;
+    } else {
+        x = xv;
+    }
 
     FusedDecode f;
     if (fused_decode_plan(d, L, t, x_dtype == OOMB_BF16, f)) {

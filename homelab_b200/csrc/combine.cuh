@@ -5,6 +5,18 @@
 
 namespace oomb {
 
+// Copies n16 16-byte words of activations from pinned host memory, read at
+// its mapped device address (.cv: fetched again, never a stale cached line),
+// into device memory once the previous kernel of the stream has completed, so
+// the kernels after it read a device copy.
+__global__ void __launch_bounds__(256) stage_host_kernel(uint4* dst, const uint4* src, int64_t n16) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < n16;
+         i += static_cast<int64_t>(gridDim.x) * 256)
+        dst[i] = __ldcv(src + i);
+}
+
 // out[t, c] = sum_s w[t, s] * y[slot[t, s], c] in slot order with fmaf
 // (moe_combine_slots, moe.cu:155-164).  Four columns per thread; the slot
 // indices and weights of a group of 8 slots are loaded before their rows so the

@@ -190,6 +190,11 @@ int oomb_moe_combine(const float* routed, const float* shared, const float* gate
  * results as calling the separate entry points in that order.
  *   x: [t, hidden] (x_dtype); out: [t, hidden] (out_dtype);
  *   ids, weights: optional [t, top_k] copies of the routing (NULL to skip).
+ * x and out may be pinned host memory (cudaHostAlloc / cudaHostRegister): the
+ * step then reads x over the bus into the workspace with one small kernel
+ * after the stream's previous work, and stores out straight into host memory,
+ * with no separate copies; pageable host memory is refused (OOMB_E_ARG).  The
+ * workspace, ids and weights are device memory.
  * The workspace must hold oomb_moe_decode_workspace_bytes(t, layer) bytes and
  * be zeroed once before first use (oomb_workspace_clear), and again after a
  * device error (oomb_device_error); calls that share a workspace must be

@@ -9,8 +9,10 @@ weights, out) across activation dtypes, scale layouts, output dtypes, batch
 sizes (one token, two, and the chunked path) and layer shapes; repeated
 launches on one workspace (grid-barrier and row-group counters reset
 themselves), launches of different batch sizes on one workspace and CUDA graph
-replays must keep giving the same bits; and the one-launch result must meet
-the float64 bound on its own.
+replays must keep giving the same bits; the one-launch result must meet the
+float64 bound on its own; and activations and outputs in pinned host memory
+(read and written by the step's kernels over the bus) must give the same bits
+as device buffers, in graphs too, while pageable host memory is refused.
 """
 import os
 
@@ -169,3 +171,82 @@ def test_one_launch_meets_the_float64_bound(gpu, name, xbf16, t):
     truth = O.combine_slots_f64(y, slot, want_w, t, H, K)
     got = out.cpu().numpy()
     assert np.abs(got - truth).max() / np.abs(truth).max() <= 1e-4
+
+
+def _same_bits(a, b):
+    if a.dtype == torch.float32:
+        return torch.equal(a.view(torch.int32), b.view(torch.int32))
+    return torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+@pytest.mark.parametrize("chain", [False, True])
+@pytest.mark.parametrize("xbf16,out_dtype,t", [(True, torch.bfloat16, 1), (False, torch.float32, 3),
+                                               (True, torch.float32, 16), (False, torch.bfloat16, 24)])
+def test_pinned_host_activations_and_outputs(gpu, chain, xbf16, out_dtype, t):
+    """x and out in pinned host memory: the same bits as device buffers (the step
+    reads x over the bus into its workspace and stores out into host memory)."""
+    lay = get_layer(gpu, "config2")
+    L, H, K = lay["L"], lay["L"].hidden, lay["L"].top_k
+    x = make_x(H, t, xbf16, 1300 + t)
+    want = run(gpu, lay, x, t, out_dtype, chain=chain)
+    xh = x.cpu().pin_memory()
+    oh = torch.full((t, H), float("nan"), dtype=out_dtype).pin_memory()
+    ids = torch.full((t, K), -1, dtype=torch.int32, device=DEV)
+    wts = torch.full((t, K), float("nan"), dtype=torch.float32, device=DEV)
+    ws = gpu.moe_decode_workspace(L, t)
+    if chain:
+        os.environ["OOMB_DECODE_CHAIN"] = "1"
+    try:
+        for _ in range(2):  # the second call reuses the workspace's staged copy region
+            gpu.moe_decode(L, xh, t, oh, ws, ids, wts)
+    finally:
+        os.environ.pop("OOMB_DECODE_CHAIN", None)
+    torch.cuda.synchronize()
+    assert _same_bits(oh, want[0].cpu())
+    assert torch.equal(ids, want[1]) and _same_bits(wts, want[2])
+
+
+def test_pinned_host_buffers_in_a_graph(gpu):
+    """Graph replays of steps whose x and out are pinned host buffers, new host
+    contents before every replay."""
+    lay = get_layer(gpu, "config2")
+    L, H = lay["L"], lay["L"].hidden
+    t = 1
+    xs = [make_x(H, t, True, 1400 + i) for i in range(4)]
+    want = [run(gpu, lay, x, t, torch.bfloat16, chain=True)[0].cpu() for x in xs]
+    xh = [torch.empty((t, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    oh = [torch.empty((t, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    ws = gpu.moe_decode_workspace(L, t)
+    s = torch.cuda.Stream(DEV)
+    s.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(s):
+        xh[0].copy_(xs[0].cpu())
+        gpu.moe_decode(L, xh[0], t, oh[0], ws)  # warm-up outside the capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for j in range(2):
+                gpu.moe_decode(L, xh[j], t, oh[j], ws)
+    torch.cuda.current_stream(DEV).wait_stream(s)
+    torch.cuda.synchronize()
+    for r in range(2):
+        for j in range(2):
+            xh[j].copy_(xs[2 * r + j].cpu())
+            oh[j].fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        for j in range(2):
+            assert _same_bits(oh[j], want[2 * r + j])
+    del g
+
+
+def test_pageable_host_memory_is_refused(gpu):
+    lay = get_layer(gpu, "small")
+    L, H = lay["L"], lay["L"].hidden
+    ws = gpu.moe_decode_workspace(L, 1)
+    x = torch.zeros((1, H), dtype=torch.bfloat16)  # pageable
+    out = torch.empty((1, H), dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(hb.OombError):
+        gpu.moe_decode(L, x, 1, out, ws)
+    with pytest.raises(hb.OombError):
+        gpu.moe_decode(L, x.to(DEV), 1, torch.empty((1, H), dtype=torch.bfloat16), ws)
+    torch.cuda.synchronize()
