@@ -138,6 +138,28 @@ __device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, unsig
         : "memory");
 }
 
+// Block scales are read again every step and are 0.4 % of the weight bytes:
+// loaded with evict-last priority they stay in L2 under the streamed weights, so
+// a step's scale reads do not queue in HBM behind its weight copies.
+#ifndef OOMB_SCALE_KEEP
+#define OOMB_SCALE_KEEP 1
+#endif
+__device__ __forceinline__ uint64_t make_evict_last_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ float ld_scale(const float* a, uint64_t keep) {
+#if OOMB_SCALE_KEEP
+    float v;
+    asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(a), "l"(keep));
+    return v;
+#else
+    return __ldg(a);
+#endif
+}
+
 // Weights are streamed once per step: mark them evict-first so they do not push
 // activations and routing tables out of L2.
 __device__ __forceinline__ uint64_t make_evict_first_policy() {

@@ -388,10 +388,14 @@ __device__ __forceinline__ void reduce_write(const StreamParams& p, const float 
 // ---- the three roles --------------------------------------------------------------------
 
 // Copy producer (one lane): streams units [u0, u1) into the stage ring,
-// continuing at ring position s.  After a wait that ran out it drains its
-// copies in flight and returns false.
+// continuing at ring position s.  With lag > 0 at most `lag` stages are in
+// flight: stage s is requested once stage s - lag has landed, so when every CTA
+// requests at once, each CTA's first stages are served first instead of all of
+// its ring landing together at the end of the burst.  After a wait that ran out
+// it drains its copies in flight and returns false.
 template <int PARTS, int P, bool MOE, bool TSMEM>
-__device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1, int& s) {
+__device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1, int& s,
+                            int lag = 0) {
     constexpr unsigned TLK = timeline_kind<PARTS, MOE>();
     if (u1 <= u0) return true;
     const int S = rg.stages, KS = p.ks;
@@ -410,6 +414,8 @@ __device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring&
             for (int pi = 0; pi < pn; pi++, s++) {
                 const int slot = s % S;
                 ok = mbar_wait(&rg.empty[slot], ((s / S) & 1) ^ 1, p.err, ERR_EMPTY_WAIT);
+                if (ok && lag > 0 && lag < S && s >= lag)
+                    ok = mbar_wait(&rg.full[(s - lag) % S], ((s - lag) / S) & 1, p.err, ERR_EMPTY_WAIT);
                 if (!ok) break;
                 const int u = pf + pi;
                 const int uei = u / p.gpe, g = u - uei * p.gpe;
@@ -460,6 +466,7 @@ __device__ bool stream_meta(const StreamParams& p, const Tables& tb, const Ring&
     const int lane = threadIdx.x & 31;
     const int meta_ints = P * 4;
     const int pair_floats = p.sr * p.nb;  // scale table of one (unit, part)
+    const uint64_t keep = make_evict_last_policy();
     for (int pf = u0; pf < u1; pf += P, q++) {
         const int buf = q % kMetaBufs;
         if (!mbar_wait(&rg.mempty[buf], ((q / kMetaBufs) & 1) ^ 1, p.err, ERR_EMPTY_WAIT)) return false;
@@ -501,7 +508,7 @@ __device__ bool stream_meta(const StreamParams& p, const Tables& tb, const Ring&
                                           : p.scale;
                     const int r = ep / p.nb, kb = ep - r * p.nb;
                     const int srow = p.layout ? (row0 >> 7) + r : row0 + r;
-                    if ((p.layout ? srow * 128 : srow) < p.nrows) v[m] = __ldg(sp + static_cast<int64_t>(srow) * p.nb + kb);
+                    if ((p.layout ? srow * 128 : srow) < p.nrows) v[m] = ld_scale(sp + static_cast<int64_t>(srow) * p.nb + kb, keep);
                 }
             }
 #pragma unroll
