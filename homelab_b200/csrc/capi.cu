@@ -453,6 +453,11 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     fill(q.dn, pd, I, H, gpe_d);
     q.dn.w_off[0] = q.dn.w_off[1] = L->geo.down_weight;
     q.dn.s_off[0] = q.dn.s_off[1] = L->geo.down_scale;
+    // one token: down and combine per row group of 8 rows (intermediate up to 2048:
+    // at most four 512-column slabs; a slot's 8 rows fit a ring slot; a group's
+    // stages fit the ring at once, since its consumers release them together)
+    const Down1 d1 = down1_plan(K, I, slot);
+    q.dn1 = OOMB_DECODE_DOWN1 && ranks == 0 && f.tb == 1 && I <= 2048 && d1.spp >= 1 && d1.nst <= stages;
     return true;
 }
 
@@ -1356,3 +1361,18 @@ extern "C" int oomb_moe_decode_fp8_noalloc(const oomb_moe_layer* layer, const vo
     return oomb_moe_decode_fp8(layer, x, x_dtype, t, out, out_dtype, ids, weights, scratch,
                                OOMB_NOALLOC_SCRATCH_BYTES, stream);
 }
+
+#ifdef OOMB_TIMELINE
+// Built only into the tracing variant of the library (python -m
+// homelab_b200.build --timeline): copies the device timeline table
+// [kinds][events][CTAs] of %globaltimer stamps to the host, or zeroes it.
+extern "C" int oomb_timeline_read(void* host, size_t bytes) {
+    if (!host || bytes > sizeof(oomb::g_timeline)) return OOMB_E_ARG;
+    return cudaMemcpyFromSymbol(host, oomb::g_timeline, bytes) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+extern "C" int oomb_timeline_clear(void) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, oomb::g_timeline) != cudaSuccess) return OOMB_E_DEVICE;
+    return cudaMemset(p, 0, sizeof(oomb::g_timeline)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+#endif

@@ -84,6 +84,7 @@ struct DecodeParams {
     // then holds this rank's epr records, gu.x the mailbox's received activations
     EpPeer ep;
     int epr;
+    int dn1;  // one token: the down phase and the combine run per row group in one CTA (down1_*)
 };
 
 // Routing tables in shared memory (byte offsets from the table area).
@@ -213,6 +214,144 @@ __device__ __forceinline__ void logits_row(const RouteParams& p, const uint8_t* 
         const float v = xor_tree32(acc);
         if (lane == 0) p.logits[static_cast<int64_t>(t) * p.E + e] = v;
     }
+}
+
+// ---- one token: down and combine per row group ----
+// With one token the step's K assignments are its K slots, one per expert.  A
+// CTA owns row groups of 8 output rows.  For each it streams the group's 8 rows
+// of every slot's down matrix (stages of `spp` slots), warp w computes the 8
+// outputs of slots w, w + kWarps, ... with the arithmetic of the stand-alone
+// down kernel (the same 16-column lane slices of 512-column slabs, block scales,
+// fp32 dot products, lane tree and slab order, so every y is bit-identical to
+// it), and the CTA combines the group's slots in slot order right away: no y
+// rows through L2, no counters between CTAs, no last-arriver hand-off.
+#ifndef OOMB_DECODE_DOWN1
+#define OOMB_DECODE_DOWN1 1
+#endif
+struct Down1 {
+    int spp, nst;  // slots per stage, stages per row group
+};
+__host__ __device__ inline Down1 down1_plan(int K, int I, int slot_bytes) {
+    Down1 d;
+    d.spp = slot_bytes / (8 * I);
+    if (d.spp > K) d.spp = K;
+    d.nst = d.spp > 0 ? (K + d.spp - 1) / d.spp : 0;
+    return d;
+}
+
+// Copy producer: row groups [g0, g1) from ring position s on.
+__device__ bool down1_copy(const StreamParams& dn, const int32_t* ids_sm, const uint64_t* recs_sm, int K,
+                           const Ring& rg, int g0, int g1, int& s, int lag) {
+    const int S = rg.stages, I = dn.k;
+    const Down1 d = down1_plan(K, I, rg.slot_bytes);
+    const unsigned rows8 = static_cast<unsigned>(8 * I);
+    const uint64_t pol = make_evict_first_policy();
+    const int s_begin = s;
+    bool ok = true;
+    for (int g = g0; g < g1 && ok; g++) {
+        for (int q = 0; q < d.nst; q++, s++) {
+            const int slot = s % S;
+            ok = mbar_wait(&rg.empty[slot], ((s / S) & 1) ^ 1, dn.err, ERR_EMPTY_WAIT);
+            if (ok && lag > 0 && lag < S && s >= lag)
+                ok = mbar_wait(&rg.full[(s - lag) % S], ((s - lag) / S) & 1, dn.err, ERR_EMPTY_WAIT);
+            if (!ok) break;
+            const int s0 = q * d.spp, ns = min(d.spp, K - s0);
+            mbar_arrive_expect_tx(&rg.full[slot], static_cast<unsigned>(ns) * rows8);
+            uint8_t* dst = rg.stage_buf + slot * rg.slot_bytes;
+            for (int i = 0; i < ns; i++) {
+                const uint8_t* rec = reinterpret_cast<const uint8_t*>(recs_sm[ids_sm[s0 + i]]);
+                bulk_g2s(dst + i * rows8, rec + dn.w_off[0] + static_cast<int64_t>(g) * rows8, rows8, &rg.full[slot],
+                         pol);
+            }
+        }
+    }
+    if (!ok) {
+        for (int t = max(s_begin, s - S); t < s; t++) mbar_wait(&rg.full[t % S], (t / S) & 1, dn.err, ERR_DRAIN_WAIT);
+    }
+    return ok;
+}
+
+// Consumers: row groups [g0, g1) from ring position pos.s on; V: partials per
+// lane (8 rows x slabs, rounded up to a power of two).  ysm: K x 8 floats.
+template <bool BLK, int V>
+__device__ bool down1_consume(const DecodeParams& p, const int32_t* ids_sm, const float* w_sm, const int32_t* slot_sm,
+                              const uint64_t* recs_sm, int K, const Ring& rg, int g0, int g1, RingPos& pos, float* ysm) {
+    const StreamParams& dn = p.dn;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = rg.stages, I = dn.k;
+    const Down1 d = down1_plan(K, I, rg.slot_bytes);
+    const int nsl = (I + 511) / 512;
+    constexpr int VS = V / 8;  // partials per row
+    const uint64_t keep = make_evict_last_policy();
+    const float* h = static_cast<const float*>(dn.x);
+    int s = pos.s;
+    for (int g = g0; g < g1; g++, s += d.nst) {
+        const int row0 = g * 8;
+        for (int si = warp; si < K; si += kWarps) {
+            const uint8_t* rec = reinterpret_cast<const uint8_t*>(recs_sm[ids_sm[si]]);
+            const float* scl = reinterpret_cast<const float*>(rec + dn.s_off[0]);
+            const int64_t hrow = static_cast<int64_t>(slot_sm[si]) * I;
+            const int q = si / d.spp, st = s + q, slot = st % S;
+            float v[V];
+#pragma unroll
+            for (int i = 0; i < V; i++) v[i] = 0.0f;
+#pragma unroll
+            for (int qs = 0; qs < VS; qs++) {
+                if (qs >= nsl) break;
+                const int col = qs * 512 + lane * 16;
+                const bool col_ok = col < I;
+                const int ccol = col_ok ? col : 0;
+                const int kb = ccol >> 7;
+                XSlice<false> xs;
+                if (col_ok) xs.load(h, hrow + col);
+                else xs.zero();
+                float sc[8];
+                if (BLK) {
+                    const float s0 = ld_scale(scl + static_cast<int64_t>(row0 >> 7) * dn.nb + kb, keep);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) sc[j] = s0;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) sc[j] = ld_scale(scl + static_cast<int64_t>(row0 + j) * dn.nb + kb, keep);
+                }
+                if (!mbar_wait(&rg.full[slot], (st / S) & 1, dn.err, ERR_FULL_WAIT)) return false;
+                const uint8_t* base = rg.stage_buf + slot * rg.slot_bytes + (si - q * d.spp) * 8 * I + ccol;
+                uint4 raw[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) raw[j] = *reinterpret_cast<const uint4*>(base + j * I);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    WDec<false> w;
+                    w.decode(raw[j]);
+                    v[j * VS + qs] = fmaf(xs.dot(w), sc[j] * xs.scale(), 0.0f);
+                }
+            }
+            warp_reduce_multi<V>(v, lane);
+            // value i's total sits in lane i * (32 / V); row j adds its slabs in slab order
+            float y = 0.0f;
+#pragma unroll
+            for (int qs = 0; qs < VS; qs++) {
+                const float t = __shfl_sync(0xffffffffu, v[0], ((lane & 7) * VS + qs) * (32 / V));
+                if (qs < nsl) y += t;
+            }
+            if (lane < 8) ysm[si * 8 + lane] = y;
+        }
+        // every warp releases every stage of the group (its producer waits for all kWarps)
+        __syncwarp();
+        if (lane == 0)
+            for (int q = 0; q < d.nst; q++) mbar_arrive(&rg.empty[(s + q) % S]);
+        consumers_sync();
+        if (threadIdx.x < 8) {
+            float acc = 0.0f;
+            for (int si = 0; si < K; si++) acc = fmaf(w_sm[si], ysm[si * 8 + threadIdx.x], acc);
+            const int64_t oi = row0 + threadIdx.x;
+            if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(acc);
+            else static_cast<float*>(p.out)[oi] = acc;
+        }
+        consumers_sync();
+    }
+    pos.s = s;
+    return true;
 }
 
 // XBF16: activations bf16 (else fp32).  BLK: 128x128 block scales.  TB, P: the
@@ -412,20 +551,24 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     const int n_e = *n_active;
     const Tables tgu{recs_active, off_sm, assign_tok, n_e, nullptr};
     const Tables tdn{recs_active, off_sm, nullptr, n_e, EP ? reinterpret_cast<const int32_t*>(tabs + dt.aret) : nullptr};
-    int gu0, gu1, dn0, dn1;
+    int gu0, gu1, dn0, dn1, g10 = 0, g11 = 0;
     cta_units(n_e, p.gu.gpe, gu0, gu1);
     cta_units(n_e, p.dn.gpe, dn0, dn1);
+    constexpr bool D1 = TB == 1 && !EP;  // one token (TB == 1 only for a one-token step)
+    if (D1 && p.dn1) cta_units(1, H / 8, g10, g11);
 
     if (warp == kWarps) {
         if (lane != 0) return;
         int s = 0;
-        if (stream_copy<2, P, true, true>(p.gu, tgu, rg, gu0, gu1, s, kDecodeLag))
-            stream_copy<1, P, true, true>(p.dn, tdn, rg, dn0, dn1, s, kDecodeLag);
+        if (stream_copy<2, P, true, true>(p.gu, tgu, rg, gu0, gu1, s, kDecodeLag)) {
+            if (D1 && p.dn1) down1_copy(p.dn, ids_sm, recs_sm, K, rg, g10, g11, s, kDecodeLag);
+            else stream_copy<1, P, true, true>(p.dn, tdn, rg, dn0, dn1, s, kDecodeLag);
+        }
         return;
     }
     if (warp == kWarps + 1) {
         int q = 0;
-        if (stream_meta<2, P, true, true>(p.gu, tgu, rg, gu0, gu1, q))
+        if (stream_meta<2, P, true, true>(p.gu, tgu, rg, gu0, gu1, q) && !(D1 && p.dn1))
             stream_meta<1, P, true, true>(p.dn, tdn, rg, dn0, dn1, q);
         return;
     }
@@ -443,6 +586,19 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         // every CTA has read the epoch: hand it to the next launch
         if (blockIdx.x == 0) st_relaxed_u32(p.sync + kSyncEpoch, epoch);
         tl_mark(TL_DOWN, TL_WAITED);
+    }
+    if constexpr (D1) {
+        if (p.dn1) {
+            // one token: down and combine per row group, then done
+            bool ok;
+            if (((p.dn.k + 511) / 512) <= 2)
+                ok = down1_consume<BLK, 16>(p, ids_sm, w_sm, slot_sm, recs_sm, K, rg, g10, g11, pos, rg.red);
+            else
+                ok = down1_consume<BLK, 32>(p, ids_sm, w_sm, slot_sm, recs_sm, K, rg, g10, g11, pos, rg.red);
+            if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
+            (void)ok;
+            return;
+        }
     }
     if (!stream_consume<1, TB, P, false, true, BLK, true, EP>(p.dn, tdn, rg, dn0, dn1, pos)) s_fail = 1;
     consumers_sync();  // the CTA's y rows are written
