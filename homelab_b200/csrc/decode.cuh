@@ -295,17 +295,13 @@ __device__ bool down1_consume(const DecodeParams& p, const int32_t* ids_sm, cons
             float v[V];
 #pragma unroll
             for (int i = 0; i < V; i++) v[i] = 0.0f;
-#pragma unroll
-            for (int qs = 0; qs < VS; qs++) {
-                if (qs >= nsl) break;
+            // the activation slice and block scales of slab qs (h rows come from L2)
+            auto load = [&](int qs, XSlice<false>& xs, float (&sc)[8]) {
                 const int col = qs * 512 + lane * 16;
                 const bool col_ok = col < I;
-                const int ccol = col_ok ? col : 0;
-                const int kb = ccol >> 7;
-                XSlice<false> xs;
+                const int kb = (col_ok ? col : 0) >> 7;
                 if (col_ok) xs.load(h, hrow + col);
                 else xs.zero();
-                float sc[8];
                 if (BLK) {
                     const float s0 = ld_scale(scl + static_cast<int64_t>(row0 >> 7) * dn.nb + kb, keep);
 #pragma unroll
@@ -314,7 +310,10 @@ __device__ bool down1_consume(const DecodeParams& p, const int32_t* ids_sm, cons
 #pragma unroll
                     for (int j = 0; j < 8; j++) sc[j] = ld_scale(scl + static_cast<int64_t>(row0 + j) * dn.nb + kb, keep);
                 }
-                if (!mbar_wait(&rg.full[slot], (st / S) & 1, dn.err, ERR_FULL_WAIT)) return false;
+            };
+            auto dot8 = [&](int qs, const XSlice<false>& xs, const float (&sc)[8]) {
+                const int col = qs * 512 + lane * 16;
+                const int ccol = col < I ? col : 0;
                 const uint8_t* base = rg.stage_buf + slot * rg.slot_bytes + (si - q * d.spp) * 8 * I + ccol;
                 uint4 raw[8];
 #pragma unroll
@@ -324,6 +323,28 @@ __device__ bool down1_consume(const DecodeParams& p, const int32_t* ids_sm, cons
                     WDec<false> w;
                     w.decode(raw[j]);
                     v[j * VS + qs] = fmaf(xs.dot(w), sc[j] * xs.scale(), 0.0f);
+                }
+            };
+            if constexpr (VS <= 2) {
+                // every slab's loads in flight before the stage wait
+                XSlice<false> xs[VS];
+                float sc[VS][8];
+#pragma unroll
+                for (int qs = 0; qs < VS; qs++)
+                    if (qs < nsl) load(qs, xs[qs], sc[qs]);
+                if (!mbar_wait(&rg.full[slot], (st / S) & 1, dn.err, ERR_FULL_WAIT)) return false;
+#pragma unroll
+                for (int qs = 0; qs < VS; qs++)
+                    if (qs < nsl) dot8(qs, xs[qs], sc[qs]);
+            } else {
+#pragma unroll
+                for (int qs = 0; qs < VS; qs++) {
+                    if (qs >= nsl) break;
+                    XSlice<false> xs;
+                    float sc[8];
+                    load(qs, xs, sc);
+                    if (!mbar_wait(&rg.full[slot], (st / S) & 1, dn.err, ERR_FULL_WAIT)) return false;
+                    dot8(qs, xs, sc);
                 }
             }
             warp_reduce_multi<V>(v, lane);

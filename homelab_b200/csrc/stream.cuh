@@ -551,6 +551,17 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
 
     XSlice<XBF16> xs[TB];
     int x_key0 = -1, x_key1 = -1;  // (expert or K-stage, first assignment) the slices hold
+    if constexpr (MOE && PARTS == 2 && TB == 1 && TSMEM) {
+        // tables in shared memory: the first unit's token is known without its pass
+        // table, so its activation slice is requested before the first table wait
+        if (u0 < u1) {
+            const int tok = tb.assign_tok[tb.off[u0 / p.gpe]];
+            if (active && col < min(p.kc, p.k)) xs[0].load(p.x, static_cast<int64_t>(tok) * p.k + col);
+            else xs[0].zero();
+            x_key0 = 0;
+            x_key1 = tok;
+        }
+    }
     int s = pos.s, q = pos.q, rparity = pos.rparity;
     bool first_meta = true, first_stage = true;
 
