@@ -114,6 +114,8 @@ SIGNATURES = [
     ("oomb_moe_down_fp8", I, [P, P, I, P, P, C.POINTER(Fp8Record), I, I, S]),
     ("oomb_moe_combine_slots", I, [P, P, P, P, I, I, I, I, S]),
     ("oomb_moe_combine", I, [P, P, P, P, I, I, S]),
+    ("oomb_moe_tiled_fp8", I, [P, P, P, I, I, P, I, P, I, I, C.c_int64, C.c_int64, I, S]),
+    ("oomb_moe_swiglu_range", I, [P, P, P, C.c_int64, C.c_int64, S]),
     ("oomb_moe_decode_workspace_bytes", Z, [I, C.POINTER(MoeLayer)]),
     ("oomb_moe_decode_fp8", I, [C.POINTER(MoeLayer), P, I, I, P, I, P, P, P, Z, S]),
     ("oomb_workspace_clear", I, [P, Z, S]),

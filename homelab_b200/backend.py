@@ -118,6 +118,22 @@ class Gpu:
                                        max_per_expert, _lib.TABLES_READY if tables_ready else 0, self._stream()),
               "moe_down")
 
+    def moe_tiled(self, recs, off, rows, n_experts: int, max_per_expert: int, x, y, n: int, k: int,
+                  proj: tuple, layout: int):
+        """y[a] = x[row(a)] . W_e^T for one projection (w_off, s_off) of every group, on the tensor
+        cores (Experts::moe_tiled, backend.rs:873-886); rows None means row(a) = a."""
+        w_off, s_off = proj
+        check(self.L.oomb_moe_tiled_fp8(_ptr(recs), _ptr(off), None if rows is None else _ptr(rows), n_experts,
+                                        max_per_expert, _ptr(x), _dtype_code(x), _ptr(y), n, k, w_off, s_off,
+                                        layout, self._stream()), "moe_tiled")
+
+    def moe_swiglu_range(self, g, u, h, start: int, end: int):
+        """h[i] = silu(g[i]) * u[i] for i in [start, end) (Experts::moe_swiglu_range, backend.rs:888)."""
+        if not (0 <= start <= end <= min(g.numel(), u.numel(), h.numel())):
+            raise ValueError("moe_swiglu_range bounds")
+        check(self.L.oomb_moe_swiglu_range(_ptr(g), _ptr(u), _ptr(h), start, end, self._stream()),
+              "moe_swiglu_range")
+
     def moe_combine_slots(self, y, slot_assign, w, out, t: int, h: int, k: int):
         """out[t] = sum_s w[t, s] * y[slot_assign[t, s]] in slot order (backend.rs:898-907)."""
         check(self.L.oomb_moe_combine_slots(_ptr(y), _ptr(slot_assign), _ptr(w), _ptr(out), _dtype_code(out),

@@ -20,6 +20,7 @@
 #include "route.cuh"
 #include "stream.cuh"
 #include "tc.cuh"
+#include "tcgroup.cuh"
 
 namespace oomb {
 namespace {
@@ -325,6 +326,48 @@ int tc_launch(int t, const TcPlan& pl, const CUtensorMap& map, const TcParams& t
     return tc_launch_t<XB, 64>(pl, map, tp, s);
 }
 
+// Grouped tensor-core plan: the chunk (assignments per unit) is the smallest of
+// 8, 16, 32, 64 that holds max_per_expert, shrunk until the rings fit one CTA
+// per SM; 512 tensor-memory columns hold nbufs accumulators of nmma columns.
+bool tg_plan(int max_per_expert, bool x_bf16, int n_experts, TgParams& tp, size_t& smem) {
+    const int ts = tc_ts(x_bf16), xb = x_bf16 ? 2 : 4;
+    const int want = max_per_expert > 0 ? max_per_expert : 64;
+    int ch = 8;
+    while (ch < want && ch < 64) ch *= 2;
+    for (; ch >= 8; ch /= 2) {
+        const int nmma = ch * ts;
+        int nbufs = kTcAccBufs;
+        while (nbufs > 2 && nbufs * nmma > 512) nbufs /= 2;
+        if (nbufs * nmma > 512) continue;
+        int cols = 32;
+        while (cols < nbufs * nmma) cols *= 2;
+        int stages = kTcMaxStages, xdepth = kTcXDepth;
+        auto total = [&](int st, int xd) { return tg_smem_bytes(st, nmma, ch, ts, xb, xd, n_experts) + 1024; };
+        while (stages > kTcSplitters && total(stages, xdepth) > kTcSmemLimit1) stages--;
+        if (total(stages, xdepth) > kTcSmemLimit1) xdepth = 1;
+        if (total(stages, xdepth) > 227 * 1024) continue;
+        tp.chunk = ch;
+        tp.nmma = nmma;
+        tp.nbufs = nbufs;
+        tp.tmem_cols = cols;
+        tp.stages = stages;
+        tp.xdepth = xdepth;
+        smem = total(stages, xdepth);
+        return true;
+    }
+    return false;
+}
+
+template <bool XB>
+int tg_launch(const TgParams& tp, int grid, size_t smem, cudaStream_t s) {
+    switch (tp.chunk) {
+        case 8: return launch(tc_group_kernel<XB, 8>, dim3(grid), dim3(kTcThreads), smem, s, tp);
+        case 16: return launch(tc_group_kernel<XB, 16>, dim3(grid), dim3(kTcThreads), smem, s, tp);
+        case 32: return launch(tc_group_kernel<XB, 32>, dim3(grid), dim3(kTcThreads), smem, s, tp);
+        default: return launch(tc_group_kernel<XB, 64>, dim3(grid), dim3(kTcThreads), smem, s, tp);
+    }
+}
+
 
 // The one-launch decode (decode.cuh) for up to kDecodeMaxT tokens and routers of
 // at most kRouteSmallE experts: its plan, or false when the layer or batch is
@@ -552,6 +595,53 @@ int oomb_gemm_fp8_tc(const void* x, int x_dtype, const uint8_t* q, int q_format,
     tp.tmem_cols = pl.tmem_cols;
     tp.err = d->err;
     return x_dtype == OOMB_BF16 ? tc_launch<true>(t, pl, map, tp, stream) : tc_launch<false>(t, pl, map, tp, stream);
+}
+
+int oomb_moe_tiled_fp8(const uint64_t* recs, const int32_t* off, const int32_t* rows, int n_experts,
+                       int max_per_expert, const void* x, int x_dtype, float* y, int n, int k, int64_t w_off,
+                       int64_t s_off, int scale_layout, oomb_stream stream) {
+    if (!recs || !off || !x || !y) return OOMB_E_ARG;
+    if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) ||
+        (scale_layout != OOMB_SCALE_1X128 && scale_layout != OOMB_SCALE_128X128) || max_per_expert < 0)
+        return OOMB_E_ARG;
+    if (n <= 0 || k <= 0 || n % kTcTile || k % kTcTile || n_experts < 0 || n_experts > kTgMaxExperts)
+        return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(y) || (w_off & 15) || (s_off & 3) || w_off < 0 || s_off < 0)
+        return OOMB_E_ALIGN;
+    if (n_experts == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    TgParams tp{};
+    size_t smem = 0;
+    if (!tg_plan(max_per_expert, x_dtype == OOMB_BF16, n_experts, tp, smem)) return OOMB_E_SHAPE;
+    tp.recs = recs;
+    tp.off = off;
+    tp.rows = rows;
+    tp.n_experts = n_experts;
+    tp.x = x;
+    tp.K = k;
+    tp.N = n;
+    tp.w_off = w_off;
+    tp.s_off = s_off;
+    tp.layout = scale_layout;
+    tp.y = y;
+    tp.rblocks = n / kTcTile;
+    tp.kblocks = k / kTcTile;
+    tp.err = d->err;
+    return x_dtype == OOMB_BF16 ? tg_launch<true>(tp, d->sms, smem, stream)
+                                : tg_launch<false>(tp, d->sms, smem, stream);
+}
+
+int oomb_moe_swiglu_range(const float* g, const float* u, float* h, int64_t start, int64_t end,
+                          oomb_stream stream) {
+    if (!g || !u || !h) return OOMB_E_ARG;
+    if (start < 0 || end < start) return OOMB_E_SHAPE;
+    if (start == end) return OOMB_OK;
+    if (!device_state()) return OOMB_E_DEVICE;
+    const int64_t blocks = (end - start + 255) / 256;
+    if (blocks > 0x7fffffff) return OOMB_E_SHAPE;
+    return launch(swiglu_range_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, g, u, h, start,
+                  end);
 }
 
 

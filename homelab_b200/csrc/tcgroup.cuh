@@ -1,0 +1,427 @@
+// tcgroup.cuh - grouped FP8 expert GEMM on the 5th-generation tensor cores: the
+// large-step path of the routed experts (the reference's moe_tiled,
+// crates/oominf-cuda/kernels/moe.cu:204-335, launched from Moe::run_group,
+// crates/oominf-models-qwen/src/moe.rs:650,746-758).
+//
+// One projection per launch, over every group of a CSR grouping:
+//   y[a, r] = sum_k x[row(a), k] * e4m3(W_e[r, k]) * scale_e(r, k)
+// for a in [off[e], off[e+1]), row(a) = rows ? rows[a] : a, W_e the e4m3
+// matrix [N, K] at byte offset w_off of record recs[e] and scale_e its fp32
+// block scales at s_off (1x128 or 128x128).  fp32 accumulation, fp32 y [A, N].
+//
+// Work units are (group chunk, 128-row block): every group is cut into chunks
+// of at most CH assignments, and the units are spread over a persistent grid
+// (CTA b takes units b, b + grid, ...), each unit's K blocks in order inside one
+// CTA - no split-K fix-up.  Units of one row block of one expert are
+// consecutive, so the CTAs working at the same time read the same weight tiles
+// and the chunks after the first find them in L2.
+//
+// The arithmetic is the dense tensor-core kernel's (tc.cuh): a chunk's
+// activations are split exactly into e4m3 terms with power-of-two scales
+// (two terms for bf16 x, four for fp32 x), each (assignment, term) one column of
+// the B operand; tcgen05.mma (kind::f8f6f4, M = 128, K = 32) accumulates one K
+// block per tensor-memory buffer and the epilogue folds
+//   acc = fma(w_scale, sum_term s_term * D_term, acc)
+// K blocks in order.  The MMA's N is the chunk's own column count (rounded up
+// to 16), so a chunk of 4 assignments costs a 16-column MMA.
+//
+// Weights: records live at arbitrary addresses (resident, staged or received),
+// so no tensor map can name them.  The copy warp moves each 128 x 128 weight
+// tile with 16-byte cp.async straight into the 128-byte swizzled K-major layout
+// the MMA reads (every lane 32 chunks of 16 bytes: 4 rows of 128 bytes per warp
+// instruction, coalesced), commits one group per tile and releases a tile to the
+// MMA kTgLag tiles later, after cp.async.wait_group and a proxy fence.
+//
+// Warp roles (10 warps): 0 weight copies, 1 MMA issuer and tensor-memory owner,
+// 2-5 epilogue, 6-9 activation splitters (tile j to splitter j % 4).  Every wait
+// is bounded and records an error code.
+#pragma once
+
+#include "tc.cuh"
+
+namespace oomb {
+
+constexpr int kTgMaxExperts = 4096;  // groups per launch (their chunk prefix sits in shared memory)
+constexpr int kTgLag = 3;            // weight tiles in flight before the oldest is released (< stages)
+
+enum : unsigned {
+    ERR_TG_WAIT = 0x580,  // a grouped tensor-core pipeline wait ran out (+ the waiting role)
+};
+
+struct TgParams {
+    const uint64_t* recs;  // [n_experts] record addresses
+    const int32_t* off;    // [n_experts + 1] CSR offsets of the groups
+    const int32_t* rows;   // [A] activation row of each assignment, or null (row = assignment)
+    int n_experts;
+    const void* x;         // [*, K] bf16 or fp32
+    int K, N;
+    int64_t w_off, s_off;  // byte offsets of the projection's e4m3 weights and fp32 scales in a record
+    int layout;            // OOMB_SCALE_1X128 (0) or OOMB_SCALE_128X128 (1)
+    float* y;              // [A, N] fp32
+    int chunk;             // assignments per unit (the kernel's CH)
+    int rblocks, kblocks;  // N / 128, K / 128
+    int nmma;              // B columns per stage, and the accumulator stride in tensor memory
+    int stages, nbufs, xdepth, tmem_cols;
+    unsigned* err;
+};
+
+// Shared memory: the dense kernel's layout for T = CH, then the chunk prefix.
+__host__ __device__ inline size_t tg_smem_bytes(int stages, int nmma, int ch, int ts, int xbytes, int xdepth,
+                                                int n_experts) {
+    const TcSmem m = tc_smem(stages, nmma, ch, ts, xbytes, xdepth);
+    return ((m.total + 15) & ~static_cast<size_t>(15)) + 4 * static_cast<size_t>(n_experts + 1);
+}
+
+struct TgUnit {
+    int e, rb, a0, nt;
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool XBF16, int CH>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams p) {
+    constexpr int TS = tc_ts(XBF16), TERMS = tc_terms(XBF16);
+    constexpr int XB = XBF16 ? 2 : 4;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const TcSmem L = tc_smem(p.stages, p.nmma, CH, TS, XB, p.xdepth);
+    uint8_t* a_ring = smem + L.a_off;
+    uint8_t* b_ring = smem + L.b_off;
+    uint8_t* x_ring = smem + L.x_off;
+    float* sx_ring = reinterpret_cast<float*>(smem + L.sx_off);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = bars + kTcMaxStages;
+    uint64_t* b_full = bars + 2 * kTcMaxStages;
+    uint64_t* b_empty = bars + 3 * kTcMaxStages;
+    uint64_t* x_full = bars + 4 * kTcMaxStages;  // [splitter][x slot]
+    uint64_t* mma_done = bars + (4 + kTcSplitters) * kTcMaxStages;
+    uint64_t* tmem_empty = mma_done + kTcAccBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + kTcAccBufs);
+    int* cs = reinterpret_cast<int*>(smem + ((L.total + 15) & ~static_cast<size_t>(15)));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = p.stages, KB = p.kblocks;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) {
+            mbar_init(&a_full[i], 1);
+            mbar_init(&a_empty[i], 1);
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 4);
+            for (int w = 0; w < kTcSplitters; w++) mbar_init(&x_full[w * kTcMaxStages + i], 1);
+        }
+        for (int i = 0; i < p.nbufs; i++) {
+            mbar_init(&mma_done[i], 1);
+            mbar_init(&tmem_empty[i], 4);
+        }
+        fence_barrier_init();
+    }
+    // B columns a chunk does not fill keep whatever an earlier chunk left there:
+    // an MMA column only feeds its own accumulator column, which no epilogue reads
+    for (int i = threadIdx.x; i < S * p.nmma * 32; i += kTcThreads) reinterpret_cast<uint32_t*>(b_ring)[i] = 0u;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // the grouping (off, rows) and the activations may come from the previous kernel
+    pdl_wait();
+    if (warp == 0) {
+        // cs[e] = chunks of the groups before e (exclusive prefix), cs[n_experts] = all chunks
+        const int E = p.n_experts, per = (E + 31) / 32;
+        const int e0 = min(E, lane * per), e1 = min(E, e0 + per);
+        int mine = 0;
+        for (int e = e0; e < e1; e++) {
+            const int c = __ldg(p.off + e + 1) - __ldg(p.off + e);
+            mine += c > 0 ? (c + p.chunk - 1) / p.chunk : 0;
+        }
+        int incl = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - mine;
+        for (int e = e0; e < e1; e++) {
+            cs[e] = run;
+            const int c = __ldg(p.off + e + 1) - __ldg(p.off + e);
+            run += c > 0 ? (c + p.chunk - 1) / p.chunk : 0;
+        }
+        if (lane == 31) cs[E] = incl;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_launch_dependents();
+
+    const int grid = gridDim.x;
+    const int units = cs[p.n_experts] * p.rblocks;
+    const int my_units = static_cast<int>(blockIdx.x) < units ? (units - static_cast<int>(blockIdx.x) + grid - 1) / grid : 0;
+    const int ntiles = my_units * KB;
+    // the unit of this CTA's j-th tile
+    auto unit_of = [&](int j) {
+        const int u = static_cast<int>(blockIdx.x) + (j / KB) * grid;
+        const int g = u / p.rblocks;
+        int lo = 0, hi = p.n_experts;  // cs[lo] <= g < cs[hi]
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (cs[mid] <= g) lo = mid;
+            else hi = mid;
+        }
+        TgUnit U;
+        U.e = lo;
+        U.rb = u - g * p.rblocks;
+        U.a0 = __ldg(p.off + lo) + (g - cs[lo]) * p.chunk;
+        U.nt = min(p.chunk, __ldg(p.off + lo + 1) - U.a0);
+        return U;
+    };
+
+    if (warp == 0) {
+        // ================= weight copies: 16-byte cp.async into the swizzled ring =================
+        int j = 0;
+        const uint8_t* wrow = nullptr;
+        for (; j < ntiles; j++) {
+            const int s = j % S, it = j / S, kb = j % KB;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&a_empty[s], (it & 1) ^ 1, p.err, ERR_TG_WAIT + 1);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            if (kb == 0) {
+                const TgUnit U = unit_of(j);
+                wrow = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(p.recs) + U.e)) +
+                       p.w_off + static_cast<int64_t>(U.rb) * kTcTile * p.K;
+                if (reinterpret_cast<uintptr_t>(wrow) & 15u) {
+                    // a record address the 16-byte copies cannot take: skip the work, report it
+                    if (lane == 0) record_error(p.err, ERR_BAD_TABLE);
+                    break;
+                }
+            }
+            uint8_t* dst = a_ring + s * kTcTileBytes;
+            const uint8_t* src = wrow + kb * kTcTile;
+#pragma unroll 8
+            for (int i = 0; i < kTcTileBytes / 16 / 32; i++) {
+                const int q = lane + 32 * i, r = q >> 3, c = (q & 7) * 16;
+                cp_async16(dst + sw128_offset(r, c), src + static_cast<int64_t>(r) * p.K + c);
+            }
+            cp_async_commit();
+            if (j >= kTgLag) {
+                // tile j - kTgLag has landed for this lane; make it visible to the tensor cores
+                cp_async_wait<kTgLag>();
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[(j - kTgLag) % S]);
+            }
+        }
+        cp_async_wait<0>();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0)
+            for (int i = j > kTgLag ? j - kTgLag : 0; i < j; i++) mbar_arrive(&a_full[i % S]);
+    } else if (warp >= 6) {
+        // ================= activation splitters: B tiles and their term scales =================
+        constexpr int SG = CH < kTcSplitGroup ? CH : kTcSplitGroup;
+        const int sw = warp - 6, XD = p.xdepth;
+        uint64_t* xf = x_full + sw * kTcMaxStages;
+        uint8_t* xr = x_ring + static_cast<size_t>(sw) * XD * L.x_stage;
+        auto fetch = [&](int m) {
+            const int j = sw + m * kTcSplitters;
+            if (j >= ntiles) return;
+            const TgUnit U = unit_of(j);
+            const int slot = m % XD, kb = j % KB;
+            if (lane == 0) mbar_arrive_expect_tx(&xf[slot], static_cast<unsigned>(U.nt * kTcTile * XB));
+            __syncwarp();
+            for (int t = lane; t < U.nt; t += 32) {
+                const int row = p.rows ? __ldg(p.rows + U.a0 + t) : U.a0 + t;
+                const uint8_t* src = static_cast<const uint8_t*>(p.x) +
+                                     (static_cast<int64_t>(row) * p.K + static_cast<int64_t>(kb) * kTcTile) * XB;
+                bulk_g2s_plain(xr + slot * L.x_stage + t * kTcTile * XB, src, kTcTile * XB, &xf[slot]);
+            }
+        };
+        for (int m = 0; m < XD; m++) fetch(m);
+        for (int m = 0; sw + m * kTcSplitters < ntiles; m++) {
+            const int j = sw + m * kTcSplitters;
+            const int s = j % S, it = j / S;
+            const int nt = unit_of(j).nt;
+            if (!mbar_wait(&b_empty[s], (it & 1) ^ 1, p.err, ERR_TG_WAIT + 2)) break;
+            if (!mbar_wait(&xf[m % XD], (m / XD) & 1, p.err, ERR_TG_WAIT + 7)) break;
+            uint8_t* bt = b_ring + s * p.nmma * 128;
+            float* sx = sx_ring + s * CH * TS;
+            const uint8_t* xs = xr + (m % XD) * L.x_stage;
+            for (int g = 0; g < nt; g += SG) {
+                // lane l holds columns 4l .. 4l+3 of assignments g .. g+SG-1 of the chunk
+                float v[SG][4];
+#pragma unroll
+                for (int u = 0; u < SG; u++) {
+                    const int t = g + u;
+                    if (t < nt) {
+                        if (XBF16) {
+                            const uint2 w = *reinterpret_cast<const uint2*>(xs + (t * kTcTile + lane * 4) * 2);
+                            v[u][0] = __uint_as_float(w.x << 16);
+                            v[u][1] = __uint_as_float(w.x & 0xffff0000u);
+                            v[u][2] = __uint_as_float(w.y << 16);
+                            v[u][3] = __uint_as_float(w.y & 0xffff0000u);
+                        } else {
+                            const float4 w = *reinterpret_cast<const float4*>(xs + (t * kTcTile + lane * 4) * 4);
+                            v[u][0] = w.x;
+                            v[u][1] = w.y;
+                            v[u][2] = w.z;
+                            v[u][3] = w.w;
+                        }
+                    } else {
+                        v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int term = 0; term < TERMS; term++) {
+                    float mx[SG];
+#pragma unroll
+                    for (int u = 0; u < SG; u++)
+                        mx[u] = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                        for (int u = 0; u < SG; u++) mx[u] = fmaxf(mx[u], __shfl_xor_sync(0xffffffffu, mx[u], o));
+#pragma unroll
+                    for (int u = 0; u < SG; u++) {
+                        const int t = g + u;
+                        if (t < nt) {
+                            float inv;
+                            const float sc = tc_term_scale(mx[u], inv);
+                            const uint32_t lo2 = e4m3x2_from_f32(v[u][0] * inv, v[u][1] * inv);
+                            const uint32_t hi2 = e4m3x2_from_f32(v[u][2] * inv, v[u][3] * inv);
+                            *reinterpret_cast<uint32_t*>(bt + sw128_offset(t * TS + term, lane * 4)) =
+                                lo2 | (hi2 << 16);
+                            if (lane == 0) sx[t * TS + term] = sc;
+                            if (term + 1 < TERMS) {
+                                // exact residual: q * sc carries at most 4 significant bits
+                                const float2 a = e4m3x2_to_float2(static_cast<unsigned short>(lo2));
+                                const float2 b = e4m3x2_to_float2(static_cast<unsigned short>(hi2));
+                                v[u][0] -= a.x * sc;
+                                v[u][1] -= a.y * sc;
+                                v[u][2] -= b.x * sc;
+                                v[u][3] -= b.y * sc;
+                            }
+                        }
+                    }
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            fetch(m + XD);
+            if (lane == 0) mbar_arrive(&b_full[s]);
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer =================
+        if (lane == 0) {
+            int nt = 0;
+            for (int j = 0; j < ntiles; j++) {
+                const int s = j % S, it = j / S;
+                const int buf = j % p.nbufs, use = j / p.nbufs;
+                if (j % KB == 0) nt = unit_of(j).nt;
+                const int n = (nt * TS + 15) / 16 * 16;  // this chunk's columns, a valid MMA N (16..nmma)
+                if (!mbar_wait(&a_full[s], it & 1, p.err, ERR_TG_WAIT + 3)) break;
+                if (!mbar_wait(&b_full[s], it & 1, p.err, ERR_TG_WAIT + 4)) break;
+                if (!mbar_wait(&tmem_empty[buf], (use & 1) ^ 1, p.err, ERR_TG_WAIT + 5)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(a_ring + s * kTcTileBytes);
+                const uint32_t b_addr = smem_addr(b_ring + s * p.nmma * 128);
+                const uint32_t d = tmem_base + static_cast<uint32_t>(buf * p.nmma);
+                const uint32_t idesc = tc_idesc(n);
+#pragma unroll
+                for (int k = 0; k < kTcKSteps; k++)
+                    tc_mma(d, tc_smem_desc(a_addr + 32 * k), tc_smem_desc(b_addr + 32 * k), idesc, k > 0);
+                tc_commit(&a_empty[s]);
+                tc_commit(&mma_done[buf]);
+            }
+        }
+    } else {
+        // ================= epilogue warpgroup (warps 2..5) =================
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;  // row of the tile this thread owns
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        float acc[CH];
+#pragma unroll
+        for (int t = 0; t < CH; t++) acc[t] = 0.0f;
+        TgUnit U{};
+        const float* sp = nullptr;
+        for (int j = 0; j < ntiles; j++) {
+            const int s = j % S, buf = j % p.nbufs, kb = j % KB;
+            if (kb == 0) {
+                U = unit_of(j);
+                sp = reinterpret_cast<const float*>(
+                    reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(p.recs) + U.e)) +
+                    p.s_off);
+            }
+            // the weight scale of this thread's row for this K block (its load overlaps the wait)
+            const float ws = p.layout ? __ldg(sp + static_cast<int64_t>(U.rb) * KB + kb)
+                                      : __ldg(sp + static_cast<int64_t>(U.rb * kTcTile + r) * KB + kb);
+            if (!mbar_wait(&mma_done[buf], (j / p.nbufs) & 1, p.err, ERR_TG_WAIT + 6)) break;
+            tc_fence_after();
+            const float* sx = sx_ring + s * CH * TS;
+#pragma unroll
+            for (int c0 = 0; c0 < CH * TS; c0 += 8) {
+                if (c0 < U.nt * TS) {
+                    float d[8];
+                    tc_ld8(tmem_base + lane_base + static_cast<uint32_t>(buf * p.nmma + c0), d);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 8; q += TS) {
+                        const int t = (c0 + q) / TS;
+                        if (t < U.nt) {
+                            float u = sx[t * TS] * d[q];
+#pragma unroll
+                            for (int term = 1; term < TERMS; term++) u = __fadd_rn(u, sx[t * TS + term] * d[q + term]);
+                            acc[t] = fmaf(ws, u, acc[t]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&tmem_empty[buf]);
+                mbar_arrive(&b_empty[s]);
+            }
+            if (kb == KB - 1) {
+#pragma unroll
+                for (int t = 0; t < CH; t++) {
+                    if (t < U.nt) p.y[static_cast<int64_t>(U.a0 + t) * p.N + U.rb * kTcTile + r] = acc[t];
+                    acc[t] = 0.0f;
+                }
+            }
+        }
+    }
+    // the copy-side roles ran on lane 0 alone in places: reconverge before the CTA barrier
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.tmem_cols)
+                     : "memory");
+    }
+}
+
+// h[i] = silu(g[i]) * u[i] for i in [start, end), silu(v) = v / (1 + exp(-v)):
+// the reference's moe_swiglu (moe.cu:335-339) between the tiled gate and up
+// projections and the tiled down projection.
+__global__ void swiglu_range_kernel(const float* g, const float* u, float* h, int64_t start, int64_t end) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t i = start + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= end) return;
+    const float v = __ldcg(g + i);
+    h[i] = v / (1.0f + expf(-v)) * __ldcg(u + i);
+}
+
+}  // namespace oomb

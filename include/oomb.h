@@ -182,6 +182,28 @@ int oomb_moe_combine_slots(const float* y, const int32_t* slot_assign, const flo
 int oomb_moe_combine(const float* routed, const float* shared, const float* gate_logit,
                      float* out, int t, int h, oomb_stream stream);
 
+/* Grouped FP8 expert GEMM on the tensor cores (tcgen05) for large steps:
+ * y[a, :] = x[row(a), :] . W_e^T for every assignment a of group e (a in
+ * [off[e], off[e+1])), row(a) = rows[a], or a when rows is NULL; W_e the e4m3
+ * matrix [n, k] at byte offset w_off of record recs[e], its fp32 block scales
+ * (scale_layout) at s_off.  Replaces Experts::moe_tiled (backend.rs:873-886;
+ * crates/oominf-cuda/src/experts.rs:211-266; moe.cu:204-335) for FP8 records:
+ * the projection (w_off, s_off, s2_idx) becomes (w_off, s_off, scale_layout),
+ * and the result is the Exact precision's (activations split exactly into
+ * e4m3 terms: bf16 x exact, fp32 x to 16 significant bits; fp32 accumulate).
+ * x: [*, k] fp32 or bf16; y: [A, n] fp32.  n, k multiples of 128; n_experts <=
+ * 4096; w_off % 16 == 0.  max_per_expert picks the chunk size (assignments per
+ * MMA, <= 64); any group size is correct, 0 if unknown. */
+int oomb_moe_tiled_fp8(const uint64_t* recs, const int32_t* off, const int32_t* rows, int n_experts,
+                       int max_per_expert, const void* x, int x_dtype, float* y, int n, int k,
+                       int64_t w_off, int64_t s_off, int scale_layout, oomb_stream stream);
+
+/* h[i] = silu(g[i]) * u[i] for i in [start, end), silu(v) = v / (1 + exp(-v)).
+ * Replaces Experts::moe_swiglu_range (backend.rs; experts.rs:269-297;
+ * moe.cu:337-341), the step between the tiled gate/up and down projections. */
+int oomb_moe_swiglu_range(const float* g, const float* u, float* h, int64_t start, int64_t end,
+                          oomb_stream stream);
+
 /* ---- fused decode step of one resident MoE layer ------------------------ */
 /* Router GEMV, softmax top-k, grouping of the step's assignments by expert
  * (expert order, slots in slot order: Moe::begin_routed / finish_routed,
