@@ -24,6 +24,9 @@ e2e     the same through the public C ABI with host buffers, inside the timed
 roofline  the dominant kernel (gate/up+SiLU), timed in its own loop of
         back-to-back launches with CUDA events, against the measured HBM copy
         bandwidth of MEASURED_PEAKS.json.
+grouped_experts_config5  config 5's routed experts (hidden 4096, 256 experts,
+        top-8, intermediate 2048) at batches 32 / 128 / 1024: the tensor-core
+        grouped GEMM against the CUDA-core expert kernels on the same routing.
 cpu_baseline  the reference's host expert path restated in C++ with AVX-512
         (oracle/cpu_baseline.cpp) on this box's host cores, rank 0, N=1 only.
 
@@ -70,6 +73,9 @@ def parse():
                     help="run N eager decode steps of the workload and exit (a small driver for ncu)")
     ap.add_argument("--profile-mlp", type=int, default=0, metavar="B",
                     help="with --profile: run N config-3 MLP steps at batch B instead (tensor-core path)")
+    ap.add_argument("--profile-tiled", type=int, default=0, metavar="B",
+                    help="with --profile: run N grouped tensor-core expert steps (config-5 shapes, 32 experts) "
+                         "at batch B instead")
     return ap.parse_args()
 
 
@@ -236,6 +242,13 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     gpu = Gpu(local_rank)
     B = args.batch
+    if args.profile and args.profile_tiled:
+        # a small ncu driver: the 32-expert grouped case alone (805 MB of records)
+        measure_experts_config5(gpu, dev, torch.cuda.current_stream(dev), batches=(args.profile_tiled,),
+                                steps=args.profile, experts=32, forms=("tcgen05_grouped",), warm=0)
+        torch.cuda.synchronize()
+        assert gpu.device_error() == 0
+        return None, None
 
     # ---- weights: 8 layer replicas; with N > 1 every rank holds E/N of each layer's experts ----
     LAYERS = args.layers
@@ -419,6 +432,7 @@ def run_ours(args, rank, world, local_rank):
     del layers
     torch.cuda.empty_cache()
     mlp3 = measure_mlp_config3(gpu, dev, s) if world == 1 else None
+    experts5 = measure_experts_config5(gpu, dev, s) if world == 1 else None
     staging = measure_staging(dev) if world == 1 else None
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
@@ -446,6 +460,7 @@ def run_ours(args, rank, world, local_rank):
                              "achieved_gbs": gemv1["gbs"], "frac": gemv1["gbs"] / peak, "launch_us": gemv1["us"],
                              "algorithmic_bytes_per_launch": gemv1["bytes"]},
             "batched_dense_config3": mlp3,
+            "grouped_experts_config5": experts5,
             "offload_staging_config5": staging,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
@@ -616,6 +631,81 @@ def measure_mlp_config3(gpu, dev, s, batches=(1, 4, 16, 64), steps=24):
         out[f"B{B}"] = {"us_per_mlp": us, "tokens_per_s": B / (us * 1e-6), "gbs": nbytes / (us * 1e-6) / 1e9,
                         "path": "tcgen05" if B >= 2 else "cuda-core stream"}
         del g
+    return out
+
+
+def measure_experts_config5(gpu, dev, s, batches=(32, 128, 1024), steps=6, experts=256,
+                            forms=("tcgen05_grouped", "cuda_core"), warm=3):
+    """BASELINE config 5's routed experts on one GPU: hidden 4096, 256 experts, top-8,
+    intermediate 2048, 128x128 scales (6.44 GB of records, beyond L2 many times).
+    Per batch, one seeded routing (grouped by expert as Moe::finish_routed does) and
+    two step forms over it: the CUDA-core expert kernels (oomb_moe_gate_up_fp8 +
+    oomb_moe_down_fp8) and the tensor-core grouped GEMM (oomb_moe_tiled_fp8 for gate,
+    up and down + oomb_moe_swiglu_range, the order of Moe::run_group's tiled branch)."""
+    import numpy as np
+    import torch
+
+    import homelab_b200 as hb
+    from homelab_b200.records import ExpertBank
+    H, I, E, K = 4096, 2048, experts, 8
+    bank = ExpertBank(E, H, I, hb.SCALE_128X128, dev)
+    bank.fill_random(gpu, seed=29)
+    torch.cuda.synchronize()
+    g = bank.geo
+    rec_bytes = 3 * H * I + 3 * (H // 128) * (I // 128) * 4
+    rng = np.random.default_rng(31)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(37)
+    out = {}
+    for B in batches:
+        ids = np.argsort(rng.standard_normal((B, E)), axis=1)[:, :K].astype(np.int32)
+        flat = ids.reshape(-1)
+        order = np.argsort(flat, kind="stable")
+        active, counts = np.unique(flat, return_counts=True)
+        off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+        tok = (order // K).astype(np.int32)
+        A, n_e, maxn = B * K, len(active), int(counts.max())
+        recs = bank.addrs[torch.from_numpy(active).long().to(dev)].contiguous()
+        offd = torch.from_numpy(off).to(dev)
+        tokd = torch.from_numpy(tok).to(dev)
+        x = torch.randn((B, H), generator=gen, device=dev).to(torch.bfloat16)
+        gg = torch.empty((A, I), dtype=torch.float32, device=dev)
+        uu = torch.empty_like(gg)
+        hh = torch.empty_like(gg)
+        y = torch.empty((A, H), dtype=torch.float32, device=dev)
+
+        def tiled():
+            gpu.moe_tiled(recs, offd, tokd, n_e, maxn, x, gg, I, H, (g.gate_weight, g.gate_scale), g.layout)
+            gpu.moe_tiled(recs, offd, tokd, n_e, maxn, x, uu, I, H, (g.up_weight, g.up_scale), g.layout)
+            gpu.moe_swiglu_range(gg, uu, hh, 0, A * I)
+            gpu.moe_tiled(recs, offd, None, n_e, maxn, hh, y, H, I, (g.down_weight, g.down_scale), g.layout)
+
+        def cuda_cores():
+            gpu.moe_gate_up(recs, offd, tokd, n_e, x, hh, g, maxn)
+            gpu.moe_down(recs, offd, n_e, hh, y, g, maxn)
+
+        res = {"assignments": A, "distinct_experts": n_e, "max_per_expert": maxn}
+        for name, fn in (("tcgen05_grouped", tiled), ("cuda_core", cuda_cores)):
+            if name not in forms:
+                continue
+            with torch.cuda.stream(s):
+                for _ in range(warm):
+                    fn()
+                s.synchronize()
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record(s)
+                for _ in range(steps):
+                    fn()
+                ev1.record(s)
+            ev1.synchronize()
+            us = ev0.elapsed_time(ev1) / steps * 1e3
+            res[name] = {"us_per_step": us, "tokens_per_s": B / (us * 1e-6),
+                         "weight_gbs": n_e * rec_bytes / (us * 1e-6) / 1e9,
+                         "tflops": 2.0 * A * 3 * H * I / (us * 1e-6) / 1e12}
+        out[f"B{B}"] = res
+        del gg, uu, hh, y
+    del bank
+    torch.cuda.empty_cache()
     return out
 
 
