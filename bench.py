@@ -21,17 +21,26 @@ e2e     the same through the public C ABI with host buffers, inside the timed
         the host buffers itself (a staging kernel reads x over the bus after the
         previous step, the step stores out into host memory); expert-parallel
         ranks copy in and out with stream-ordered copies.
-roofline  the dominant kernel (gate/up+SiLU), timed in its own loop of
-        back-to-back launches with CUDA events, against the measured HBM copy
-        bandwidth of MEASURED_PEAKS.json.
+roofline  the dominant kernel: at N = 1 and B <= 16 the whole step is one
+        decode_kernel launch, so its algorithmic bytes over the device-timed
+        step give the achieved bandwidth, against the measured HBM copy
+        bandwidth of MEASURED_PEAKS.json; gate_up_kernel and gemv_config1 time
+        the stand-alone gate/up and dense GEMV kernels in back-to-back launches.
 grouped_experts_config5  config 5's routed experts (hidden 4096, 256 experts,
         top-8, intermediate 2048) at batches 32 / 128 / 1024: the tensor-core
         grouped GEMM against the CUDA-core expert kernels on the same routing.
 cpu_baseline  the reference's host expert path restated in C++ with AVX-512
-        (oracle/cpu_baseline.cpp) on this box's host cores, rank 0, N=1 only.
+        (oracle/cpu_baseline.cpp) on this box's host cores (all of them, and one
+        thread), rank 0, N=1 only; the CPU model is reported beside it.
 
-With N > 1 (torchrun) every rank runs its own replica of the workload
-(weak scaling, no collective on the data path) and rank 0 prints one line.
+With N > 1 (torchrun) the experts of every layer are sharded over the ranks
+(expert parallelism, expert e on rank e / (E / N)); each rank decodes its own
+batch of tokens (weak scaling), dispatching every token's slots to the ranks
+that own their experts and taking the outputs back.  By default each rank runs
+the whole step as one kernel launch whose dispatch and return are stores into
+the peers' mailboxes over NVLink (--ep-step fused); --ep-step chain runs it as
+a chain of kernels, --ep-transport nccl with NCCL all-to-alls.  Rank 0 prints
+one line; times are the max over ranks.
 """
 from __future__ import annotations
 
@@ -64,7 +73,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel all-to-alls: kernels storing into peer mailboxes over NVLink, or NCCL")
-    ap.add_argument("--ep-step", choices=["chain", "fused"], default="chain",
+    ap.add_argument("--ep-step", choices=["chain", "fused"], default="fused",
                     help="with peer transport: the chain of kernels, or one launch per rank and step")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU work of the cpu_baseline / reference sample")
@@ -79,10 +88,23 @@ def parse():
     return ap.parse_args()
 
 
-def config_dict(batch, layers=LAYERS):
+def config_dict(batch, layers=LAYERS, world=1):
+    """The workload's keys, identical for both arms."""
     return {"workload": WORKLOAD, "hidden": H, "experts": E, "top_k": K_TOP, "inter": I,
             "batch_per_gpu": batch, "scale_blocks": "128x128", "layers_rotated": layers,
-            "l2": f"inputs larger than L2: each step reads a different layer's experts ({layers} x 604 MB)"}
+            "l2": f"inputs larger than L2: each step reads a different layer's experts ({layers} x 604 MB)",
+            "parallelism": f"ep{world}" if world > 1 else "single"}
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def load_peaks():
@@ -212,15 +234,18 @@ def run_reference(args, rank, world):
         return
     steps = args.steps
     per, threads, sample, n = time_cpu(args.batch, args.cpu_seconds)
+    per1, _, sample1, _ = time_cpu(args.batch, args.cpu_seconds / 3, threads=1)
     tok_s = args.batch / per
     line = {
         "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(args.batch),
+        "config": config_dict(args.batch, LAYERS, world),
         "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "cpu_model": cpu_model(), "value_1_thread": args.batch / per1,
                          "sample": sample + "; the reference's host expert path (oominf-cpu) restated in "
-                                             "C++ with AVX-512, FP8 decode, whole layer on the CPU"},
+                                             "C++ with AVX-512, FP8 decode, whole layer on the CPU; one thread: "
+                                   + sample1},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -443,7 +468,7 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(config_dict(B, LAYERS), parallelism=f"ep{world}" if world > 1 else "single",
+            "config": dict(config_dict(B, LAYERS, world),
                            **({"expert_parallel": f"{E // world} experts per GPU, " + (
                                ("one launch per rank and step: " if args.ep_step == "fused" and B <= 16 else
                                 "chain of kernels: ") + "dispatch and return stored by the kernels into peer "
@@ -804,9 +829,11 @@ def main():
         return
     if rank == 0 and world == 1 and not args.no_cpu:
         per, threads, sample, _ = time_cpu(args.batch, args.cpu_seconds)
+        per1, _, sample1, _ = time_cpu(args.batch, args.cpu_seconds / 3, threads=1)
         result["cpu_baseline"] = {"value": args.batch / per, "unit": "tokens/s", "cores": threads,
-                                  "kind": "port",
-                                  "sample": sample + "; oominf-cpu host expert path restated in C++/AVX-512"}
+                                  "kind": "port", "cpu_model": cpu_model(), "value_1_thread": args.batch / per1,
+                                  "sample": sample + "; oominf-cpu host expert path restated in C++/AVX-512; "
+                                            "one thread: " + sample1}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:

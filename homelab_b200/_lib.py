@@ -71,6 +71,7 @@ SIGNATURES = [
     ("oomb_version", C.c_char_p, []),
     ("oomb_status_string", C.c_char_p, [I]),
     ("oomb_device_error", I, [C.POINTER(C.c_int), I]),
+    ("oomb_set_wait_limit", I, [C.c_uint64]),
     ("oomb_gemm_fp8", I, [P, I, P, P, I, P, I, I, I, I, P, Z, S]),
     ("oomb_gemm_fp8_workspace_bytes", Z, [I, I, I, I]),
     ("oomb_gemm_fp8_tc", I, [P, I, P, I, P, I, P, I, I, I, I, P, Z, S]),

@@ -176,3 +176,7 @@ class Gpu:
         code = C.c_int(0)
         self.L.oomb_device_error(C.byref(code), int(clear))
         return code.value
+
+    def set_wait_limit(self, ns: int = 0) -> None:
+        """How long a bounded device wait polls before it gives up (0: the default 2 s)."""
+        check(self.L.oomb_set_wait_limit(int(ns)), "set_wait_limit")

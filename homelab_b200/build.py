@@ -42,26 +42,20 @@ def stale() -> bool:
     return any(os.path.getmtime(d) > t for d in DEPS if os.path.exists(d))
 
 
-TIMELINE_LIB = os.path.join(HERE, "liboomb_timeline.so")
-
-
-def build(force: bool = False, verbose: bool = False, timeline: bool = False) -> str:
-    """Builds liboomb.so, or with timeline=True the tracing variant
-    liboomb_timeline.so (-DOOMB_TIMELINE: kernels stamp a device timeline that
-    homelab_b200.timeline reads)."""
-    out = TIMELINE_LIB if timeline else LIB
-    if not timeline and not force and not stale():
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Builds liboomb.so when a source is newer than it (or always with force)."""
+    if not force and not stale():
         return LIB
-    cmd = [nvcc(), *NVCC_FLAGS, *(["-DOOMB_TIMELINE"] if timeline else []), "-o", out + ".tmp", *SOURCES]
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", LIB + ".tmp", *SOURCES]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
-        raise RuntimeError(f"nvcc failed building {os.path.basename(out)}")
+        raise RuntimeError("nvcc failed building liboomb.so")
     if verbose:
         sys.stderr.write(r.stderr)
-    os.replace(out + ".tmp", out)
-    return out
+    os.replace(LIB + ".tmp", LIB)
+    return LIB
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv, timeline="--timeline" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

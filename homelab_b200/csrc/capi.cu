@@ -522,6 +522,12 @@ int fused_launch_any(bool xbf16, int layout, const FusedDecode& f, cudaStream_t 
 
 using namespace oomb;
 
+namespace {
+// Zeroes the sync words of the no-alloc entry point's fixed scratch on the
+// current device (defined with that entry point, at the end of this file).
+bool noalloc_reset_sync();
+}  // namespace
+
 extern "C" {
 
 int oomb_silu_mul_rows(const float* gu, void* y, int y_dtype, int rows, int n, oomb_stream stream) {
@@ -670,8 +676,17 @@ int oomb_device_error(int* code, int clear) {
     if (clear && v) {
         const unsigned z = 0;
         if (cudaMemcpy(d->err, &z, sizeof(z), cudaMemcpyHostToDevice) != cudaSuccess) return OOMB_E_LAUNCH;
+        // a wait that ran out can leave counts behind in the sync words of the
+        // library's own decode scratch, which no caller can reach: zero them too
+        if (!noalloc_reset_sync()) return OOMB_E_LAUNCH;
     }
     return v ? OOMB_E_TIMEOUT : OOMB_OK;
+}
+
+int oomb_set_wait_limit(uint64_t ns) {
+    if (!device_state()) return OOMB_E_DEVICE;
+    const unsigned long long v = ns ? static_cast<unsigned long long>(ns) : kWaitLimitNs;
+    return cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
 }
 
 int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* scale,
@@ -1404,8 +1419,13 @@ namespace {
 
 __device__ __align__(256) uint8_t g_noalloc_scratch[OOMB_NOALLOC_SCRATCH_BYTES];
 
+// The part of the array that must be zero before a call and that the kernels
+// keep consistent from call to call: the chain's self-resetting arrival
+// counter (the first 256 bytes) and the one-launch kernel's sync words after
+// it (launch epoch, barrier counts, row-group counters).
+constexpr size_t kNoallocSyncBytes = 256 + ((static_cast<size_t>(kSyncWords) * 4 + 255) & ~static_cast<size_t>(255));
+
 struct NoallocState {
-    bool init = false;
     bool ok = false;
     uint8_t* scratch = nullptr;
 };
@@ -1413,26 +1433,39 @@ struct NoallocState {
 NoallocState g_noalloc[kMaxDevices];
 std::mutex g_noalloc_mu;
 
-// One-time set-up per device, with that device current: look up the array's
-// address and zero the pieces that must start at zero and that the kernels keep
-// consistent from call to call: the chain's arrival counter (first 256 bytes)
-// and the one-launch kernel's sync words after it (launch epoch, barrier
-// counts, row-group counters).  Returns nullptr if set-up failed.
+// Set-up per device, with that device current, done by the first call that
+// succeeds in it: look up the array's device address and zero its sync words.
+// A set-up that failed (for instance a first call made during stream capture)
+// leaves the state untouched, so a later call retries.  Returns nullptr on
+// failure.
 uint8_t* noalloc_scratch(oomb_stream stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     NoallocState& s = g_noalloc[dev];
-    if (!s.init) {
-        s.init = true;
+    if (!s.ok) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) == cudaSuccess &&
-            cudaMemsetAsync(p, 0, 256 + up256(kSyncWords * 4), stream) == cudaSuccess) {
-            s.scratch = static_cast<uint8_t*>(p);
-            s.ok = true;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return nullptr;
         }
+        if (cudaMemsetAsync(p, 0, kNoallocSyncBytes, stream) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return nullptr;
+        }
+        s.scratch = static_cast<uint8_t*>(p);
+        s.ok = true;
     }
-    return s.ok ? s.scratch : nullptr;
+    return s.scratch;
+}
+
+bool noalloc_reset_sync() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    const NoallocState& s = g_noalloc[dev];
+    if (!s.ok) return true;  // never set up: the next call's set-up zeroes them
+    return cudaMemset(s.scratch, 0, kNoallocSyncBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
 }
 
 }  // namespace
@@ -1451,18 +1484,3 @@ extern "C" int oomb_moe_decode_fp8_noalloc(const oomb_moe_layer* layer, const vo
     return oomb_moe_decode_fp8(layer, x, x_dtype, t, out, out_dtype, ids, weights, scratch,
                                OOMB_NOALLOC_SCRATCH_BYTES, stream);
 }
-
-#ifdef OOMB_TIMELINE
-// Built only into the tracing variant of the library (python -m
-// homelab_b200.build --timeline): copies the device timeline table
-// [kinds][events][CTAs] of %globaltimer stamps to the host, or zeroes it.
-extern "C" int oomb_timeline_read(void* host, size_t bytes) {
-    if (!host || bytes > sizeof(oomb::g_timeline)) return OOMB_E_ARG;
-    return cudaMemcpyFromSymbol(host, oomb::g_timeline, bytes) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
-}
-extern "C" int oomb_timeline_clear(void) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, oomb::g_timeline) != cudaSuccess) return OOMB_E_DEVICE;
-    return cudaMemset(p, 0, sizeof(oomb::g_timeline)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
-}
-#endif

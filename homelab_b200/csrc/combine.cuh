@@ -24,10 +24,8 @@ __global__ void __launch_bounds__(256) stage_host_kernel(uint4* dst, const uint4
 template <bool OUT_BF16>
 __global__ void combine_slots_kernel(const float* y, const int32_t* slot, const float* w, void* out,
                                      int T, int H, int K) {
-    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_ENTRY);
     pdl_wait();
     pdl_launch_dependents();
-    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_WAITED);
     const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (i >= static_cast<int64_t>(T) * H) return;
     const int t = static_cast<int>(i / H), c = static_cast<int>(i % H);
@@ -66,7 +64,6 @@ __global__ void combine_slots_kernel(const float* y, const int32_t* slot, const 
     } else {
         *reinterpret_cast<float4*>(static_cast<float*>(out) + i) = acc;
     }
-    if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
 }
 
 // SwiGLU on stacked rows (silu_mul_rows, ops.cu:302-309): y[r, i] =

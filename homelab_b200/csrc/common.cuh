@@ -25,8 +25,16 @@ enum : unsigned {
 
 // A bounded wait gives up after this long (globaltimer nanoseconds): orders of
 // magnitude above any legitimate stage wait, short enough that a lost copy
-// ends the kernel with an error instead of hanging the GPU.
+// ends the kernel with an error instead of hanging the GPU.  The limit in
+// force lives in a device word (one per device), so a caller can shorten it
+// (oomb_set_wait_limit) to make a wait that nothing will satisfy run out fast.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+
+// The limit in force, read once when a wait did not succeed at once.
+__device__ __forceinline__ unsigned long long wait_limit() {
+    return *const_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -37,27 +45,6 @@ __device__ __forceinline__ unsigned long long global_ns() {
 __device__ __forceinline__ void record_error(unsigned* err, unsigned code) {
     if (err) atomicCAS(err, 0u, code);
 }
-
-// Device timeline (built only with -DOOMB_TIMELINE): kernels stamp
-// %globaltimer at fixed points into a slot per (kind, event, CTA) with a plain
-// store (no atomics on the kernel's path).  Each launch overwrites the slots of
-// its kind, so after a replay of a chain of launches the table holds the last
-// launch of every kind: a host tool reads it to lay out where the chain spends
-// its time.
-enum : unsigned {
-    TL_ROUTE = 1, TL_GATE_UP = 2, TL_DOWN = 3, TL_COMBINE = 4, TL_GEMV = 5, TL_TC = 6,
-    TL_ENTRY = 0, TL_WAITED = 1, TL_END = 2, TL_FIRST_COPY = 3, TL_FIRST_STAGE = 4, TL_LOGITS_DONE = 5,
-    TL_LAST_CTA = 6, TL_X_STAGED = 7, TL_TOPK_DONE = 8, TL_FIRST_META = 9, TL_LAST_COPY = 10,
-};
-#ifdef OOMB_TIMELINE
-constexpr int kTimelineKinds = 8, kTimelineEvents = 16, kTimelineCtas = 1024;
-__device__ unsigned long long g_timeline[kTimelineKinds][kTimelineEvents][kTimelineCtas];
-__device__ __forceinline__ void tl_mark(unsigned kind, unsigned event) {
-    if (blockIdx.x < kTimelineCtas) g_timeline[kind][event][blockIdx.x] = global_ns();
-}
-#else
-__device__ __forceinline__ void tl_mark(unsigned, unsigned) {}
-#endif
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -101,14 +88,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
 }
 
 // Waits for the phase of `bar` with the given parity to complete.  Gives up
-// after kWaitLimitNs, records `code` and returns false.
+// after wait_limit() nanoseconds, records `code` and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* err,
                                           unsigned code) {
     if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
+    const unsigned long long t0 = global_ns(), limit = wait_limit();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit) {
             record_error(err, code);
             return false;
         }

@@ -158,9 +158,9 @@ __device__ __forceinline__ void bar_arrive(unsigned* ctr) {
 // n.  False when the wait ran out (the error code is recorded).
 __device__ __forceinline__ bool bar_wait(const unsigned* ctr, unsigned n, unsigned* err, unsigned code) {
     if (ld_acquire_u32(ctr) >= n) return true;
-    const unsigned long long t0 = global_ns();
+    const unsigned long long t0 = global_ns(), limit = wait_limit();
     while (ld_acquire_u32(ctr) < n) {
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit) {
             record_error(err, code);
             return false;
         }
@@ -437,7 +437,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         mbar_init(rbar, 1);
         mbar_init(xbar, 1);
         fence_barrier_init();
-        tl_mark(TL_ROUTE, TL_ENTRY);
         if (nrow > 0) {
             mbar_arrive_expect_tx(rbar, static_cast<unsigned>(nrow * H * 2));
             bulk_g2s_plain(smem, p.r.w + static_cast<int64_t>(row0) * H, static_cast<unsigned>(nrow * H * 2), rbar);
@@ -450,7 +449,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     pdl_wait();
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
-        tl_mark(TL_ROUTE, TL_WAITED);
         // every launch on this workspace before this one has completed
         s_epoch = ld_relaxed_u32(p.sync + kSyncEpoch) + 1u;
         if (blockIdx.x == 0) {
@@ -490,11 +488,9 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     // the CTAs with router rows publish their logits; every CTA waits for all of them
     unsigned* bars = p.sync + kSyncBars + (epoch & 3u) * kSyncSlot;
     if (threadIdx.x == 0) {
-        tl_mark(TL_ROUTE, TL_LOGITS_DONE);
         if (nrow > 0 && !s_fail) bar_arrive(bars);
         const unsigned writers = static_cast<unsigned>((E + kWarps - 1) / kWarps);
         if (!s_fail && !bar_wait(bars, writers, p.r.err, ERR_GRID_WAIT)) s_fail = 1;
-        tl_mark(TL_ROUTE, TL_LAST_CTA);
     }
     __syncthreads();
     if (s_fail) return;
@@ -512,7 +508,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
                 p.w_out[o] = w_sm[o];
             }
         }
-        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_TOPK_DONE);
         if constexpr (EP) {
             const EpMailbox mb = ep_mailbox(p.ep.ranks, p.ep.t_max, p.ep.k, p.ep.h, p.ep.xb);
             const unsigned ep_ep = s_ep_epoch;
@@ -566,7 +561,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_END);
 
     // ---- 4. gate/up then down through one ring ----
     const int n_e = *n_active;
@@ -606,7 +600,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     if (threadIdx.x == 0) {
         // every CTA has read the epoch: hand it to the next launch
         if (blockIdx.x == 0) st_relaxed_u32(p.sync + kSyncEpoch, epoch);
-        tl_mark(TL_DOWN, TL_WAITED);
     }
     if constexpr (D1) {
         if (p.dn1) {
@@ -616,7 +609,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
                 ok = down1_consume<BLK, 16>(p, ids_sm, w_sm, slot_sm, recs_sm, K, rg, g10, g11, pos, rg.red);
             else
                 ok = down1_consume<BLK, 32>(p, ids_sm, w_sm, slot_sm, recs_sm, K, rg, g10, g11, pos, rg.red);
-            if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
             (void)ok;
             return;
         }
@@ -644,9 +636,9 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
             const unsigned* flags = reinterpret_cast<const unsigned*>(p.ep.mailbox + mb.flags_return);
             for (int g = 0; g < G && !s_fail; g++) {
                 if (ep_ld_acquire_sys(flags + g) == ep_ep) continue;
-                const unsigned long long t0 = global_ns();
+                const unsigned long long t0 = global_ns(), limit = wait_limit();
                 while (ep_ld_acquire_sys(flags + g) != ep_ep) {
-                    if (global_ns() - t0 > kWaitLimitNs) {
+                    if (global_ns() - t0 > limit) {
                         record_error(p.r.err, ERR_EP_RETURN_WAIT);
                         s_fail = 1;
                         break;
@@ -669,7 +661,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
             if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(acc);
             else static_cast<float*>(p.out)[o] = acc;
         }
-        if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
     }
 
     if constexpr (!EP) {
@@ -714,7 +705,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
                 }
             }
         }
-        if (threadIdx.x == 0) tl_mark(TL_COMBINE, TL_END);
     }
 }
 

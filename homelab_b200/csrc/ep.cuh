@@ -241,9 +241,9 @@ __device__ __forceinline__ bool ep_wait_flags(const unsigned* flags, int ranks, 
     __syncthreads();
     for (int g = threadIdx.x; g < ranks; g += blockDim.x) {
         if (ep_ld_acquire_sys(flags + g) != epoch) {
-            const unsigned long long t0 = global_ns();
+            const unsigned long long t0 = global_ns(), limit = wait_limit();
             while (ep_ld_acquire_sys(flags + g) != epoch) {
-                if (global_ns() - t0 > kWaitLimitNs) {
+                if (global_ns() - t0 > limit) {
                     record_error(err, code);
                     failed = 1;
                     break;

@@ -689,7 +689,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
     uint64_t* recs_sm = (p.do_group && p.recs_all && p.E <= kRouteRecsSmem)
                             ? reinterpret_cast<uint64_t*>(rsm + sm.recs_off) : nullptr;
     int32_t* ids_sm = p.do_group ? reinterpret_cast<int32_t*>(rsm + sm.ids_off) : nullptr;
-    if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_ENTRY);
 
     // The layer's record addresses do not depend on the previous kernel: every
     // CTA fetches them before waiting (only the last CTA will use them).
@@ -711,7 +710,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         if (narrow && has_row) router_row_load(p, e, lane, row);
         pdl_wait();
         pdl_launch_dependents();
-        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_WAITED);
         if (narrow) {
             const int xb = XBF16 ? 2 : 4;
             for (int xt0 = 0; xt0 < p.T; xt0 += sm.xtile_tokens) {
@@ -723,7 +721,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
                 uint4* dst = reinterpret_cast<uint4*>(rsm);
                 for (int c = threadIdx.x; c < chunks; c += kRouteThreads) dst[c] = __ldcg(src + c);
                 __syncthreads();
-                if (threadIdx.x == 0 && xt0 == 0) tl_mark(TL_ROUTE, TL_X_STAGED);
                 if (has_row)
                     for (int t0 = xt0; t0 < xt0 + xn; t0 += kRouteTT)
                         router_row_dot<XBF16>(p, row, rsm, xt0, e, t0, min(kRouteTT, xt0 + xn - t0), lane);
@@ -732,7 +729,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         } else if (has_row) {
             for (int t0 = 0; t0 < p.T; t0 += kRouteTT) router_row_wide<XBF16>(p, e, t0, min(kRouteTT, p.T - t0), lane);
         }
-        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_LOGITS_DONE);
         if (!p.do_topk) return;
         // The last CTA to finish its logits runs the rest (deterministic: the
         // work it does depends only on the logits, not on which CTA it is).
@@ -745,7 +741,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
         __threadfence();
         if (threadIdx.x == 0) {
             *p.ticket = 0u;
-            tl_mark(TL_ROUTE, TL_LAST_CTA);
         }
     } else {
         pdl_wait();
@@ -766,10 +761,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteParams 
             for (int t = warp; t < p.T; t += nwarps) topk_token(p, t, lane, ids_sm);
         }
         __syncthreads();
-        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_TOPK_DONE);
         const GroupOut go{p.n_active, p.active, p.off, p.assign_tok, p.slot_assign, p.recs_active, nullptr};
         group_assignments<kRouteThreads>(p, go, ids_sm, ids_sm + p.T * p.K, ids_sm + p.T * p.K + p.E, recs_sm);
-        if (threadIdx.x == 0) tl_mark(TL_ROUTE, TL_END);
     } else if (ranked) {
         for (int t0 = blockIdx.x * nwarps; t0 < p.T; t0 += gridDim.x * nwarps) {
             topk_block<kRouteThreads>(p, p.logits, t0, min(p.T, t0 + nwarps), prob, pick_id, pick_p, p.ids, p.weights,

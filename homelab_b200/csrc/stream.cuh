@@ -311,11 +311,6 @@ struct RingPos {
     int s, q, rparity;
 };
 
-template <int PARTS, bool MOE>
-__host__ __device__ constexpr unsigned timeline_kind() {
-    return !MOE ? TL_GEMV : (PARTS == 2 ? TL_GATE_UP : TL_DOWN);
-}
-
 // ---- per-pass reduction and output ----------------------------------------------------------
 
 // hdr[pi] = {a_begin, a_end, row0, nr} of the pass's units (shared memory).
@@ -396,7 +391,6 @@ __device__ __forceinline__ void reduce_write(const StreamParams& p, const float 
 template <int PARTS, int P, bool MOE, bool TSMEM>
 __device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1, int& s,
                             int lag = 0) {
-    constexpr unsigned TLK = timeline_kind<PARTS, MOE>();
     if (u1 <= u0) return true;
     const int S = rg.stages, KS = p.ks;
     const int kcs = min(p.kc, p.k);  // shared-memory row stride
@@ -406,7 +400,7 @@ __device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring&
     const uint8_t* rec_next =
         (MOE && ei + 1 < tb.n_e) ? reinterpret_cast<const uint8_t*>(tab_u64<TSMEM>(tb.recs + ei + 1)) : rec;
     int rec_ei = ei;
-    bool ok = true, first = true;
+    bool ok = true;
     const int s_begin = s;
     for (int pf = u0; pf < u1 && ok; pf += P) {
         const int pn = min(P, u1 - pf);
@@ -430,10 +424,6 @@ __device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring&
                 const int kcl = min(p.kc, p.k - kc0);
                 uint8_t* dst = rg.stage_buf + slot * rg.slot_bytes;
                 mbar_arrive_expect_tx(&rg.full[slot], static_cast<unsigned>(PARTS * nr * kcl));
-                if (first) {
-                    tl_mark(TLK, TL_FIRST_COPY);
-                    first = false;
-                }
 #pragma unroll
                 for (int part = 0; part < PARTS; part++) {
                     const uint8_t* src = (MOE ? rec + (part ? p.w_off[1] : p.w_off[0]) : rec) +
@@ -450,7 +440,6 @@ __device__ bool stream_copy(const StreamParams& p, const Tables& tb, const Ring&
             }
         }
     }
-    tl_mark(TLK, TL_LAST_COPY);
     if (!ok) {
         // copies issued from this phase's stages that may still be in flight
         for (int d = max(s_begin, s - S); d < s; d++) mbar_wait(&rg.full[d % S], (d / S) & 1, p.err, ERR_DRAIN_WAIT);
@@ -528,7 +517,6 @@ template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool BLK, bool TSMEM, 
 __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ring& rg, int u0, int u1,
                                RingPos& pos) {
     static_assert(kRows * P * TB <= kRedV, "too many partials per lane");
-    constexpr unsigned TLK = timeline_kind<PARTS, MOE>();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = rg.stages, KS = p.ks;
     const int kcs = min(p.kc, p.k);  // shared-memory row stride
@@ -563,14 +551,11 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
         }
     }
     int s = pos.s, q = pos.q, rparity = pos.rparity;
-    bool first_meta = true, first_stage = true;
 
     for (int pf = u0; pf < u1; pf += P, q++) {
         const int pn = min(P, u1 - pf);
         const int buf = q % kMetaBufs;
         if (!mbar_wait(&rg.mfull[buf], (q / kMetaBufs) & 1, p.err, ERR_FULL_WAIT)) return false;
-        if (first_meta && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_META);
-        first_meta = false;
         const int* hdr = rg.meta + buf * rg.meta_stride;
         const float* sct = reinterpret_cast<const float*>(hdr + meta_ints);
         float acc[P][kRows][TB];
@@ -640,8 +625,6 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
                     if (a_begin < a_end) ensure_x(a_begin, min(TB, a_end - a_begin));
                     const int slot = s % S;
                     if (!mbar_wait(&rg.full[slot], (s / S) & 1, p.err, ERR_FULL_WAIT)) return false;
-                    if (first_stage && threadIdx.x == 0) tl_mark(TLK, TL_FIRST_STAGE);
-                    first_stage = false;
                     const uint8_t* base = rg.stage_buf + slot * rg.slot_bytes + ccol;
                     for (int a0 = a_begin; a0 < a_end; a0 += TB) {
                         const int nb = min(TB, a_end - a0);
@@ -700,7 +683,6 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
     pos.s = s;
     pos.q = q;
     pos.rparity = rparity;
-    if (threadIdx.x == 0) tl_mark(TLK, TL_END);
     return true;
 }
 
@@ -733,7 +715,6 @@ __device__ __forceinline__ void ring_init(const Ring& rg) {
 // [chunk headers 2 x 4 ints]
 template <int PARTS, int TB, int P, bool XBF16, bool MOE, bool EARLY, bool BLK>
 __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kernel(const StreamParams p) {
-    constexpr unsigned TLK = timeline_kind<PARTS, MOE>();
     extern __shared__ __align__(128) uint8_t smem[];
     Ring rg;
     rg.stages = p.stages;
@@ -752,7 +733,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
     if (threadIdx.x == 0) {
         ring_init(rg);
         fence_barrier_init();
-        tl_mark(TLK, TL_ENTRY);
     }
     __syncthreads();
 
@@ -787,7 +767,6 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) stream_kern
     // ================= consumers =================
     pdl_wait();
     pdl_launch_dependents();
-    if (threadIdx.x == 0) tl_mark(TLK, TL_WAITED);
     const Tables tb = global_tables(p, MOE);
     int u0, u1;
     cta_units(tb.n_e, p.gpe, u0, u1);

@@ -267,7 +267,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     pdl_launch_dependents();
-    if (threadIdx.x == 0) tl_mark(TL_TC, TL_ENTRY);
 
     if (warp == 0) {
         // ================= TMA producer: weight tiles (independent of the previous kernel) =================
@@ -282,9 +281,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     tma_load_2d(a_ring + s * kTcTileBytes, &qmap, 0, i * kTcTile, &a_full[s], pol);
                 else
                     tma_load_2d(a_ring + s * kTcTileBytes, &qmap, kb * kTcTile, rb * kTcTile, &a_full[s], pol);
-                if (i == lo) tl_mark(TL_TC, TL_FIRST_COPY);
             }
-            tl_mark(TL_TC, TL_LAST_COPY);
         }
     } else if (warp >= 6) {
         // ================= activation splitters: B tiles and their term scales =================
@@ -307,7 +304,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             }
         };
         pdl_wait();
-        if (sw == 0 && lane == 0) tl_mark(TL_TC, TL_WAITED);
         for (int m = 0; m < XD; m++) fetch(m);
         for (int m = 0; my_tile(m) < hi; m++) {
             const int i = my_tile(m);
@@ -401,9 +397,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     tc_mma(d, tc_smem_desc(a_addr + 32 * k), tc_smem_desc(b_addr + 32 * k), idesc, k > 0);
                 tc_commit(&a_empty[s]);
                 tc_commit(&mma_done[buf]);
-                if (j < 4) tl_mark(TL_TC, 11 + j);
             }
-            tl_mark(TL_TC, 8);
         }
     } else {
         // ================= epilogue warpgroup (warps 2..5) =================
@@ -458,7 +452,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             if (lane == 0) {
                 mbar_arrive(&tmem_empty[buf]);
                 mbar_arrive(&b_empty[s]);
-                if (warp == 2 && j < 4) tl_mark(TL_TC, 4 + j);
             }
             // end of this CTA's part of row block rb: write it, or hand it to the split-K fix-up
             if (i + 1 == hi || (i + 1) % p.kblocks == 0) {
@@ -501,13 +494,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             }
         }
     }
-    if (warp == 2 && lane == 0) tl_mark(TL_TC, 9);
     // the producer and MMA roles ran on lane 0 alone: reconverge every warp
     // before the CTA barrier (an aligned barrier must not be reached diverged)
     __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (threadIdx.x == 0) tl_mark(TL_TC, TL_END);
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.tmem_cols)

@@ -88,8 +88,18 @@ typedef struct {
 const char* oomb_version(void);
 const char* oomb_status_string(int status);
 /* The first bounded-wait failure recorded on the current device since the
- * last clear (0 if none); `clear` != 0 resets it.  Synchronises the device. */
+ * last clear (0 if none); `clear` != 0 resets it, and then also zeroes the
+ * sync words of the no-alloc decode's fixed scratch on this device (see
+ * oomb_moe_decode_fp8_noalloc).  Synchronises the device.  No counterpart in
+ * the reference, whose kernels never wait on one another. */
 int oomb_device_error(int* code, int clear);
+/* Sets how long a bounded device wait polls before it gives up and records
+ * its code, in nanoseconds, on the current device (0 restores the default of
+ * 2 s).  Takes effect for kernels launched after it returns.  A diagnostic
+ * knob: a short limit makes a wait that nothing will satisfy (a peer that
+ * never raises its flag) end within milliseconds, so the failure path can be
+ * exercised without hanging anything.  No counterpart in the reference. */
+int oomb_set_wait_limit(uint64_t ns);
 
 /* ---- Linear ------------------------------------------------------------ */
 /* y[t, n] = x[t, k] . W[n, k]^T for FP8 e4m3 W with block scales, fp32
@@ -243,12 +253,18 @@ int oomb_workspace_clear(void* workspace, size_t bytes, oomb_stream stream);
  *     and intermediate 768 that is t <= 92); larger calls return
  *     OOMB_E_WORKSPACE before any launch.
  *   - The first call on each device, made with that device current, does a
- *     one-time set-up: it looks up the array's address and zeroes its arrival
- *     counter (a 256-byte memset on `stream`).  Make that first call before
- *     any stream capture.
+ *     one-time set-up: it looks up the array's device address and zeroes the
+ *     array's first 4096 bytes on `stream` (one cudaMemsetAsync): the kernel
+ *     chain's self-resetting arrival counter (256 bytes) and the one-launch
+ *     kernel's sync words (launch epoch, grid-barrier counts, row-group
+ *     counters).  Make that first call before any stream capture.  If the
+ *     set-up fails the call returns OOMB_E_DEVICE and the next call retries it.
  *   - All calls on one device share the array: they must be ordered (one
  *     stream, or otherwise serialised).  Overlapping calls race on the
- *     scratch and corrupt each other's results. */
+ *     scratch and corrupt each other's results.
+ *   - After a bounded device wait has run out (oomb_device_error reports a
+ *     code), clearing the error with oomb_device_error(&code, 1) zeroes those
+ *     4096 bytes again, so the next call starts from clean sync words. */
 #define OOMB_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 int oomb_moe_decode_fp8_noalloc(const oomb_moe_layer* layer, const void* x, int x_dtype, int t, void* out,
                                 int out_dtype, int32_t* ids, float* weights, oomb_stream stream);
