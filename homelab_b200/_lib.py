@@ -27,6 +27,8 @@ SCALE_1X128 = 0
 SCALE_128X128 = 1
 TABLES_READY = 1
 NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
+PART_ALIGN = 256
+RECORD_ALIGN = 4096
 Q_ROWS = 0
 Q_TILES = 1
 
@@ -60,6 +62,16 @@ class EpPeer(C.Structure):
         ("peers", C.c_void_p), ("mailbox", C.c_void_p),
         ("ranks", C.c_int32), ("rank", C.c_int32), ("t_max", C.c_int32),
         ("top_k", C.c_int32), ("hidden", C.c_int32), ("x_dtype", C.c_int32),
+    ]
+
+
+class SharedExpert(C.Structure):
+    """oomb_shared_expert: a layer's shared expert(s) as one FP8 SwiGLU MLP plus a bf16 gate row."""
+
+    _fields_ = [
+        ("hidden", C.c_int32), ("inter", C.c_int32), ("scale_layout", C.c_int32), ("pad_", C.c_int32),
+        ("gate_up_q", C.c_void_p), ("gate_up_scale", C.c_void_p),
+        ("down_q", C.c_void_p), ("down_scale", C.c_void_p), ("gate_w", C.c_void_p),
     ]
 
 
@@ -115,13 +127,31 @@ SIGNATURES = [
     ("oomb_moe_down_fp8", I, [P, P, I, P, P, C.POINTER(Fp8Record), I, I, S]),
     ("oomb_moe_combine_slots", I, [P, P, P, P, I, I, I, I, S]),
     ("oomb_moe_combine", I, [P, P, P, P, I, I, S]),
-    ("oomb_moe_tiled_fp8", I, [P, P, P, I, I, P, I, P, I, I, C.c_int64, C.c_int64, I, S]),
+    ("oomb_moe_tiled_fp8_workspace_bytes", Z, [I, I, I]),
+    ("oomb_moe_tiled_fp8", I, [P, P, P, I, I, I, P, I, P, I, I, C.c_int64, C.c_int64, I, P, Z, S]),
     ("oomb_moe_swiglu_range", I, [P, P, P, C.c_int64, C.c_int64, S]),
     ("oomb_moe_decode_workspace_bytes", Z, [I, C.POINTER(MoeLayer)]),
     ("oomb_moe_decode_fp8", I, [C.POINTER(MoeLayer), P, I, I, P, I, P, P, P, Z, S]),
     ("oomb_workspace_clear", I, [P, Z, S]),
     ("oomb_moe_decode_fp8_noalloc", I, [C.POINTER(MoeLayer), P, I, I, P, I, P, P, S]),
     ("oomb_quantize_fp8", I, [P, I, I, I, P, P, S]),
+    ("oomb_attention_decode_workspace_bytes", Z, [I, I, I, I, I]),
+    ("oomb_fp8_record_layout", I, [C.c_int64, C.c_int64, I, C.POINTER(Fp8Record), C.POINTER(C.c_size_t)]),
+    ("oomb_quantize_fp8_record", I, [P, P, P, C.POINTER(Fp8Record), P, S]),
+    ("oomb_policy_create", I, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    ("oomb_policy_destroy", I, [P]),
+    ("oomb_policy_touch", I, [P, C.c_uint32, C.c_uint64]),
+    ("oomb_policy_remove", I, [P, C.c_uint32]),
+    ("oomb_policy_victim", C.c_int64, [P, P, I]),
+    ("oomb_tier_create", I, [P, Z, I, I, P, I, C.c_char_p, C.POINTER(C.c_void_p)]),
+    ("oomb_tier_destroy", I, [P]),
+    ("oomb_tier_begin_fetch", I, [P, S, I, P, I, P, P]),
+    ("oomb_tier_finish_fetch", I, [P, S]),
+    ("oomb_tier_stats", I, [P, P]),
+    ("oomb_moe_layer_workspace_bytes", Z, [I, C.POINTER(MoeLayer), C.POINTER(SharedExpert), I]),
+    ("oomb_moe_layer_decode_fp8", I, [C.POINTER(MoeLayer), C.POINTER(SharedExpert), P, I, I, P, I, P, P, P, Z,
+                                      S]),
+    ("oomb_attention_decode", I, [P, I, P, P, C.c_int64, P, I, P, I, I, I, I, I, I, C.c_float, P, Z, S]),
 ]
 
 _LIB = None

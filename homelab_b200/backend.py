@@ -27,6 +27,14 @@ def _dtype_code(t: torch.Tensor) -> int:
     raise TypeError(f"activations must be float32 or bfloat16, got {t.dtype}")
 
 
+def _dtype_code_of(dt: torch.dtype) -> int:
+    if dt == torch.float32:
+        return F32
+    if dt == torch.bfloat16:
+        return BF16
+    raise TypeError(f"activations must be float32 or bfloat16, got {dt}")
+
+
 def _ptr(t) -> int:
     if t is None:
         return 0
@@ -53,6 +61,7 @@ class Gpu:
     def __init__(self, device: int = 0):
         self.device = torch.device("cuda", device)
         self.L = _lib.lib()
+        self._tiled_ws = None  # grown on demand by moe_tiled calls without a workspace
 
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
@@ -118,14 +127,31 @@ class Gpu:
                                        max_per_expert, _lib.TABLES_READY if tables_ready else 0, self._stream()),
               "moe_down")
 
+    def moe_tiled_workspace(self, max_assignments: int, k: int, x_dtype=torch.bfloat16) -> torch.Tensor:
+        """A workspace for moe_tiled calls of up to max_assignments assignments over k columns."""
+        n = int(self.L.oomb_moe_tiled_fp8_workspace_bytes(max_assignments, k, _dtype_code_of(x_dtype)))
+        if n == 0:
+            raise ValueError("unsupported moe_tiled shape")
+        return torch.empty(n, dtype=torch.uint8, device=self.device)
+
     def moe_tiled(self, recs, off, rows, n_experts: int, max_per_expert: int, x, y, n: int, k: int,
-                  proj: tuple, layout: int):
+                  proj: tuple, layout: int, workspace=None, max_assignments: int = 0):
         """y[a] = x[row(a)] . W_e^T for one projection (w_off, s_off) of every group, on the tensor
-        cores (Experts::moe_tiled, backend.rs:873-886); rows None means row(a) = a."""
+        cores (Experts::moe_tiled, backend.rs:873-886); rows None means row(a) = a.  The assignment
+        count is bounded by y's rows unless max_assignments says otherwise; without a workspace one
+        is kept per Gpu object and grown as needed (allocate it once up front before graph capture)."""
         w_off, s_off = proj
+        A = int(max_assignments) if max_assignments else int(y.shape[0])
+        if workspace is None:
+            need = int(self.L.oomb_moe_tiled_fp8_workspace_bytes(A, k, _dtype_code(x)))
+            if need == 0:
+                raise ValueError("unsupported moe_tiled shape")
+            if self._tiled_ws is None or self._tiled_ws.numel() < need:
+                self._tiled_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            workspace = self._tiled_ws
         check(self.L.oomb_moe_tiled_fp8(_ptr(recs), _ptr(off), None if rows is None else _ptr(rows), n_experts,
-                                        max_per_expert, _ptr(x), _dtype_code(x), _ptr(y), n, k, w_off, s_off,
-                                        layout, self._stream()), "moe_tiled")
+                                        max_per_expert, A, _ptr(x), _dtype_code(x), _ptr(y), n, k, w_off, s_off,
+                                        layout, _ptr(workspace), workspace.numel(), self._stream()), "moe_tiled")
 
     def moe_swiglu_range(self, g, u, h, start: int, end: int):
         """h[i] = silu(g[i]) * u[i] for i in [start, end) (Experts::moe_swiglu_range, backend.rs:888)."""
@@ -171,6 +197,42 @@ class Gpu:
         check(self.L.oomb_quantize_fp8(_ptr(w_bf16), n, k, layout, _ptr(q), _ptr(scale), self._stream()),
               "quantize_fp8")
         return q, scale
+
+    def moe_layer_workspace(self, layer: MoeLayer, shared, t: int, x_dtype=torch.bfloat16) -> torch.Tensor:
+        """A zeroed workspace for moe_layer_decode of up to t tokens."""
+        n = int(self.L.oomb_moe_layer_workspace_bytes(t, C.byref(layer), C.byref(shared), _dtype_code_of(x_dtype)))
+        if n == 0:
+            raise ValueError("unsupported MoE layer shape")
+        return torch.zeros(n, dtype=torch.uint8, device=self.device)
+
+    def moe_layer_decode(self, layer: MoeLayer, shared, x, t: int, out, workspace, ids=None, weights=None):
+        """One MoE layer (Moe::forward, moe.rs:479-495): shared expert, routed experts and the gated combine."""
+        check(self.L.oomb_moe_layer_decode_fp8(C.byref(layer), C.byref(shared), _ptr(x), _dtype_code(x), t, _ptr(out),
+                                               _dtype_code(out), _ptr(ids), _ptr(weights), _ptr(workspace),
+                                               workspace.numel(), self._stream()), "moe_layer_decode")
+
+    # ---- Attention ----------------------------------------------------------------------
+
+    def attention_workspace(self, batch: int, heads: int, kv_heads: int, head_dim: int, kv_max: int) -> torch.Tensor:
+        n = int(self.L.oomb_attention_decode_workspace_bytes(batch, heads, kv_heads, head_dim, kv_max))
+        if n == 0:
+            raise ValueError("unsupported attention shape")
+        return torch.zeros(n, dtype=torch.uint8, device=self.device)
+
+    def attention_decode(self, q, k_cache, v_cache, out, kv_len, scale: float, workspace, kv_heads: int):
+        """out[b, h] = softmax(scale * q[b, h] . K[b, :, h / G]) V[b, :, h / G] over each sequence's
+        first kv_len positions (Attention::attention for one token per sequence, backend.rs:551-568).
+        q, out [B, H, D]; k_cache, v_cache bf16 [B, kv_max, kv_heads, D]; kv_len an int (all
+        sequences) or a device int32 tensor [B]."""
+        B, H, D = q.shape
+        kv_max = k_cache.shape[1]
+        if k_cache.shape != v_cache.shape or k_cache.dtype != torch.bfloat16 or k_cache.shape[2] != kv_heads:
+            raise ValueError("k_cache and v_cache must be bf16 [B, kv_max, kv_heads, D]")
+        lens, all_len = (None, int(kv_len)) if isinstance(kv_len, int) else (_ptr(kv_len), 0)
+        check(self.L.oomb_attention_decode(_ptr(q), _dtype_code(q), _ptr(k_cache), _ptr(v_cache),
+                                           k_cache.stride(0), lens, all_len, _ptr(out), _dtype_code(out), B, H,
+                                           kv_heads, D, kv_max, float(scale), _ptr(workspace), workspace.numel(),
+                                           self._stream()), "attention_decode")
 
     def device_error(self, clear: bool = True) -> int:
         code = C.c_int(0)

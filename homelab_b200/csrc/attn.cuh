@@ -1,0 +1,233 @@
+// attn.cuh - grouped-query decode attention over a bf16 KV cache (split-K flash-decode).
+//
+// For every sequence b (one query token each) and query head h of kv head
+// h / G (G = heads / kv_heads query heads share a kv head):
+//   out[b, h, :] = sum_j softmax_j(scale * q[b, h, :] . K[b, j, h / G, :]) V[b, j, h / G, :],
+// j < kv_len[b], fp32 softmax and accumulation.  The decode case of the
+// reference's Attention::attention (crates/oominf-core/src/backend.rs:551-568)
+// as its flash-decode kernels compute it (attn_decode_partial_g12 +
+// attn_decode_combine, crates/oominf-cuda/kernels/attention.cu:592-700): each
+// worker keeps an online-softmax partial (running max m, sum l, unnormalised
+// accumulator) over its share of the positions, and the partials merge as
+//   out = sum_w e^(m_w - M) acc_w / sum_w e^(m_w - M) l_w,  M = max_w m_w.
+// Here the cache is bf16 (the reference's is fp32 with hd 256 and G = 12), the
+// merge runs in the same launch, and the layout is the reference's: row j of
+// kv head c at ((j * kv_heads + c) * D) elements from the sequence's base.
+//
+// Bound: HBM (every K and V byte read once; 2 * kv_len * kv_heads * D * 2
+// bytes per sequence).  Grid (splits, kv_heads, batch), 4 warps per CTA; warp
+// w of split s takes a contiguous share of the positions and walks it in
+// chunks of CP = min(32 / G, 8) positions: lane l owns elements [l * E, l * E + E) of a
+// row (E = D / 32), so a warp reads each 2D-byte row with one coalesced load;
+// the CP x G partial dot products of a chunk are summed over the lanes by one
+// multi-value butterfly (lane l ends with the score of (position l / G, head
+// l % G)); the chunk's softmax runs one score per lane; the weights reach
+// every lane through shared memory for the V update.  Each warp's partial
+// goes to the workspace; the last CTA of a (sequence, kv head) to finish (an
+// arrival counter that resets itself) merges them in warp order and writes
+// the output: deterministic.
+#pragma once
+
+#include "common.cuh"
+
+namespace oomb {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+
+enum : unsigned {
+    ERR_ATTN_LEN = 0x800,  // a kv_len entry was outside [0, kv_max] (clamped)
+};
+
+struct AttnParams {
+    const void* q;         // [B, H, D] fp32 or bf16
+    int q_bf16;
+    const uint16_t* k;     // bf16 K cache: sequence b at b * seq_stride elements, row j of kv head c at (j * Hkv + c) * D
+    const uint16_t* v;     // bf16 V cache, same layout
+    int64_t seq_stride;
+    const int32_t* kv_len; // [B] visible positions per sequence (device), or null: kv_len_host for all
+    int kv_len_host;
+    void* out;             // [B, H, D] fp32 or bf16
+    int out_bf16;
+    int B, H, Hkv, kv_max;
+    int splits;            // CTAs per (sequence, kv head)
+    float scale;
+    float* part;           // [B][Hkv][splits * kAttnWarps][G][D + 4]: acc, m, l (rows 16-byte aligned)
+    unsigned* counters;    // [B * Hkv] arrivals, zero between launches
+    unsigned* err;
+};
+
+__device__ __forceinline__ void bf16x4_to_f32(uint2 w, float (&f)[4]) {
+    f[0] = __uint_as_float(w.x << 16);
+    f[1] = __uint_as_float(w.x & 0xffff0000u);
+    f[2] = __uint_as_float(w.y << 16);
+    f[3] = __uint_as_float(w.y & 0xffff0000u);
+}
+
+template <int G, int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnParams p) {
+    static_assert(D == 128, "lanes own four elements of a row");
+    static_assert(G >= 1 && G <= 32 && (32 % G) == 0, "G must divide 32");
+    constexpr int E = D / 32;
+    constexpr int CP = 32 / G < 8 ? 32 / G : 8;  // positions per chunk: CP * G <= 32 scores, one per lane
+    constexpr int PS = D + 4;                      // floats per partial row: acc[D], m, l, padding
+    __shared__ float ebuf[kAttnWarps][32];
+    __shared__ float cbuf[kAttnWarps][32];
+    __shared__ bool last;
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    pdl_wait();  // q (and the cache rows just appended) come from earlier kernels
+    pdl_launch_dependents();
+    int L = p.kv_len ? __ldcg(p.kv_len + b) : p.kv_len_host;
+    if (L < 0 || L > p.kv_max) {
+        if (threadIdx.x == 0) record_error(p.err, ERR_ATTN_LEN);
+        L = max(0, min(L, p.kv_max));
+    }
+    const int W = p.splits * kAttnWarps, wi = split * kAttnWarps + warp;
+    const int j0 = static_cast<int>(static_cast<int64_t>(L) * wi / W);
+    const int j1 = static_cast<int>(static_cast<int64_t>(L) * (wi + 1) / W);
+
+    // this lane's elements of the G query heads, scaled
+    float qv[G][E];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const int64_t qi = (static_cast<int64_t>(b) * p.H + kvh * G + g) * D + lane * E;
+        if (p.q_bf16) {
+            float f[4];
+            bf16x4_to_f32(__ldcg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.q) + qi)), f);
+#pragma unroll
+            for (int e = 0; e < E; e++) qv[g][e] = f[e] * p.scale;
+        } else {
+            const float4 f = __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + qi));
+            qv[g][0] = f.x * p.scale;
+            qv[g][1] = f.y * p.scale;
+            qv[g][2] = f.z * p.scale;
+            qv[g][3] = f.w * p.scale;
+        }
+    }
+    float acc[G][E];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < E; e++) acc[g][e] = 0.0f;
+    // running max and sum of the lane's head (lane % G); the same in every lane of that head
+    float m_run = -INFINITY, l_run = 0.0f;
+    const int64_t row_stride = static_cast<int64_t>(p.Hkv) * D;
+    const uint16_t* kb = p.k + static_cast<int64_t>(b) * p.seq_stride + static_cast<int64_t>(kvh) * D + lane * E;
+    const uint16_t* vb = p.v + static_cast<int64_t>(b) * p.seq_stride + static_cast<int64_t>(kvh) * D + lane * E;
+
+    uint2 kr[CP];
+    auto load_k = [&](int j) {
+#pragma unroll
+        for (int c = 0; c < CP; c++)
+            kr[c] = j + c < j1 ? __ldcs(reinterpret_cast<const uint2*>(kb + (j + c) * row_stride)) : make_uint2(0u, 0u);
+    };
+    if (j0 < j1) load_k(j0);
+    for (int j = j0; j < j1; j += CP) {
+        const int n = min(CP, j1 - j);
+        uint2 vr[CP];
+#pragma unroll
+        for (int c = 0; c < CP; c++)
+            vr[c] = c < n ? __ldcs(reinterpret_cast<const uint2*>(vb + (j + c) * row_stride)) : make_uint2(0u, 0u);
+        // partial scores: value c * G + g = this lane's share of q_g . k_c
+        float s[32];
+#pragma unroll
+        for (int i = CP * G; i < 32; i++) s[i] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CP; c++) {
+            float kf[4];
+            bf16x4_to_f32(kr[c], kf);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float d = qv[g][0] * kf[0];
+#pragma unroll
+                for (int e = 1; e < E; e++) d = fmaf(qv[g][e], kf[e], d);
+                s[c * G + g] = d;
+            }
+        }
+        if (j + CP < j1) load_k(j + CP);  // the next chunk's keys load under this chunk's math
+        warp_reduce_multi<32>(s, lane);   // lane l: the score of (position l / G, head l % G)
+        const int c_l = lane / G;  // lanes past CP * G hold padding: c_l >= CP >= n
+        const float sc = c_l < n ? s[0] : -INFINITY;
+        float cmax = sc;
+#pragma unroll
+        for (int o = G; o < 32; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+        const float m_new = fmaxf(m_run, cmax);
+        const float corr = __expf(m_run - m_new);
+        const float e = c_l < n ? __expf(sc - m_new) : 0.0f;
+        float esum = e;
+#pragma unroll
+        for (int o = G; o < 32; o <<= 1) esum += __shfl_xor_sync(0xffffffffu, esum, o);
+        l_run = fmaf(l_run, corr, esum);
+        m_run = m_new;
+        ebuf[warp][lane] = e;
+        cbuf[warp][lane] = corr;
+        __syncwarp();
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float cg = cbuf[warp][g];
+#pragma unroll
+            for (int e2 = 0; e2 < E; e2++) acc[g][e2] *= cg;
+        }
+#pragma unroll
+        for (int c = 0; c < CP; c++) {
+            float vf[4];
+            bf16x4_to_f32(vr[c], vf);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float w = ebuf[warp][c * G + g];
+#pragma unroll
+                for (int e2 = 0; e2 < E; e2++) acc[g][e2] = fmaf(w, vf[e2], acc[g][e2]);
+            }
+        }
+        __syncwarp();
+    }
+
+    // this warp's partial: acc, m, l of each head
+    const int64_t pbase = (static_cast<int64_t>(b) * p.Hkv + kvh) * W;
+    float* mine = p.part + (pbase + wi) * G * PS;
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        float* o = mine + g * PS;
+        *reinterpret_cast<float4*>(o + lane * E) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    }
+    if (lane < G) {
+        mine[lane * PS + D] = m_run;
+        mine[lane * PS + D + 1] = l_run;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(p.counters + b * p.Hkv + kvh, 1u);
+        last = prev == static_cast<unsigned>(p.splits - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // merge the W partials of this (sequence, kv head) in warp order
+    const float* all = p.part + pbase * G * PS;
+    for (int o = threadIdx.x; o < G * D; o += kAttnThreads) {
+        const int g = o / D, d = o - g * D;
+        float M = -INFINITY;
+        for (int w = 0; w < W; w++) M = fmaxf(M, __ldcg(all + (static_cast<int64_t>(w) * G + g) * PS + D));
+        float num = 0.0f, den = 0.0f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < W; w++) {
+                const float* pr = all + (static_cast<int64_t>(w) * G + g) * PS;
+                const float mw = __ldcg(pr + D);
+                if (mw == -INFINITY) continue;
+                const float f = __expf(mw - M);
+                num = fmaf(f, __ldcg(pr + d), num);
+                den = fmaf(f, __ldcg(pr + D + 1), den);
+            }
+        }
+        const float r = den > 0.0f ? num / den : 0.0f;  // no visible position: zeros
+        const int64_t oi = (static_cast<int64_t>(b) * p.H + kvh * G + g) * D + d;
+        if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(r);
+        else static_cast<float*>(p.out)[oi] = r;
+    }
+    if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0u;
+}
+
+}  // namespace oomb

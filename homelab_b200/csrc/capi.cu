@@ -13,6 +13,7 @@
 #include <unordered_map>
 
 #include "../../include/oomb.h"
+#include "attn.cuh"
 #include "combine.cuh"
 #include "decode.cuh"
 #include "ep.cuh"
@@ -21,6 +22,7 @@
 #include "stream.cuh"
 #include "tc.cuh"
 #include "tcgroup.cuh"
+#include "tiers.h"
 
 namespace oomb {
 namespace {
@@ -249,15 +251,16 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// Tensor map of an e4m3 matrix [rows, k] (row-major) in 128 x 128 boxes with
-// the 128-byte swizzle the MMA descriptors expect.  Packed tiles are mapped as
-// a [tiles * 128, 128] matrix (k = 128 there).
-bool encode_fp8_tiles(CUtensorMap* map, const uint8_t* q, int rows, int k) {
+// Tensor map of a byte matrix [rows, k] (row-major) in boxes of 128 bytes x
+// box_rows rows with the 128-byte swizzle the MMA descriptors expect: e4m3
+// weights (box 128 x 128; packed tiles are a [tiles * 128, 128] matrix) and the
+// split activation images (box 128 x nmma).
+bool encode_u8_tiles(CUtensorMap* map, const uint8_t* q, int rows, int k, int box_rows) {
     EncodeTiledFn enc = encode_tiled();
     if (!enc) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
-    const cuuint32_t box[2] = {kTcTile, kTcTile};
+    const cuuint32_t box[2] = {kTcTile, static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -270,101 +273,139 @@ bool encode_fp8_tiles(CUtensorMap* map, const uint8_t* q, int rows, int k) {
     return true;
 }
 
+bool encode_fp8_tiles(CUtensorMap* map, const uint8_t* q, int rows, int k) {
+    return encode_u8_tiles(map, q, rows, k, kTcTile);
+}
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+// The activation split of one call: terms image [rows_alloc, k] and term scales
+// [k/128][tc_sx_stride(rows_alloc)] at the given workspace offsets.
+struct XsLayout {
+    size_t xs_off, sx_off, end;
+    int rows_alloc, sx_stride;
+};
+
+XsLayout xs_layout(size_t base, int rows_alloc, int k) {
+    XsLayout x{};
+    x.rows_alloc = rows_alloc;
+    x.sx_stride = tc_sx_stride(rows_alloc);
+    x.xs_off = align256(base);
+    x.sx_off = align256(x.xs_off + static_cast<size_t>(rows_alloc) * k);
+    x.end = align256(x.sx_off + static_cast<size_t>(k / kTcTile) * x.sx_stride * 4);
+    return x;
+}
+
+int launch_xsplit(bool x_bf16, const XsParams& xp, cudaStream_t s) {
+    const int64_t warps = static_cast<int64_t>(xp.a_cover) * xp.kblocks;
+    const int64_t blocks = (warps + 7) / 8;
+    if (blocks <= 0 || blocks > 0x7fffffff) return OOMB_E_SHAPE;
+    return x_bf16 ? launch(xsplit_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, xp)
+                  : launch(xsplit_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, xp);
+}
+
 struct TcPlan {
-    int grid, tiles, kblocks, nmma, stages, nbufs, xdepth, tmem_cols;
+    int grid, tiles, kblocks, nmma, stages, nbufs, tmem_cols;
     size_t smem, counters_off, partial_off, ws_bytes;
+    XsLayout xs;
 };
 
 // Up to 4 tokens two CTAs fit on an SM (registers and shared memory), so the next
 // launch of a dependent chain can start streaming; larger batches take one.
 constexpr size_t kTcSmemLimit2 = 110 * 1024, kTcSmemLimit1 = 210 * 1024;
 constexpr int kTcMinTokens = 2;  // oomb_gemm_fp8 takes the tensor cores from this batch size
+constexpr int kTcMaxTF32 = 32;   // fp32 x: six terms a token, at most 192 MMA columns
 
 bool tc_plan(const DeviceState* d, int t, int n, int k, bool x_bf16, TcPlan& pl) {
-    if (t < 1 || t > kTcMaxT || n % kTcTile != 0 || k % kTcTile != 0 || n <= 0 || k <= 0) return false;
-    const int ts = tc_ts(x_bf16), xb = x_bf16 ? 2 : 4;
+    if (t < 1 || t > (x_bf16 ? kTcMaxT : kTcMaxTF32) || n % kTcTile != 0 || k % kTcTile != 0 || n <= 0 || k <= 0)
+        return false;
+    const int ts = tc_ts(x_bf16);
     pl.kblocks = k / kTcTile;
     pl.tiles = (n / kTcTile) * pl.kblocks;
     pl.grid = pl.tiles < d->sms ? pl.tiles : d->sms;
     pl.nmma = (t * ts + 7) / 8 * 8;
+    if (pl.nmma > kTcMaxN) return false;
     pl.nbufs = kTcAccBufs;
-    while (pl.nbufs > 2 && pl.nbufs * pl.nmma > 256) pl.nbufs /= 2;
+    while (pl.nbufs > 2 && pl.nbufs * pl.nmma > 512) pl.nbufs /= 2;
     int cols = 32;
     while (cols < pl.nbufs * pl.nmma) cols *= 2;
     if (cols > 512) return false;
     pl.tmem_cols = cols;
     const size_t limit = t <= 4 ? kTcSmemLimit2 : kTcSmemLimit1;
-    pl.xdepth = kTcXDepth;
-    auto total = [&](int st) { return tc_smem(st, pl.nmma, t, ts, xb, pl.xdepth).total + 1024; };
-    // The splitters share the B ring round-robin by tile; a splitter's parity
-    // waits on a slot stay within one phase of the slot's barrier only when the
-    // ring has at least one slot per splitter.
+    auto total = [&](int st) { return tc_smem(st, pl.nmma).total + 1024; };
     pl.stages = kTcMaxStages;
-    while (pl.stages > kTcSplitters && total(pl.stages) > limit) pl.stages--;
-    if (total(pl.stages) > limit) pl.xdepth = 1;
+    while (pl.stages > kTcMinStages && total(pl.stages) > limit) pl.stages--;
     pl.smem = total(pl.stages);
     if (pl.smem > 227 * 1024) return false;
     pl.counters_off = 0;
-    pl.partial_off = (static_cast<size_t>(n / kTcTile) * 4 * 4 + 255) & ~static_cast<size_t>(255);
-    pl.ws_bytes = pl.partial_off + static_cast<size_t>(pl.grid) * 2 * t * kTcTile * 4;
+    pl.partial_off = align256(static_cast<size_t>(n / kTcTile) * 4 * 4);
+    pl.xs = xs_layout(pl.partial_off + static_cast<size_t>(pl.grid) * 2 * t * kTcTile * 4, pl.nmma, k);
+    pl.ws_bytes = pl.xs.end;
     return true;
 }
 
 template <bool XB, int MAXT>
-int tc_launch_t(const TcPlan& pl, const CUtensorMap& map, const TcParams& tp, cudaStream_t s) {
-    return launch(tc_gemm_kernel<XB, MAXT>, dim3(pl.grid), dim3(kTcThreads), pl.smem, s, map, tp);
+int tc_launch_t(const TcPlan& pl, const CUtensorMap& qmap, const CUtensorMap& xmap, const TcParams& tp,
+                cudaStream_t s) {
+    return launch(tc_gemm_kernel<XB, MAXT>, dim3(pl.grid), dim3(kTcThreads), pl.smem, s, qmap, xmap, tp);
 }
 
 template <bool XB>
-int tc_launch(int t, const TcPlan& pl, const CUtensorMap& map, const TcParams& tp, cudaStream_t s) {
-    if (t <= 1) return tc_launch_t<XB, 1>(pl, map, tp, s);
-    if (t <= 2) return tc_launch_t<XB, 2>(pl, map, tp, s);
-    if (t <= 4) return tc_launch_t<XB, 4>(pl, map, tp, s);
-    if (t <= 8) return tc_launch_t<XB, 8>(pl, map, tp, s);
-    if (t <= 16) return tc_launch_t<XB, 16>(pl, map, tp, s);
-    if (t <= 32) return tc_launch_t<XB, 32>(pl, map, tp, s);
-    return tc_launch_t<XB, 64>(pl, map, tp, s);
+int tc_launch(int t, const TcPlan& pl, const CUtensorMap& qmap, const CUtensorMap& xmap, const TcParams& tp,
+              cudaStream_t s) {
+    if (t <= 1) return tc_launch_t<XB, 1>(pl, qmap, xmap, tp, s);
+    if (t <= 2) return tc_launch_t<XB, 2>(pl, qmap, xmap, tp, s);
+    if (t <= 4) return tc_launch_t<XB, 4>(pl, qmap, xmap, tp, s);
+    if (t <= 8) return tc_launch_t<XB, 8>(pl, qmap, xmap, tp, s);
+    if (t <= 16) return tc_launch_t<XB, 16>(pl, qmap, xmap, tp, s);
+    if (t <= 32) return tc_launch_t<XB, 32>(pl, qmap, xmap, tp, s);
+    if constexpr (XB) return tc_launch_t<XB, 64>(pl, qmap, xmap, tp, s);
+    return OOMB_E_SHAPE;
 }
 
 // Grouped tensor-core plan: the chunk (assignments per unit) is the smallest of
-// 8, 16, 32, 64 that holds max_per_expert, shrunk until the rings fit one CTA
-// per SM; 512 tensor-memory columns hold nbufs accumulators of nmma columns.
+// 8, 16, 32, 64 that holds max_per_expert (at most 32 for fp32 x, whose six
+// terms a column make 192 B rows), shrunk until the rings fit one CTA per SM;
+// 512 tensor-memory columns hold nbufs accumulators of nmma columns.
 bool tg_plan(int max_per_expert, bool x_bf16, int n_experts, TgParams& tp, size_t& smem) {
-    const int ts = tc_ts(x_bf16), xb = x_bf16 ? 2 : 4;
+    const int ts = tc_ts(x_bf16);
     const int want = max_per_expert > 0 ? max_per_expert : 64;
+    const int ch_max = x_bf16 ? 64 : 32;
     int ch = 8;
-    while (ch < want && ch < 64) ch *= 2;
+    while (ch < want && ch < ch_max) ch *= 2;
     for (; ch >= 8; ch /= 2) {
         const int nmma = ch * ts;
+        if (nmma > kTcMaxN) continue;
         int nbufs = kTcAccBufs;
         while (nbufs > 2 && nbufs * nmma > 512) nbufs /= 2;
         if (nbufs * nmma > 512) continue;
         int cols = 32;
         while (cols < nbufs * nmma) cols *= 2;
-        int stages = kTcMaxStages, xdepth = kTcXDepth;
-        auto total = [&](int st, int xd) { return tg_smem_bytes(st, nmma, ch, ts, xb, xd, n_experts) + 1024; };
-        while (stages > kTcSplitters && total(stages, xdepth) > kTcSmemLimit1) stages--;
-        if (total(stages, xdepth) > kTcSmemLimit1) xdepth = 1;
-        if (total(stages, xdepth) > 227 * 1024) continue;
+        int stages = kTcMaxStages;
+        auto total = [&](int st) { return tg_smem_bytes(st, nmma, n_experts) + 1024; };
+        // the weight-copy warp keeps kTgLag tiles unreleased: the ring needs one more
+        while (stages > kTgLag + 1 && total(stages) > kTcSmemLimit1) stages--;
+        if (total(stages) > 227 * 1024) continue;
         tp.chunk = ch;
         tp.nmma = nmma;
         tp.nbufs = nbufs;
         tp.tmem_cols = cols;
         tp.stages = stages;
-        tp.xdepth = xdepth;
-        smem = total(stages, xdepth);
+        smem = total(stages);
         return true;
     }
     return false;
 }
 
 template <bool XB>
-int tg_launch(const TgParams& tp, int grid, size_t smem, cudaStream_t s) {
+int tg_launch(const TgParams& tp, const CUtensorMap& xmap, int grid, size_t smem, cudaStream_t s) {
     switch (tp.chunk) {
-        case 8: return launch(tc_group_kernel<XB, 8>, dim3(grid), dim3(kTcThreads), smem, s, tp);
-        case 16: return launch(tc_group_kernel<XB, 16>, dim3(grid), dim3(kTcThreads), smem, s, tp);
-        case 32: return launch(tc_group_kernel<XB, 32>, dim3(grid), dim3(kTcThreads), smem, s, tp);
-        default: return launch(tc_group_kernel<XB, 64>, dim3(grid), dim3(kTcThreads), smem, s, tp);
+        case 8: return launch(tc_group_kernel<XB, 8>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
+        case 16: return launch(tc_group_kernel<XB, 16>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
+        case 32: return launch(tc_group_kernel<XB, 32>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
+        default:
+            if constexpr (XB) return launch(tc_group_kernel<XB, 64>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
+            return OOMB_E_SHAPE;
     }
 }
 
@@ -573,15 +614,32 @@ int oomb_gemm_fp8_tc(const void* x, int x_dtype, const uint8_t* q, int q_format,
     if (t == 0) return OOMB_OK;
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
+    const bool xb = x_dtype == OOMB_BF16;
     TcPlan pl{};
-    if (!tc_plan(d, t, n, k, x_dtype == OOMB_BF16, pl)) return OOMB_E_SHAPE;
+    if (!tc_plan(d, t, n, k, xb, pl)) return OOMB_E_SHAPE;
     if (workspace_bytes < pl.ws_bytes) return OOMB_E_WORKSPACE;
-    CUtensorMap map;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    CUtensorMap qmap, xmap;
     const bool packed = q_format == OOMB_Q_TILES;
-    if (!(packed ? encode_fp8_tiles(&map, q, pl.tiles * kTcTile, kTcTile) : encode_fp8_tiles(&map, q, n, k)))
+    if (!(packed ? encode_fp8_tiles(&qmap, q, pl.tiles * kTcTile, kTcTile) : encode_fp8_tiles(&qmap, q, n, k)) ||
+        !encode_u8_tiles(&xmap, ws + pl.xs.xs_off, pl.xs.rows_alloc, k, pl.nmma))
         return OOMB_E_LAUNCH;
+    // 1. split x once into e4m3 terms (rows past t * TS are zero terms)
+    XsParams xp{};
+    xp.x = x;
+    xp.a_host = t;
+    xp.a_cover = (pl.nmma + tc_ts(xb) - 1) / tc_ts(xb);
+    xp.zero_pad = 1;
+    xp.K = k;
+    xp.kblocks = pl.kblocks;
+    xp.xs = ws + pl.xs.xs_off;
+    xp.rows_alloc = pl.xs.rows_alloc;
+    xp.sx = reinterpret_cast<float*>(ws + pl.xs.sx_off);
+    xp.sx_stride = pl.xs.sx_stride;
+    int rc = launch_xsplit(xb, xp, stream);
+    if (rc) return rc;
+    // 2. the GEMM, its weight stream starting under the split
     TcParams tp{};
-    tp.x = x;
     tp.T = t;
     tp.K = k;
     tp.nrows = n;
@@ -589,53 +647,86 @@ int oomb_gemm_fp8_tc(const void* x, int x_dtype, const uint8_t* q, int q_format,
     tp.layout = scale_layout;
     tp.y = y;
     tp.y_bf16 = y_dtype == OOMB_BF16;
-    tp.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) + pl.counters_off);
-    tp.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partial_off);
+    tp.counters = reinterpret_cast<unsigned*>(ws + pl.counters_off);
+    tp.partial = reinterpret_cast<float*>(ws + pl.partial_off);
+    tp.sx = xp.sx;
+    tp.sx_stride = xp.sx_stride;
     tp.tiles = pl.tiles;
     tp.kblocks = pl.kblocks;
     tp.q_tiles = packed;
     tp.nmma = pl.nmma;
     tp.stages = pl.stages;
     tp.nbufs = pl.nbufs;
-    tp.xdepth = pl.xdepth;
     tp.tmem_cols = pl.tmem_cols;
     tp.err = d->err;
-    return x_dtype == OOMB_BF16 ? tc_launch<true>(t, pl, map, tp, stream) : tc_launch<false>(t, pl, map, tp, stream);
+    return xb ? tc_launch<true>(t, pl, qmap, xmap, tp, stream) : tc_launch<false>(t, pl, qmap, xmap, tp, stream);
+}
+
+size_t oomb_moe_tiled_fp8_workspace_bytes(int max_assignments, int k, int x_dtype) {
+    if (max_assignments <= 0 || k <= 0 || k % kTcTile || (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16)) return 0;
+    return xs_layout(0, max_assignments * tc_ts(x_dtype == OOMB_BF16), k).end;
 }
 
 int oomb_moe_tiled_fp8(const uint64_t* recs, const int32_t* off, const int32_t* rows, int n_experts,
-                       int max_per_expert, const void* x, int x_dtype, float* y, int n, int k, int64_t w_off,
-                       int64_t s_off, int scale_layout, oomb_stream stream) {
-    if (!recs || !off || !x || !y) return OOMB_E_ARG;
+                       int max_per_expert, int max_assignments, const void* x, int x_dtype, float* y, int n, int k,
+                       int64_t w_off, int64_t s_off, int scale_layout, void* workspace, size_t workspace_bytes,
+                       oomb_stream stream) {
+    if (!recs || !off || !x || !y || !workspace) return OOMB_E_ARG;
     if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) ||
         (scale_layout != OOMB_SCALE_1X128 && scale_layout != OOMB_SCALE_128X128) || max_per_expert < 0)
         return OOMB_E_ARG;
-    if (n <= 0 || k <= 0 || n % kTcTile || k % kTcTile || n_experts < 0 || n_experts > kTgMaxExperts)
+    if (n <= 0 || k <= 0 || n % kTcTile || k % kTcTile || n_experts < 0 || n_experts > kTgMaxExperts ||
+        max_assignments <= 0)
         return OOMB_E_SHAPE;
-    if (!aligned16(x) || !aligned16(y) || (w_off & 15) || (s_off & 3) || w_off < 0 || s_off < 0)
+    if (!aligned16(x) || !aligned16(y) || !aligned16(workspace) || (w_off & 15) || (s_off & 3) || w_off < 0 ||
+        s_off < 0)
         return OOMB_E_ALIGN;
     if (n_experts == 0) return OOMB_OK;
+    const bool xb = x_dtype == OOMB_BF16;
+    const XsLayout xl = xs_layout(0, max_assignments * tc_ts(xb), k);
+    if (workspace_bytes < xl.end) return OOMB_E_WORKSPACE;
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
     TgParams tp{};
     size_t smem = 0;
-    if (!tg_plan(max_per_expert, x_dtype == OOMB_BF16, n_experts, tp, smem)) return OOMB_E_SHAPE;
+    if (!tg_plan(max_per_expert, xb, n_experts, tp, smem)) return OOMB_E_SHAPE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    CUtensorMap xmap;
+    if (!encode_u8_tiles(&xmap, ws + xl.xs_off, xl.rows_alloc, k, tp.nmma)) return OOMB_E_LAUNCH;
+    // 1. split every assignment's row (through `rows`) once into e4m3 terms;
+    //    the assignment count is off[n_experts], on the device
+    XsParams xp{};
+    xp.x = x;
+    xp.rows = rows;
+    xp.first = off;
+    xp.count = off + n_experts;
+    xp.a_cover = max_assignments;
+    xp.zero_pad = 0;
+    xp.K = k;
+    xp.kblocks = k / kTcTile;
+    xp.xs = ws + xl.xs_off;
+    xp.rows_alloc = xl.rows_alloc;
+    xp.sx = reinterpret_cast<float*>(ws + xl.sx_off);
+    xp.sx_stride = xl.sx_stride;
+    int rc = launch_xsplit(xb, xp, stream);
+    if (rc) return rc;
+    // 2. the grouped GEMM
     tp.recs = recs;
     tp.off = off;
-    tp.rows = rows;
     tp.n_experts = n_experts;
-    tp.x = x;
+    tp.a_max = max_assignments;
     tp.K = k;
     tp.N = n;
     tp.w_off = w_off;
     tp.s_off = s_off;
     tp.layout = scale_layout;
     tp.y = y;
+    tp.sx = xp.sx;
+    tp.sx_stride = xp.sx_stride;
     tp.rblocks = n / kTcTile;
     tp.kblocks = k / kTcTile;
     tp.err = d->err;
-    return x_dtype == OOMB_BF16 ? tg_launch<true>(tp, d->sms, smem, stream)
-                                : tg_launch<false>(tp, d->sms, smem, stream);
+    return xb ? tg_launch<true>(tp, xmap, d->sms, smem, stream) : tg_launch<false>(tp, xmap, d->sms, smem, stream);
 }
 
 int oomb_moe_swiglu_range(const float* g, const float* u, float* h, int64_t start, int64_t end,
@@ -842,8 +933,91 @@ int oomb_moe_combine(const float* routed, const float* shared, const float* gate
     if (t == 0) return OOMB_OK;
     if (!device_state()) return OOMB_E_DEVICE;
     const int64_t n = static_cast<int64_t>(t) * h;
-    return launch(moe_combine_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream,
-                  routed, shared, gate_logit, out, t, h);
+    return launch(moe_combine_kernel<false>, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream,
+                  routed, shared, gate_logit, static_cast<void*>(out), t, h);
+}
+
+// ---- decode attention ----------------------------------------------------------
+
+namespace {
+struct AttnPlan {
+    int splits;
+    size_t counters_off, part_off, ws_bytes;
+};
+
+bool attn_plan(const DeviceState* d, int batch, int heads, int kv_heads, int head_dim, int kv_max, AttnPlan& pl) {
+    if (batch <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim != 128 || kv_max < 0) return false;
+    const int G = heads / kv_heads;
+    if (G != 1 && G != 2 && G != 4 && G != 8) return false;
+    const int64_t pairs = static_cast<int64_t>(batch) * kv_heads;
+    if (pairs > 65535LL * 65535LL) return false;
+    // about four CTAs of four warps per SM, each warp at least one chunk of positions
+    const int64_t want = (static_cast<int64_t>(d->sms) * 4 + pairs - 1) / pairs;
+    const int cp = 32 / G < 8 ? 32 / G : 8;
+    const int64_t most = (static_cast<int64_t>(kv_max) + cp * kAttnWarps - 1) / (cp * kAttnWarps);
+    pl.splits = static_cast<int>(want < most ? want : (most > 0 ? most : 1));
+    if (pl.splits < 1) pl.splits = 1;
+    if (pl.splits > 65535) pl.splits = 65535;
+    pl.counters_off = 0;
+    pl.part_off = (static_cast<size_t>(pairs) * 4 + 255) & ~static_cast<size_t>(255);
+    pl.ws_bytes = pl.part_off + static_cast<size_t>(pairs) * pl.splits * kAttnWarps * G * (head_dim + 4) * 4;
+    return true;
+}
+}  // namespace
+
+size_t oomb_attention_decode_workspace_bytes(int batch, int heads, int kv_heads, int head_dim, int kv_max) {
+    const DeviceState* d = device_state();
+    AttnPlan pl{};
+    if (!d || !attn_plan(d, batch, heads, kv_heads, head_dim, kv_max, pl)) return 0;
+    return pl.ws_bytes;
+}
+
+int oomb_attention_decode(const void* q, int q_dtype, const uint16_t* k_cache, const uint16_t* v_cache,
+                          int64_t seq_stride, const int32_t* kv_len, int kv_len_all, void* out, int out_dtype,
+                          int batch, int heads, int kv_heads, int head_dim, int kv_max, float scale, void* workspace,
+                          size_t workspace_bytes, oomb_stream stream) {
+    if (!q || !k_cache || !v_cache || !out || !workspace) return OOMB_E_ARG;
+    if ((q_dtype != OOMB_F32 && q_dtype != OOMB_BF16) || (out_dtype != OOMB_F32 && out_dtype != OOMB_BF16))
+        return OOMB_E_ARG;
+    if (batch < 0 || kv_max < 0 || seq_stride < 0 || (!kv_len && (kv_len_all < 0 || kv_len_all > kv_max)))
+        return OOMB_E_SHAPE;
+    if (batch > 1 && seq_stride < static_cast<int64_t>(kv_max) * kv_heads * head_dim) return OOMB_E_SHAPE;
+    if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) || !aligned16(workspace) ||
+        (seq_stride % 8))
+        return OOMB_E_ALIGN;
+    if (batch == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    AttnPlan pl{};
+    if (!attn_plan(d, batch, heads, kv_heads, head_dim, kv_max, pl)) return OOMB_E_SHAPE;
+    if (workspace_bytes < pl.ws_bytes) return OOMB_E_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    AttnParams p{};
+    p.q = q;
+    p.q_bf16 = q_dtype == OOMB_BF16;
+    p.k = k_cache;
+    p.v = v_cache;
+    p.seq_stride = seq_stride;
+    p.kv_len = kv_len;
+    p.kv_len_host = kv_len_all;
+    p.out = out;
+    p.out_bf16 = out_dtype == OOMB_BF16;
+    p.B = batch;
+    p.H = heads;
+    p.Hkv = kv_heads;
+    p.kv_max = kv_max;
+    p.splits = pl.splits;
+    p.scale = scale;
+    p.part = reinterpret_cast<float*>(ws + pl.part_off);
+    p.counters = reinterpret_cast<unsigned*>(ws + pl.counters_off);
+    p.err = d->err;
+    const dim3 grid(static_cast<unsigned>(pl.splits), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
+    switch (heads / kv_heads) {
+        case 1: return launch(attn_decode_kernel<1, 128>, grid, dim3(kAttnThreads), 0, stream, p);
+        case 2: return launch(attn_decode_kernel<2, 128>, grid, dim3(kAttnThreads), 0, stream, p);
+        case 4: return launch(attn_decode_kernel<4, 128>, grid, dim3(kAttnThreads), 0, stream, p);
+        default: return launch(attn_decode_kernel<8, 128>, grid, dim3(kAttnThreads), 0, stream, p);
+    }
 }
 
 // ---- fused decode ------------------------------------------------------------
@@ -1022,6 +1196,113 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K)
                : launch(combine_slots_kernel<false>, cgrid, dim3(256), 0, stream, static_cast<const float*>(y),
                         static_cast<const int32_t*>(rp.slot_assign), static_cast<const float*>(rp.weights), out, t, H, K);
+}
+
+// ---- a whole MoE layer: shared expert + routed experts --------------------------
+
+namespace {
+struct LayerLayout {
+    size_t dec, routed, gu, sact, shared, gate, tc1, tc2, total;
+    size_t dec_bytes, tc1_bytes, tc2_bytes;
+};
+
+int check_shared(const oomb_shared_expert* S, const oomb_moe_layer* L) {
+    if (!S || !S->gate_up_q || !S->gate_up_scale || !S->down_q || !S->down_scale) return OOMB_E_ARG;
+    if (S->scale_layout != OOMB_SCALE_1X128 && S->scale_layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (S->hidden != L->hidden || S->inter <= 0 || S->inter % 16) return OOMB_E_SHAPE;
+    if (!aligned16(S->gate_up_q) || !aligned16(S->gate_up_scale) || !aligned16(S->down_q) ||
+        !aligned16(S->down_scale) || (S->gate_w && !aligned16(S->gate_w)))
+        return OOMB_E_ALIGN;
+    return OOMB_OK;
+}
+
+bool layer_layout(const DeviceState* d, int t, const oomb_moe_layer* L, const oomb_shared_expert* S, bool x_bf16,
+                  LayerLayout& w) {
+    const size_t T = t, H = L->hidden, SI = S->inter;
+    w = LayerLayout{};
+    w.dec_bytes = decode_layout(t, L).total;
+    TcPlan p1{}, p2{};
+    // the shared expert's two GEMVs take the tensor cores from two tokens when the shapes allow
+    if (t >= kTcMinTokens && tc_plan(d, t, static_cast<int>(2 * SI), static_cast<int>(H), x_bf16, p1))
+        w.tc1_bytes = p1.ws_bytes;
+    if (t >= kTcMinTokens && tc_plan(d, t, static_cast<int>(H), static_cast<int>(SI), false, p2))
+        w.tc2_bytes = p2.ws_bytes;
+    size_t o = 0;
+    w.dec = o; o = up256(o + w.dec_bytes);
+    w.tc1 = o; o = up256(o + w.tc1_bytes);
+    w.tc2 = o; o = up256(o + w.tc2_bytes);
+    w.routed = o; o = up256(o + T * H * 4);
+    w.gu = o; o = up256(o + T * 2 * SI * 4);
+    w.sact = o; o = up256(o + T * SI * 4);
+    w.shared = o; o = up256(o + T * H * 4);
+    w.gate = o; o = up256(o + T * 4);
+    w.total = o;
+    return true;
+}
+}  // namespace
+
+size_t oomb_moe_layer_workspace_bytes(int t, const oomb_moe_layer* layer, const oomb_shared_expert* shared,
+                                      int x_dtype) {
+    if (t <= 0 || check_layer(layer) != OOMB_OK || check_shared(shared, layer) != OOMB_OK) return 0;
+    if (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) return 0;
+    const DeviceState* d = device_state();
+    LayerLayout w;
+    if (!d || !layer_layout(d, t, layer, shared, x_dtype == OOMB_BF16, w)) return 0;
+    return w.total;
+}
+
+int oomb_moe_layer_decode_fp8(const oomb_moe_layer* L, const oomb_shared_expert* S, const void* x, int x_dtype,
+                              int t, void* out, int out_dtype, int32_t* ids, float* weights, void* workspace,
+                              size_t workspace_bytes, oomb_stream stream) {
+    int rc = check_layer(L);
+    if (rc) return rc;
+    if ((rc = check_shared(S, L))) return rc;
+    if (!x || !out || !workspace) return OOMB_E_ARG;
+    if ((x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) || (out_dtype != OOMB_F32 && out_dtype != OOMB_BF16))
+        return OOMB_E_ARG;
+    if (t < 0) return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(out) || !aligned16(workspace)) return OOMB_E_ALIGN;
+    if (t == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    LayerLayout w;
+    if (!layer_layout(d, t, L, S, x_dtype == OOMB_BF16, w)) return OOMB_E_SHAPE;
+    if (workspace_bytes < w.total) return OOMB_E_WORKSPACE;
+    const void* unused = nullptr;
+    if (mem_kind(x, &unused) != Mem::device || mem_kind(out, &unused) != Mem::device) return OOMB_E_ARG;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const int H = L->hidden, SI = S->inter;
+    float* gu = reinterpret_cast<float*>(ws + w.gu);
+    float* sact = reinterpret_cast<float*>(ws + w.sact);
+    float* shared = reinterpret_cast<float*>(ws + w.shared);
+    float* gate = reinterpret_cast<float*>(ws + w.gate);
+    float* routed = reinterpret_cast<float*>(ws + w.routed);
+    // 1. the shared expert (gate/up GEMV, SwiGLU, down GEMV) and its gate logit
+    //    (Moe::shared, crates/oominf-models-qwen/src/moe.rs:498-527), queued first
+    rc = oomb_gemm_fp8(x, x_dtype, S->gate_up_q, S->gate_up_scale, S->scale_layout, gu, OOMB_F32, t, 2 * SI, H,
+                       w.tc1_bytes ? ws + w.tc1 : nullptr, w.tc1_bytes, stream);
+    if (rc) return rc;
+    rc = oomb_silu_mul_rows(gu, sact, OOMB_F32, t, SI, stream);
+    if (rc) return rc;
+    rc = oomb_gemm_fp8(sact, OOMB_F32, S->down_q, S->down_scale, S->scale_layout, shared, OOMB_F32, t, H, SI,
+                       w.tc2_bytes ? ws + w.tc2 : nullptr, w.tc2_bytes, stream);
+    if (rc) return rc;
+    if (S->gate_w) {
+        rc = oomb_router_logits(x, x_dtype, S->gate_w, gate, t, 1, H, stream);
+        if (rc) return rc;
+    }
+    // 2. the routed experts: the fused decode step, fp32 out
+    rc = oomb_moe_decode_fp8(L, x, x_dtype, t, routed, OOMB_F32, ids, weights, ws + w.dec, w.dec_bytes, stream);
+    if (rc) return rc;
+    // 3. out = routed + sigmoid(gate) * shared (moe_combine, ops.cu:311-316)
+    const int64_t n = static_cast<int64_t>(t) * H;
+    const dim3 grid(static_cast<unsigned>((n + 255) / 256));
+    const float* g = S->gate_w ? gate : nullptr;
+    return out_dtype == OOMB_BF16
+               ? launch(moe_combine_kernel<true>, grid, dim3(256), 0, stream, static_cast<const float*>(routed),
+                        static_cast<const float*>(shared), g, out, t, H)
+               : launch(moe_combine_kernel<false>, grid, dim3(256), 0, stream, static_cast<const float*>(routed),
+                        static_cast<const float*>(shared), g, out, t, H);
 }
 
 namespace {
@@ -1395,6 +1676,228 @@ int oomb_event_destroy(oomb_event ev) {
 int oomb_copies_sync(oomb_copy_queue queue) {
     if (!queue) return OOMB_E_ARG;
     return cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(queue)) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+// ---- expert tiers: device slots over a pinned host arena --------------------------
+
+struct oomb_policy_st {
+    oomb::TierPolicy* p;
+};
+
+int oomb_policy_create(const char* spec, oomb_policy* policy) {
+    if (!policy) return OOMB_E_ARG;
+    *policy = nullptr;
+    TierPolicy* p = make_policy(spec);
+    if (!p) return OOMB_E_ARG;
+    *policy = new oomb_policy_st{p};
+    return OOMB_OK;
+}
+
+int oomb_policy_destroy(oomb_policy policy) {
+    if (!policy) return OOMB_E_ARG;
+    delete policy->p;
+    delete policy;
+    return OOMB_OK;
+}
+
+int oomb_policy_touch(oomb_policy policy, uint32_t key, uint64_t now) {
+    if (!policy) return OOMB_E_ARG;
+    policy->p->touch(key, now);
+    return OOMB_OK;
+}
+
+int oomb_policy_remove(oomb_policy policy, uint32_t key) {
+    if (!policy) return OOMB_E_ARG;
+    policy->p->remove(key);
+    return OOMB_OK;
+}
+
+int64_t oomb_policy_victim(oomb_policy policy, const uint32_t* pinned, int n_pinned) {
+    if (!policy || n_pinned < 0 || (n_pinned > 0 && !pinned)) return OOMB_E_ARG;
+    std::set<uint32_t> pin(pinned, pinned + n_pinned);
+    return policy->p->victim([&](uint32_t k) { return pin.count(k) != 0; });
+}
+
+struct oomb_tier_st {
+    oomb::Tier t;
+};
+
+int oomb_tier_create(const void* host_arena, size_t record_stride, int layers, int experts, void* device_slots,
+                     int slots, const char* policy, oomb_tier* tier) {
+    if (!tier) return OOMB_E_ARG;
+    *tier = nullptr;
+    if (!host_arena || !device_slots || record_stride == 0 || layers <= 0 || experts <= 0 || slots <= 0)
+        return OOMB_E_ARG;
+    if (static_cast<int64_t>(layers) * experts > 0xffffffffLL) return OOMB_E_SHAPE;
+    if (!device_state()) return OOMB_E_DEVICE;
+    const void* unused = nullptr;
+    if (mem_kind(host_arena, &unused) != Mem::host || mem_kind(device_slots, &unused) != Mem::device)
+        return OOMB_E_ARG;
+    TierPolicy* p = make_policy(policy);
+    if (!p) return OOMB_E_ARG;
+    auto* st = new oomb_tier_st{};
+    Tier& t = st->t;
+    t.host_base = static_cast<const uint8_t*>(host_arena);
+    t.device_base = static_cast<uint8_t*>(device_slots);
+    t.stride = record_stride;
+    t.layers = layers;
+    t.experts = experts;
+    t.slots = slots;
+    t.policy = p;
+    t.key_of.assign(slots, -1);
+    for (int i = slots - 1; i >= 0; i--) t.free_slots.push_back(i);
+    if (cudaStreamCreateWithFlags(&t.queue, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t.compute_ev, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t.copies_ev, cudaEventDisableTiming) != cudaSuccess) {
+        if (t.queue) cudaStreamDestroy(t.queue);
+        if (t.compute_ev) cudaEventDestroy(t.compute_ev);
+        delete p;
+        delete st;
+        return OOMB_E_LAUNCH;
+    }
+    *tier = st;
+    return OOMB_OK;
+}
+
+int oomb_tier_destroy(oomb_tier tier) {
+    if (!tier) return OOMB_E_ARG;
+    Tier& t = tier->t;
+    cudaStreamSynchronize(t.queue);
+    cudaEventDestroy(t.compute_ev);
+    cudaEventDestroy(t.copies_ev);
+    cudaStreamDestroy(t.queue);
+    delete t.policy;
+    delete tier;
+    return OOMB_OK;
+}
+
+int oomb_tier_finish_fetch(oomb_tier tier, oomb_stream compute) {
+    if (!tier) return OOMB_E_ARG;
+    Tier& t = tier->t;
+    if (!t.open) return OOMB_OK;
+    t.open = false;
+    if (cudaEventRecord(t.copies_ev, t.queue) != cudaSuccess) return OOMB_E_LAUNCH;
+    return cudaStreamWaitEvent(compute, t.copies_ev, 0) == cudaSuccess ? OOMB_OK : OOMB_E_LAUNCH;
+}
+
+int oomb_tier_begin_fetch(oomb_tier tier, oomb_stream compute, int layer, const int32_t* experts, int n,
+                          uint64_t* addrs, uint8_t* ready) {
+    if (!tier || (n > 0 && (!experts || !addrs || !ready)) || n < 0) return OOMB_E_ARG;
+    Tier& t = tier->t;
+    if (layer < 0 || layer >= t.layers) return OOMB_E_SHAPE;
+    for (int i = 0; i < n; i++)
+        if (experts[i] < 0 || experts[i] >= t.experts) return OOMB_E_SHAPE;
+    int rc = oomb_tier_finish_fetch(tier, compute);
+    if (rc) return rc;
+    std::set<uint32_t> wanted;
+    for (int i = 0; i < n; i++) wanted.insert(static_cast<uint32_t>(layer) * t.experts + experts[i]);
+    // refuse before touching anything when the slots cannot hold the fetch: its
+    // missing records need free slots or residents it does not want
+    size_t resident_wanted = 0;
+    for (uint32_t k : wanted) resident_wanted += t.slot_of.count(k);
+    const size_t missing = wanted.size() - resident_wanted;
+    if (missing > t.free_slots.size() + (t.slot_of.size() - resident_wanted)) return OOMB_E_SHAPE;
+    // every slot this fetch fills may still be read by compute issued before it
+    if (cudaEventRecord(t.compute_ev, compute) != cudaSuccess || cudaStreamWaitEvent(t.queue, t.compute_ev, 0) != cudaSuccess)
+        return OOMB_E_LAUNCH;
+    std::unordered_map<uint32_t, bool> placed;  // keys filled by this fetch (not ready yet)
+    for (int i = 0; i < n; i++) {
+        const uint32_t key = static_cast<uint32_t>(layer) * t.experts + experts[i];
+        t.stats.requests++;
+        auto it = t.slot_of.find(key);
+        if (it != t.slot_of.end()) {
+            const bool fresh = placed.count(key) != 0;
+            if (!fresh) t.stats.hits++;
+            addrs[i] = reinterpret_cast<uint64_t>(t.device_base + static_cast<size_t>(it->second) * t.stride);
+            ready[i] = fresh ? 0 : 1;
+            t.policy->touch(key, t.now++);
+            continue;
+        }
+        int slot;
+        if (!t.free_slots.empty()) {
+            slot = t.free_slots.back();
+            t.free_slots.pop_back();
+        } else {
+            const int64_t v = t.policy->victim([&](uint32_t k) { return wanted.count(k) != 0; });
+            if (v < 0) return OOMB_E_SHAPE;  // unreachable after the capacity check
+            const uint32_t vk = static_cast<uint32_t>(v);
+            slot = t.slot_of[vk];
+            t.slot_of.erase(vk);
+            t.policy->remove(vk);
+            t.stats.evictions++;
+        }
+        t.slot_of[key] = slot;
+        t.key_of[slot] = key;
+        placed[key] = true;
+        t.stats.misses++;
+        uint8_t* dst = t.device_base + static_cast<size_t>(slot) * t.stride;
+        const uint8_t* src = t.host_base + static_cast<size_t>(key) * t.stride;
+        if (cudaMemcpyAsync(dst, src, t.stride, cudaMemcpyHostToDevice, t.queue) != cudaSuccess) return OOMB_E_LAUNCH;
+        t.stats.bytes_copied += t.stride;
+        addrs[i] = reinterpret_cast<uint64_t>(dst);
+        ready[i] = 0;
+        t.policy->touch(key, t.now++);
+    }
+    t.open = true;
+    return OOMB_OK;
+}
+
+int oomb_tier_stats(oomb_tier tier, uint64_t* out5) {
+    if (!tier || !out5) return OOMB_E_ARG;
+    const TierStats& s = tier->t.stats;
+    out5[0] = s.requests;
+    out5[1] = s.hits;
+    out5[2] = s.misses;
+    out5[3] = s.evictions;
+    out5[4] = s.bytes_copied;
+    return OOMB_OK;
+}
+
+// ---- FP8 expert records: layout and load-time conversion ----------------------
+
+int oomb_fp8_record_layout(int64_t hidden, int64_t inter, int scale_layout, oomb_fp8_record* geo, size_t* stride) {
+    if (!geo || !stride) return OOMB_E_ARG;
+    if (scale_layout != OOMB_SCALE_1X128 && scale_layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (hidden <= 0 || inter <= 0 || hidden % 16 || inter % 16) return OOMB_E_SHAPE;
+    auto up = [](int64_t v, int64_t a) { return (v + a - 1) / a * a; };
+    auto sbytes = [&](int64_t n, int64_t k) {
+        const int64_t rows = scale_layout == OOMB_SCALE_128X128 ? (n + 127) / 128 : n;
+        return rows * ((k + 127) / 128) * 4;
+    };
+    const int64_t H = hidden, I = inter;
+    int64_t o = 0;
+    oomb_fp8_record g{};
+    g.hidden = H;
+    g.inter = I;
+    g.layout = scale_layout;
+    g.gate_weight = o; o = up(o + I * H, OOMB_PART_ALIGN);
+    g.up_weight = o; o = up(o + I * H, OOMB_PART_ALIGN);
+    g.down_weight = o; o = up(o + H * I, OOMB_PART_ALIGN);
+    g.gate_scale = o; o = up(o + sbytes(I, H), OOMB_PART_ALIGN);
+    g.up_scale = o; o = up(o + sbytes(I, H), OOMB_PART_ALIGN);
+    g.down_scale = o; o = up(o + sbytes(H, I), OOMB_PART_ALIGN);
+    *geo = g;
+    *stride = static_cast<size_t>(up(o, OOMB_RECORD_ALIGN));
+    return OOMB_OK;
+}
+
+int oomb_quantize_fp8_record(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                             const oomb_fp8_record* geo, uint8_t* record, oomb_stream stream) {
+    if (!gate || !up || !down || !geo || !record) return OOMB_E_ARG;
+    if (geo->layout != OOMB_SCALE_1X128 && geo->layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    if (geo->hidden <= 0 || geo->inter <= 0 || geo->hidden > 0x7fffffff || geo->inter > 0x7fffffff) return OOMB_E_SHAPE;
+    if (!aligned16(record) || ((geo->gate_weight | geo->up_weight | geo->down_weight | geo->gate_scale |
+                                geo->up_scale | geo->down_scale) & 15))
+        return OOMB_E_ALIGN;
+    const int H = static_cast<int>(geo->hidden), I = static_cast<int>(geo->inter);
+    int rc = oomb_quantize_fp8(gate, I, H, geo->layout, record + geo->gate_weight,
+                               reinterpret_cast<float*>(record + geo->gate_scale), stream);
+    if (rc) return rc;
+    rc = oomb_quantize_fp8(up, I, H, geo->layout, record + geo->up_weight,
+                           reinterpret_cast<float*>(record + geo->up_scale), stream);
+    if (rc) return rc;
+    return oomb_quantize_fp8(down, H, I, geo->layout, record + geo->down_weight,
+                             reinterpret_cast<float*>(record + geo->down_scale), stream);
 }
 
 int oomb_quantize_fp8(const uint16_t* w, int n, int k, int scale_layout, uint8_t* q, float* scale,

@@ -91,15 +91,26 @@ __global__ void silu_mul_rows_kernel(const float* gu, void* y, int rows, int n) 
     }
 }
 
-// out = routed + sigmoid(gate_logit[t]) * shared (ops.cu:311-316).
-__global__ void moe_combine_kernel(const float* routed, const float* shared, const float* gate_logit,
-                                   float* out, int T, int H) {
+// out = routed + sigmoid(gate_logit[t]) * shared (ops.cu:311-316); with no
+// gate_logit (a shared expert without a gate) out = routed + shared.  out fp32
+// or bf16 (RN of the fp32 sum).
+template <bool OUT_BF16>
+__global__ void moe_combine_kernel(const float* routed, const float* shared, const float* gate_logit, void* out,
+                                   int T, int H) {
     pdl_wait();
     pdl_launch_dependents();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<int64_t>(T) * H) return;
-    const float g = gate_logit[i / H];
-    out[i] = routed[i] + (1.0f / (1.0f + expf(-g))) * shared[i];
+    const float r = __ldcg(routed + i), sh = __ldcg(shared + i);
+    float v;
+    if (gate_logit) {
+        const float g = __ldcg(gate_logit + i / H);
+        v = r + (1.0f / (1.0f + expf(-g))) * sh;
+    } else {
+        v = r + sh;
+    }
+    if (OUT_BF16) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else static_cast<float*>(out)[i] = v;
 }
 
 }  // namespace oomb

@@ -5,31 +5,35 @@
 // summation order differs.
 //
 // The weights never pass through registers: TMA copies 128 x 128 e4m3 tiles of
-// q (row-major) into a shared-memory ring in the canonical K-major 128-byte
-// swizzled layout, and tcgen05.mma (kind::f8f6f4, M = 128, K = 32) reads them
-// from there.  The activations enter as the B operand: every 128-column block of
-// x[t] is split exactly into e4m3 terms with power-of-two scales,
-//   x = s1 * q1 + s2 * q2 (+ s3 * q3 + s4 * q4 for fp32 x),
+// q (row-major, or the packed tile layout) into a shared-memory ring in the
+// canonical K-major 128-byte swizzled layout, and tcgen05.mma (kind::f8f6f4,
+// M = 128, K = 32) reads them from there.  The activations enter as the B
+// operand, split once per call by xsplit_kernel: every 128-column block of an
+// activation row is written as TS e4m3 terms with power-of-two scales,
+//   x = s1 * q1 + s2 * q2 + ... + s_TS * q_TS,
 // q_i = e4m3(residual / s_i), s_i chosen so the block's largest residual lands
-// in [128, 256).  A bf16 value has 8 significant bits and an e4m3 term carries
-// 4, so two terms reproduce every bf16 activation within 2^14 of its block's
-// largest exactly (smaller ones to within 2^-20 of the largest); fp32
-// activations take four terms (16 bits).  Each (token, term) is one column of
-// B (a token owns TS = 2 or 4 consecutive columns), so one MMA gives every
-// term's partial dot product for a 128-row tile.  Accumulators live in tensor
-// memory one K block (128 columns, one weight scale) at a time, up to four
-// tiles in flight; an epilogue warpgroup folds each block into fp32 registers,
-//   acc = fma(w_scale, ((s1 * D1 + s2 * D2) (+ s3 * D3) (+ s4 * D4)), acc),
+// in [128, 256).  An e4m3 term carries 4 significant bits of each value, so the
+// largest residual shrinks by 2^-4 per term: two terms reproduce every bf16
+// activation (8 significant bits) within 2^14 of its block's largest exactly,
+// and fp32 activations take six terms, which keep every value to within
+// 2^-24 of its block's largest (24 significant bits, the fp32 mantissa).
+// The terms land in a workspace image [rows = assignment * TS + term, K] that
+// TMA copies tile by tile (nmma rows x 128 bytes, 128-byte swizzle) into the B
+// ring beside the weights, with the tile's term scales; so the split costs one
+// pass over x per call instead of one per weight tile.  Each (token, term) is
+// one column of B, so one MMA gives every term's partial dot product for a
+// 128-row tile.  Accumulators live in tensor memory one K block (128 columns,
+// one weight scale) at a time, up to four tiles in flight; an epilogue
+// warpgroup folds each block into fp32 registers,
+//   acc = fma(w_scale, s1 * D1 + s2 * D2 + ... + s_TS * D_TS, acc),
 // K blocks in order.
 // Tiles (row block, K block) are split contiguously over the CTAs (stream-K);
 // a row block split over several CTAs is summed by the last CTA to finish, in
 // CTA order (deterministic), through a caller workspace.
 //
-// Warp roles (10 warps): 0 TMA producer, 1 MMA issuer and tensor-memory owner,
-// 2-5 epilogue (warp w reads tensor-memory lanes 32*(w%4)..+31), 6-9 activation
-// splitters (tile i goes to splitter (i - first tile) % 4, which streams the
-// tile's 128-column slices of every token into its own shared-memory ring with
-// bulk copies, its ring's depth ahead).
+// Warp roles (7 warps): 0 weight TMA producer, 1 MMA issuer and tensor-memory
+// owner, 2-5 epilogue (warp w reads tensor-memory lanes 32*(w%4)..+31), 6 the
+// B loader (split activations and term scales, after the dependency wait).
 // Every wait is bounded and records an error code.
 #pragma once
 
@@ -39,22 +43,28 @@
 
 namespace oomb {
 
-constexpr int kTcThreads = 320;
-constexpr int kTcSplitters = 4;
+constexpr int kTcThreads = 224;             // 7 warps: TMA producer, MMA, 4 epilogue, B loader
 constexpr int kTcTile = 128;                 // rows of a weight tile, and columns of a K block
 constexpr int kTcTileBytes = kTcTile * kTcTile;
-constexpr int kTcMaxStages = 8;              // ring depth; at least kTcSplitters (see tc_plan)
-constexpr int kTcMaxT = 64;                  // tokens per launch
-constexpr int kTcSplitGroup = 16;            // tokens a splitter converts at once
+constexpr int kTcMaxStages = 8;              // ring depth
+constexpr int kTcMinStages = 3;
+constexpr int kTcMaxT = 64;                  // tokens per launch (bf16 x; 32 for fp32 x)
 constexpr int kTcKSteps = kTcTile / 32;      // MMAs (K = 32 each) per tile
 constexpr int kTcAccBufs = 4;                // tensor-memory accumulator buffers (tiles in flight)
+constexpr int kTcMaxN = 256;                 // largest MMA N (M = 128)
 
 enum : unsigned {
     ERR_TC_WAIT = 0x500,  // a tensor-core pipeline wait ran out (+ the waiting role)
 };
 
+// e4m3 terms per activation value: 2 reproduce bf16, 6 keep 24 bits of fp32.
+__host__ __device__ constexpr int tc_ts(bool x_bf16) { return x_bf16 ? 2 : 6; }
+
+// Row stride (floats) of the term-scale image: its rows' aligned 16-byte
+// supersets stay inside the row.
+__host__ __device__ inline int tc_sx_stride(int rows) { return ((rows + 3) & ~3) + 4; }
+
 struct TcParams {
-    const void* x;       // [T, K] bf16 or fp32
     int T, K, nrows;
     const float* scale;  // 1x128: [nrows, K/128]; 128x128: [nrows/128, K/128]
     int layout;
@@ -62,40 +72,33 @@ struct TcParams {
     int y_bf16;
     float* partial;      // [grid][2][T][128] split-K partial sums
     unsigned* counters;  // [nrows/128][4] arrivals per (row block, tensor-memory lane quarter)
+    const float* sx;     // term scales of the split activations [K/128][sx_stride]
+    int sx_stride;
     int tiles, kblocks;  // (nrows/128) * (K/128), K/128
     int q_tiles;         // q is in the packed tile layout (oomb_pack_fp8_tiles), else row-major
     int nmma;            // MMA N = T * TS rounded up to 8
     int stages;
     int nbufs;           // tensor-memory accumulator buffers in use (<= kTcAccBufs)
-    int xdepth;          // x slots per splitter in use (<= kTcXDepth)
     int tmem_cols;
     unsigned* err;
 };
 
-__host__ __device__ constexpr int tc_ts(bool x_bf16) { return x_bf16 ? 2 : 4; }
-__host__ __device__ constexpr int tc_terms(bool x_bf16) { return x_bf16 ? 2 : 4; }
-
-constexpr int kTcXDepth = 2;  // x slots per splitter (at most)
-
 // Shared memory (after aligning the base to 1024 bytes):
-// [A ring: stages x 16 KB][B ring: stages x nmma*128]
-// [x rings: 4 splitters x kTcXDepth x T x 128 x xbytes][x scales: stages x T*TS floats]
+// [A ring: stages x 16 KB][B ring: stages x nmma*128][term scales: stages x (nmma + 8) floats]
 // [barriers][tensor-memory address]
 struct TcSmem {
-    size_t a_off, b_off, x_off, x_stage, sx_off, bar_off, total;
+    size_t a_off, b_off, sx_off, sx_slot, bar_off, total;
 };
 
-__host__ __device__ inline TcSmem tc_smem(int stages, int nmma, int T, int ts, int xbytes, int xdepth) {
+__host__ __device__ inline TcSmem tc_smem(int stages, int nmma) {
     TcSmem m{};
     m.a_off = 0;
     m.b_off = static_cast<size_t>(stages) * kTcTileBytes;
-    m.x_off = m.b_off + static_cast<size_t>(stages) * nmma * 128;
-    m.x_stage = static_cast<size_t>(T) * kTcTile * xbytes;
-    m.sx_off = m.x_off + static_cast<size_t>(kTcSplitters) * xdepth * m.x_stage;
-    m.bar_off = (m.sx_off + static_cast<size_t>(stages) * T * ts * 4 + 7) & ~static_cast<size_t>(7);
-    // a_full, a_empty, b_full, b_empty [kTcMaxStages]; x_full [4][kTcMaxStages] (kTcXDepth used);
-    // mma_done, tmem_empty [kTcAccBufs]; tensor-memory address
-    m.total = m.bar_off + ((4 + kTcSplitters) * kTcMaxStages + 2 * kTcAccBufs) * 8 + 16;
+    m.sx_off = m.b_off + static_cast<size_t>(stages) * nmma * 128;
+    m.sx_slot = static_cast<size_t>(nmma + 8);
+    m.bar_off = (m.sx_off + static_cast<size_t>(stages) * m.sx_slot * 4 + 7) & ~static_cast<size_t>(7);
+    // a_full, a_empty, b_full, b_empty [kTcMaxStages]; mma_done, tmem_empty [kTcAccBufs]; tensor-memory address
+    m.total = m.bar_off + (4 * kTcMaxStages + 2 * kTcAccBufs) * 8 + 16;
     return m;
 }
 
@@ -153,6 +156,21 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
 }
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
 
 // Two floats to packed e4m3 (lo in the low byte), round to nearest even, saturating.
 __device__ __forceinline__ uint32_t e4m3x2_from_f32(float lo, float hi) {
@@ -213,25 +231,141 @@ __device__ __forceinline__ void tc_store_row(const TcParams& p, const float (&ac
     }
 }
 
+// ---- the activation split (one pass per call) ------------------------------------------
+
+struct XsParams {
+    const void* x;         // [*, K] bf16 or fp32
+    const int32_t* rows;   // [A] activation row of each assignment, or null (row = assignment)
+    const int32_t* first;  // device word holding the first assignment to split (the first CSR offset), or null: 0
+    const int32_t* count;  // device word holding A (the last CSR offset), or null: A = a_host
+    int a_host;
+    int a_cover;           // assignments the grid covers (>= A)
+    int zero_pad;          // rows of assignments in [A, a_cover) are written as zero terms
+    int K, kblocks;
+    uint8_t* xs;           // [rows_alloc, K] e4m3 terms, row = assignment * TS + term
+    int rows_alloc;
+    float* sx;             // [kblocks][sx_stride] term scales, same row index
+    int sx_stride;
+};
+
+// One warp per (assignment, K block): lane l splits columns 4l .. 4l+3 of the
+// block into TS terms (the block's largest residual sets each term's scale).
+template <bool XBF16>
+__global__ void __launch_bounds__(256) xsplit_kernel(const XsParams p) {
+    constexpr int TS = tc_ts(XBF16);
+    pdl_wait();  // x, rows and the count come from earlier kernels; xs / sx may still be read by one
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int64_t w = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    if (w >= static_cast<int64_t>(p.a_cover) * p.kblocks) return;
+    const int a = static_cast<int>(w / p.kblocks), kb = static_cast<int>(w - static_cast<int64_t>(a) * p.kblocks);
+    const int A = p.count ? __ldcg(p.count) : p.a_host;
+    if ((a >= A && !p.zero_pad) || (p.first && a < __ldcg(p.first))) return;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (a < A) {
+        const int row = p.rows ? __ldcg(p.rows + a) : a;
+        const int64_t idx = static_cast<int64_t>(row) * p.K + static_cast<int64_t>(kb) * kTcTile + lane * 4;
+        if (XBF16) {
+            const uint2 u = __ldcg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + idx));
+            v[0] = __uint_as_float(u.x << 16);
+            v[1] = __uint_as_float(u.x & 0xffff0000u);
+            v[2] = __uint_as_float(u.y << 16);
+            v[3] = __uint_as_float(u.y & 0xffff0000u);
+        } else {
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + idx));
+            v[0] = u.x;
+            v[1] = u.y;
+            v[2] = u.z;
+            v[3] = u.w;
+        }
+    }
+#pragma unroll
+    for (int term = 0; term < TS; term++) {
+        float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float inv;
+        const float sc = tc_term_scale(mx, inv);
+        const uint32_t lo2 = e4m3x2_from_f32(v[0] * inv, v[1] * inv);
+        const uint32_t hi2 = e4m3x2_from_f32(v[2] * inv, v[3] * inv);
+        const int r = a * TS + term;
+        if (r < p.rows_alloc) {
+            *reinterpret_cast<uint32_t*>(p.xs + static_cast<int64_t>(r) * p.K + static_cast<int64_t>(kb) * kTcTile +
+                                         lane * 4) = lo2 | (hi2 << 16);
+            if (lane == 0) p.sx[static_cast<int64_t>(kb) * p.sx_stride + r] = sc;
+        }
+        if (term + 1 < TS) {
+            // exact residual: q * sc carries at most 4 significant bits
+            const float2 qa = e4m3x2_to_float2(static_cast<unsigned short>(lo2));
+            const float2 qb = e4m3x2_to_float2(static_cast<unsigned short>(hi2));
+            v[0] -= qa.x * sc;
+            v[1] -= qa.y * sc;
+            v[2] -= qb.x * sc;
+            v[3] -= qb.y * sc;
+        }
+    }
+}
+
+// Folds one K block from tensor memory into acc: column c = t * TS + term of
+// the buffer at taddr, for tokens t < n, with term scales sx[c]:
+//   acc[t] = fma(ws, s_0 D_0 + s_1 D_1 + ... (left to right), acc[t]).
+// Columns are read 32 at a time (one wait per 32), the tail 8 at a time, never
+// past the last 8-column group that holds a token (the buffer's end).  Called
+// by every lane of a warp with the same n.
+template <int TS, int MAXN>
+__device__ __forceinline__ void tc_fold(uint32_t taddr, const float* sx, int n, float ws, float (&acc)[MAXN]) {
+    const int ncol = (n * TS + 7) & ~7;
+    float u = 0.0f;
+    auto fold = [&](int c, float d) {
+        const int t = c / TS, term = c - (c / TS) * TS;
+        if (t < MAXN && t < n) {
+            const float v = sx[c] * d;
+            u = term == 0 ? v : __fadd_rn(u, v);
+            if (term == TS - 1) acc[t] = fmaf(ws, u, acc[t]);
+        }
+    };
+#pragma unroll
+    for (int c0 = 0; c0 < MAXN * TS; c0 += 32) {
+        if (c0 < ncol) {
+            if (c0 + 32 <= ncol) {
+                float d[32];
+                tc_ld32(taddr + static_cast<uint32_t>(c0), d);
+                tc_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 32; q++) fold(c0 + q, d[q]);
+            } else {
+#pragma unroll
+                for (int c1 = c0; c1 < c0 + 32 && c1 < MAXN * TS; c1 += 8) {
+                    if (c1 < ncol) {
+                        float d[8];
+                        tc_ld8(taddr + static_cast<uint32_t>(c1), d);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int q = 0; q < 8; q++) fold(c1 + q, d[q]);
+                    }
+                }
+            }
+        }
+    }
+}
+
 template <bool XBF16, int MAXT>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                 const __grid_constant__ CUtensorMap xmap,
                                                                  const TcParams p) {
-    constexpr int TS = tc_ts(XBF16), TERMS = tc_terms(XBF16);
+    constexpr int TS = tc_ts(XBF16);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int XB = XBF16 ? 2 : 4;
-    const TcSmem L = tc_smem(p.stages, p.nmma, p.T, TS, XB, p.xdepth);
+    const TcSmem L = tc_smem(p.stages, p.nmma);
     uint8_t* a_ring = smem + L.a_off;
     uint8_t* b_ring = smem + L.b_off;
-    uint8_t* x_ring = smem + L.x_off;
     float* sx_ring = reinterpret_cast<float*>(smem + L.sx_off);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* a_full = bars;
     uint64_t* a_empty = bars + kTcMaxStages;
     uint64_t* b_full = bars + 2 * kTcMaxStages;
     uint64_t* b_empty = bars + 3 * kTcMaxStages;
-    uint64_t* x_full = bars + 4 * kTcMaxStages;  // [splitter][x slot]
-    uint64_t* mma_done = bars + (4 + kTcSplitters) * kTcMaxStages;
+    uint64_t* mma_done = bars + 4 * kTcMaxStages;
     uint64_t* tmem_empty = mma_done + kTcAccBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + kTcAccBufs);
 
@@ -245,7 +379,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             mbar_init(&a_empty[i], 1);
             mbar_init(&b_full[i], 1);
             mbar_init(&b_empty[i], 4);
-            for (int w = 0; w < kTcSplitters; w++) mbar_init(&x_full[w * kTcMaxStages + i], 1);
         }
         for (int i = 0; i < p.nbufs; i++) {
             mbar_init(&mma_done[i], 1);
@@ -253,15 +386,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         }
         fence_barrier_init();
     }
-    // B rows past the real (token, term) columns stay zero for the whole kernel
-    for (int i = threadIdx.x; i < S * nmma * 32; i += kTcThreads) reinterpret_cast<uint32_t*>(b_ring)[i] = 0u;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                      "r"(p.tmem_cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -283,100 +413,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     tma_load_2d(a_ring + s * kTcTileBytes, &qmap, kb * kTcTile, rb * kTcTile, &a_full[s], pol);
             }
         }
-    } else if (warp >= 6) {
-        // ================= activation splitters: B tiles and their term scales =================
-        constexpr int SG = MAXT < kTcSplitGroup ? MAXT : kTcSplitGroup;
-        const int sw = warp - 6, XD = p.xdepth;
-        uint64_t* xf = x_full + sw * kTcMaxStages;
-        uint8_t* xr = x_ring + static_cast<size_t>(sw) * XD * L.x_stage;
-        // this splitter's m-th tile, and the bulk copies of its 128-column slices of every token
-        auto my_tile = [&](int m) { return lo + sw + m * kTcSplitters; };
-        auto fetch = [&](int m) {
-            const int i = my_tile(m);
-            if (lane == 0 && i < hi) {
-                const int slot = m % XD, kb = i % p.kblocks;
-                mbar_arrive_expect_tx(&xf[slot], static_cast<unsigned>(T * kTcTile * XB));
-                for (int t = 0; t < T; t++) {
-                    const uint8_t* src = static_cast<const uint8_t*>(p.x) +
-                                         (static_cast<int64_t>(t) * p.K + static_cast<int64_t>(kb) * kTcTile) * XB;
-                    bulk_g2s_plain(xr + slot * L.x_stage + t * kTcTile * XB, src, kTcTile * XB, &xf[slot]);
-                }
+    } else if (warp == 6) {
+        // ================= B loader: the split activations of each tile's K block, and their term scales =================
+        if (lane == 0) {
+            pdl_wait();  // written by xsplit_kernel, the previous launch
+            const uint64_t keep = make_evict_last_policy();  // read once per row block
+            const int sxa = (T * TS + 3) & ~3;
+            const unsigned bytes = static_cast<unsigned>(nmma * 128 + sxa * 4);
+            for (int i = lo; i < hi; i++) {
+                const int s = (i - lo) % S, it = (i - lo) / S, kb = i % p.kblocks;
+                if (!mbar_wait(&b_empty[s], (it & 1) ^ 1, p.err, ERR_TC_WAIT + 2)) break;
+                mbar_arrive_expect_tx(&b_full[s], bytes);
+                tma_load_2d(b_ring + s * nmma * 128, &xmap, kb * kTcTile, 0, &b_full[s], keep);
+                bulk_g2s_plain(sx_ring + s * L.sx_slot, p.sx + static_cast<int64_t>(kb) * p.sx_stride,
+                               static_cast<unsigned>(sxa * 4), &b_full[s]);
             }
-        };
-        pdl_wait();
-        for (int m = 0; m < XD; m++) fetch(m);
-        for (int m = 0; my_tile(m) < hi; m++) {
-            const int i = my_tile(m);
-            const int s = (i - lo) % S, it = (i - lo) / S;
-            if (!mbar_wait(&b_empty[s], (it & 1) ^ 1, p.err, ERR_TC_WAIT + 2)) break;
-            if (!mbar_wait(&xf[m % XD], (m / XD) & 1, p.err, ERR_TC_WAIT + 7)) break;
-            uint8_t* bt = b_ring + s * nmma * 128;
-            float* sx = sx_ring + s * T * TS;
-            const uint8_t* xs = xr + (m % XD) * L.x_stage;
-            for (int g = 0; g < T; g += SG) {
-                // lane l holds columns 4l .. 4l+3 of tokens g .. g+SG-1
-                float v[SG][4];
-#pragma unroll
-                for (int u = 0; u < SG; u++) {
-                    const int t = g + u;
-                    if (t < T) {
-                        if (XBF16) {
-                            const uint2 w = *reinterpret_cast<const uint2*>(xs + (t * kTcTile + lane * 4) * 2);
-                            v[u][0] = __uint_as_float(w.x << 16);
-                            v[u][1] = __uint_as_float(w.x & 0xffff0000u);
-                            v[u][2] = __uint_as_float(w.y << 16);
-                            v[u][3] = __uint_as_float(w.y & 0xffff0000u);
-                        } else {
-                            const float4 w = *reinterpret_cast<const float4*>(xs + (t * kTcTile + lane * 4) * 4);
-                            v[u][0] = w.x;
-                            v[u][1] = w.y;
-                            v[u][2] = w.z;
-                            v[u][3] = w.w;
-                        }
-                    } else {
-                        v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.0f;
-                    }
-                }
-#pragma unroll
-                for (int term = 0; term < TERMS; term++) {
-                    float mx[SG];
-#pragma unroll
-                    for (int u = 0; u < SG; u++)
-                        mx[u] = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                        for (int u = 0; u < SG; u++) mx[u] = fmaxf(mx[u], __shfl_xor_sync(0xffffffffu, mx[u], o));
-#pragma unroll
-                    for (int u = 0; u < SG; u++) {
-                        const int t = g + u;
-                        if (t < T) {
-                            float inv;
-                            const float sc = tc_term_scale(mx[u], inv);
-                            const uint32_t lo2 = e4m3x2_from_f32(v[u][0] * inv, v[u][1] * inv);
-                            const uint32_t hi2 = e4m3x2_from_f32(v[u][2] * inv, v[u][3] * inv);
-                            *reinterpret_cast<uint32_t*>(bt + sw128_offset(t * TS + term, lane * 4)) =
-                                lo2 | (hi2 << 16);
-                            if (lane == 0) sx[t * TS + term] = sc;
-                            if (term + 1 < TERMS) {
-                                // residual for the next term: exact, since q * sc carries at most 4 significant bits
-                                const float2 a = e4m3x2_to_float2(static_cast<unsigned short>(lo2));
-                                const float2 b = e4m3x2_to_float2(static_cast<unsigned short>(hi2));
-                                v[u][0] -= a.x * sc;
-                                v[u][1] -= a.y * sc;
-                                v[u][2] -= b.x * sc;
-                                v[u][3] -= b.y * sc;
-                            }
-                        }
-                    }
-                }
-            }
-            // the x slot is read and B is written: order both against the async proxy, refill the
-            // x slot with this splitter's tile one ring depth ahead, hand B to the MMA
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            fetch(m + XD);
-            if (lane == 0) mbar_arrive(&b_full[s]);
         }
     } else if (warp == 1) {
         // ================= MMA issuer =================
@@ -420,33 +471,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const int s = (i - lo) % S;
             const int j = i - lo, buf = j % p.nbufs;
             const int rb = i / p.kblocks;
-            if (!mbar_wait(&mma_done[buf], (j / p.nbufs) & 1, p.err, ERR_TC_WAIT + 6)) break;
-            tc_fence_after();
-            const float* sx = sx_ring + s * T * TS;
             const float ws = ws_ring[0];
             ws_ring[0] = ws_ring[1];
             ws_ring[1] = ws_ring[2];
             ws_ring[2] = ws_ring[3];
             ws_ring[3] = i + 4 < hi ? tile_scale(i + 4) : 0.0f;
-            // 8 columns per load: 8 / TS tokens
-#pragma unroll
-            for (int c0 = 0; c0 < MAXT * TS; c0 += 8) {
-                if (c0 < T * TS) {
-                    float d[8];
-                    tc_ld8(tmem_base + lane_base + static_cast<uint32_t>(buf * nmma + c0), d);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int q = 0; q < 8; q += TS) {
-                        const int t = (c0 + q) / TS;
-                        if (t < T) {
-                            float u = sx[t * TS] * d[q];
-#pragma unroll
-                            for (int term = 1; term < TERMS; term++) u = __fadd_rn(u, sx[t * TS + term] * d[q + term]);
-                            acc[t] = fmaf(ws, u, acc[t]);
-                        }
-                    }
-                }
-            }
+            if (!mbar_wait(&mma_done[buf], (j / p.nbufs) & 1, p.err, ERR_TC_WAIT + 6)) break;
+            tc_fence_after();
+            tc_fold<TS, MAXT>(tmem_base + lane_base + static_cast<uint32_t>(buf * nmma), sx_ring + s * L.sx_slot, T,
+                              ws, acc);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {

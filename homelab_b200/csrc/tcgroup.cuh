@@ -16,14 +16,18 @@
 // consecutive, so the CTAs working at the same time read the same weight tiles
 // and the chunks after the first find them in L2.
 //
-// The arithmetic is the dense tensor-core kernel's (tc.cuh): a chunk's
-// activations are split exactly into e4m3 terms with power-of-two scales
-// (two terms for bf16 x, four for fp32 x), each (assignment, term) one column of
-// the B operand; tcgen05.mma (kind::f8f6f4, M = 128, K = 32) accumulates one K
-// block per tensor-memory buffer and the epilogue folds
+// The arithmetic is the dense tensor-core kernel's (tc.cuh): xsplit_kernel
+// first splits every assignment's activation row (gathered through `rows`)
+// into e4m3 terms with power-of-two scales (two terms for bf16 x, six for fp32
+// x), once per launch, into a workspace image whose row a * TS + term is one
+// column of the B operand; per tile, TMA copies the chunk's rows of that image
+// (nmma rows from row a0 * TS) into the B ring beside the weights.
+// tcgen05.mma (kind::f8f6f4, M = 128, K = 32) accumulates one K block per
+// tensor-memory buffer and the epilogue folds
 //   acc = fma(w_scale, sum_term s_term * D_term, acc)
 // K blocks in order.  The MMA's N is the chunk's own column count (rounded up
-// to 16), so a chunk of 4 assignments costs a 16-column MMA.
+// to 16), so a chunk of 4 assignments costs a 16-column MMA; an output's bits
+// do not depend on the chunking.
 //
 // Weights: records live at arbitrary addresses (resident, staged or received),
 // so no tensor map can name them.  The copy warp moves each 128 x 128 weight
@@ -32,9 +36,8 @@
 // instruction, coalesced), commits one group per tile and releases a tile to the
 // MMA kTgLag tiles later, after cp.async.wait_group and a proxy fence.
 //
-// Warp roles (10 warps): 0 weight copies, 1 MMA issuer and tensor-memory owner,
-// 2-5 epilogue, 6-9 activation splitters (tile j to splitter j % 4).  Every wait
-// is bounded and records an error code.
+// Warp roles (7 warps): 0 weight copies, 1 MMA issuer and tensor-memory owner,
+// 2-5 epilogue, 6 the B loader.  Every wait is bounded and records an error code.
 #pragma once
 
 #include "tc.cuh"
@@ -51,24 +54,24 @@ enum : unsigned {
 struct TgParams {
     const uint64_t* recs;  // [n_experts] record addresses
     const int32_t* off;    // [n_experts + 1] CSR offsets of the groups
-    const int32_t* rows;   // [A] activation row of each assignment, or null (row = assignment)
     int n_experts;
-    const void* x;         // [*, K] bf16 or fp32
+    int a_max;             // assignments the split covered (off[n_experts] must not exceed it)
     int K, N;
     int64_t w_off, s_off;  // byte offsets of the projection's e4m3 weights and fp32 scales in a record
     int layout;            // OOMB_SCALE_1X128 (0) or OOMB_SCALE_128X128 (1)
     float* y;              // [A, N] fp32
+    const float* sx;       // term scales of the split activations [K/128][sx_stride]
+    int sx_stride;
     int chunk;             // assignments per unit (the kernel's CH)
     int rblocks, kblocks;  // N / 128, K / 128
-    int nmma;              // B columns per stage, and the accumulator stride in tensor memory
-    int stages, nbufs, xdepth, tmem_cols;
+    int nmma;              // B rows per stage (CH * TS), and the accumulator stride in tensor memory
+    int stages, nbufs, tmem_cols;
     unsigned* err;
 };
 
-// Shared memory: the dense kernel's layout for T = CH, then the chunk prefix.
-__host__ __device__ inline size_t tg_smem_bytes(int stages, int nmma, int ch, int ts, int xbytes, int xdepth,
-                                                int n_experts) {
-    const TcSmem m = tc_smem(stages, nmma, ch, ts, xbytes, xdepth);
+// Shared memory: the dense kernel's layout, then the chunk prefix.
+__host__ __device__ inline size_t tg_smem_bytes(int stages, int nmma, int n_experts) {
+    const TcSmem m = tc_smem(stages, nmma);
     return ((m.total + 15) & ~static_cast<size_t>(15)) + 4 * static_cast<size_t>(n_experts + 1);
 }
 
@@ -86,23 +89,21 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 template <bool XBF16, int CH>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams p) {
-    constexpr int TS = tc_ts(XBF16), TERMS = tc_terms(XBF16);
-    constexpr int XB = XBF16 ? 2 : 4;
+__global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                  const TgParams p) {
+    constexpr int TS = tc_ts(XBF16);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const TcSmem L = tc_smem(p.stages, p.nmma, CH, TS, XB, p.xdepth);
+    const TcSmem L = tc_smem(p.stages, p.nmma);
     uint8_t* a_ring = smem + L.a_off;
     uint8_t* b_ring = smem + L.b_off;
-    uint8_t* x_ring = smem + L.x_off;
     float* sx_ring = reinterpret_cast<float*>(smem + L.sx_off);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* a_full = bars;
     uint64_t* a_empty = bars + kTcMaxStages;
     uint64_t* b_full = bars + 2 * kTcMaxStages;
     uint64_t* b_empty = bars + 3 * kTcMaxStages;
-    uint64_t* x_full = bars + 4 * kTcMaxStages;  // [splitter][x slot]
-    uint64_t* mma_done = bars + (4 + kTcSplitters) * kTcMaxStages;
+    uint64_t* mma_done = bars + 4 * kTcMaxStages;
     uint64_t* tmem_empty = mma_done + kTcAccBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + kTcAccBufs);
     int* cs = reinterpret_cast<int*>(smem + ((L.total + 15) & ~static_cast<size_t>(15)));
@@ -116,7 +117,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams 
             mbar_init(&a_empty[i], 1);
             mbar_init(&b_full[i], 1);
             mbar_init(&b_empty[i], 4);
-            for (int w = 0; w < kTcSplitters; w++) mbar_init(&x_full[w * kTcMaxStages + i], 1);
         }
         for (int i = 0; i < p.nbufs; i++) {
             mbar_init(&mma_done[i], 1);
@@ -124,16 +124,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams 
         }
         fence_barrier_init();
     }
-    // B columns a chunk does not fill keep whatever an earlier chunk left there:
-    // an MMA column only feeds its own accumulator column, which no epilogue reads
-    for (int i = threadIdx.x; i < S * p.nmma * 32; i += kTcThreads) reinterpret_cast<uint32_t*>(b_ring)[i] = 0u;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                      "r"(p.tmem_cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    // the grouping (off, rows) and the activations may come from the previous kernel
+    // the grouping (off) and the split activations come from earlier kernels
     pdl_wait();
     if (warp == 0) {
         // cs[e] = chunks of the groups before e (exclusive prefix), cs[n_experts] = all chunks
@@ -141,7 +138,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams 
         const int e0 = min(E, lane * per), e1 = min(E, e0 + per);
         int mine = 0;
         for (int e = e0; e < e1; e++) {
-            const int c = __ldg(p.off + e + 1) - __ldg(p.off + e);
+            const int c = __ldcg(p.off + e + 1) - __ldcg(p.off + e);
             mine += c > 0 ? (c + p.chunk - 1) / p.chunk : 0;
         }
         int incl = mine;
@@ -153,12 +150,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams 
         int run = incl - mine;
         for (int e = e0; e < e1; e++) {
             cs[e] = run;
-            const int c = __ldg(p.off + e + 1) - __ldg(p.off + e);
+            const int c = __ldcg(p.off + e + 1) - __ldcg(p.off + e);
             run += c > 0 ? (c + p.chunk - 1) / p.chunk : 0;
         }
-        if (lane == 31) cs[E] = incl;
+        if (lane == 31) {
+            // more assignments than the split covered: do nothing, report it
+            if (__ldcg(p.off + E) > p.a_max) {
+                record_error(p.err, ERR_BAD_TABLE);
+                incl = 0;
+            }
+            cs[E] = incl;
+        }
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -182,8 +185,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams 
         TgUnit U;
         U.e = lo;
         U.rb = u - g * p.rblocks;
-        U.a0 = __ldg(p.off + lo) + (g - cs[lo]) * p.chunk;
-        U.nt = min(p.chunk, __ldg(p.off + lo + 1) - U.a0);
+        U.a0 = __ldcg(p.off + lo) + (g - cs[lo]) * p.chunk;
+        U.nt = min(p.chunk, __ldcg(p.off + lo + 1) - U.a0);
         return U;
     };
 
@@ -227,98 +230,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams 
         __syncwarp();
         if (lane == 0)
             for (int i = j > kTgLag ? j - kTgLag : 0; i < j; i++) mbar_arrive(&a_full[i % S]);
-    } else if (warp >= 6) {
-        // ================= activation splitters: B tiles and their term scales =================
-        constexpr int SG = CH < kTcSplitGroup ? CH : kTcSplitGroup;
-        const int sw = warp - 6, XD = p.xdepth;
-        uint64_t* xf = x_full + sw * kTcMaxStages;
-        uint8_t* xr = x_ring + static_cast<size_t>(sw) * XD * L.x_stage;
-        auto fetch = [&](int m) {
-            const int j = sw + m * kTcSplitters;
-            if (j >= ntiles) return;
-            const TgUnit U = unit_of(j);
-            const int slot = m % XD, kb = j % KB;
-            if (lane == 0) mbar_arrive_expect_tx(&xf[slot], static_cast<unsigned>(U.nt * kTcTile * XB));
-            __syncwarp();
-            for (int t = lane; t < U.nt; t += 32) {
-                const int row = p.rows ? __ldg(p.rows + U.a0 + t) : U.a0 + t;
-                const uint8_t* src = static_cast<const uint8_t*>(p.x) +
-                                     (static_cast<int64_t>(row) * p.K + static_cast<int64_t>(kb) * kTcTile) * XB;
-                bulk_g2s_plain(xr + slot * L.x_stage + t * kTcTile * XB, src, kTcTile * XB, &xf[slot]);
+    } else if (warp == 6) {
+        // ================= B loader: the chunk's split activations and term scales per tile =================
+        if (lane == 0) {
+            const uint64_t keep = make_evict_last_policy();  // read once per row block of the expert
+            TgUnit U{};
+            for (int j = 0; j < ntiles; j++) {
+                const int s = j % S, it = j / S, kb = j % KB;
+                if (kb == 0) U = unit_of(j);
+                const int e0 = U.a0 * TS, e0a = e0 & ~3, e1a = (e0 + U.nt * TS + 3) & ~3;
+                if (!mbar_wait(&b_empty[s], (it & 1) ^ 1, p.err, ERR_TG_WAIT + 2)) break;
+                mbar_arrive_expect_tx(&b_full[s], static_cast<unsigned>(p.nmma * 128 + (e1a - e0a) * 4));
+                tma_load_2d(b_ring + s * p.nmma * 128, &xmap, kb * kTcTile, e0, &b_full[s], keep);
+                bulk_g2s_plain(sx_ring + s * L.sx_slot, p.sx + static_cast<int64_t>(kb) * p.sx_stride + e0a,
+                               static_cast<unsigned>((e1a - e0a) * 4), &b_full[s]);
             }
-        };
-        for (int m = 0; m < XD; m++) fetch(m);
-        for (int m = 0; sw + m * kTcSplitters < ntiles; m++) {
-            const int j = sw + m * kTcSplitters;
-            const int s = j % S, it = j / S;
-            const int nt = unit_of(j).nt;
-            if (!mbar_wait(&b_empty[s], (it & 1) ^ 1, p.err, ERR_TG_WAIT + 2)) break;
-            if (!mbar_wait(&xf[m % XD], (m / XD) & 1, p.err, ERR_TG_WAIT + 7)) break;
-            uint8_t* bt = b_ring + s * p.nmma * 128;
-            float* sx = sx_ring + s * CH * TS;
-            const uint8_t* xs = xr + (m % XD) * L.x_stage;
-            for (int g = 0; g < nt; g += SG) {
-                // lane l holds columns 4l .. 4l+3 of assignments g .. g+SG-1 of the chunk
-                float v[SG][4];
-#pragma unroll
-                for (int u = 0; u < SG; u++) {
-                    const int t = g + u;
-                    if (t < nt) {
-                        if (XBF16) {
-                            const uint2 w = *reinterpret_cast<const uint2*>(xs + (t * kTcTile + lane * 4) * 2);
-                            v[u][0] = __uint_as_float(w.x << 16);
-                            v[u][1] = __uint_as_float(w.x & 0xffff0000u);
-                            v[u][2] = __uint_as_float(w.y << 16);
-                            v[u][3] = __uint_as_float(w.y & 0xffff0000u);
-                        } else {
-                            const float4 w = *reinterpret_cast<const float4*>(xs + (t * kTcTile + lane * 4) * 4);
-                            v[u][0] = w.x;
-                            v[u][1] = w.y;
-                            v[u][2] = w.z;
-                            v[u][3] = w.w;
-                        }
-                    } else {
-                        v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.0f;
-                    }
-                }
-#pragma unroll
-                for (int term = 0; term < TERMS; term++) {
-                    float mx[SG];
-#pragma unroll
-                    for (int u = 0; u < SG; u++)
-                        mx[u] = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                        for (int u = 0; u < SG; u++) mx[u] = fmaxf(mx[u], __shfl_xor_sync(0xffffffffu, mx[u], o));
-#pragma unroll
-                    for (int u = 0; u < SG; u++) {
-                        const int t = g + u;
-                        if (t < nt) {
-                            float inv;
-                            const float sc = tc_term_scale(mx[u], inv);
-                            const uint32_t lo2 = e4m3x2_from_f32(v[u][0] * inv, v[u][1] * inv);
-                            const uint32_t hi2 = e4m3x2_from_f32(v[u][2] * inv, v[u][3] * inv);
-                            *reinterpret_cast<uint32_t*>(bt + sw128_offset(t * TS + term, lane * 4)) =
-                                lo2 | (hi2 << 16);
-                            if (lane == 0) sx[t * TS + term] = sc;
-                            if (term + 1 < TERMS) {
-                                // exact residual: q * sc carries at most 4 significant bits
-                                const float2 a = e4m3x2_to_float2(static_cast<unsigned short>(lo2));
-                                const float2 b = e4m3x2_to_float2(static_cast<unsigned short>(hi2));
-                                v[u][0] -= a.x * sc;
-                                v[u][1] -= a.y * sc;
-                                v[u][2] -= b.x * sc;
-                                v[u][3] -= b.y * sc;
-                            }
-                        }
-                    }
-                }
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            fetch(m + XD);
-            if (lane == 0) mbar_arrive(&b_full[s]);
         }
     } else if (warp == 1) {
         // ================= MMA issuer =================
@@ -367,25 +293,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const TgParams 
                                       : __ldg(sp + static_cast<int64_t>(U.rb * kTcTile + r) * KB + kb);
             if (!mbar_wait(&mma_done[buf], (j / p.nbufs) & 1, p.err, ERR_TG_WAIT + 6)) break;
             tc_fence_after();
-            const float* sx = sx_ring + s * CH * TS;
-#pragma unroll
-            for (int c0 = 0; c0 < CH * TS; c0 += 8) {
-                if (c0 < U.nt * TS) {
-                    float d[8];
-                    tc_ld8(tmem_base + lane_base + static_cast<uint32_t>(buf * p.nmma + c0), d);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int q = 0; q < 8; q += TS) {
-                        const int t = (c0 + q) / TS;
-                        if (t < U.nt) {
-                            float u = sx[t * TS] * d[q];
-#pragma unroll
-                            for (int term = 1; term < TERMS; term++) u = __fadd_rn(u, sx[t * TS + term] * d[q + term]);
-                            acc[t] = fmaf(ws, u, acc[t]);
-                        }
-                    }
-                }
-            }
+            tc_fold<TS, CH>(tmem_base + lane_base + static_cast<uint32_t>(buf * p.nmma),
+                            sx_ring + s * L.sx_slot + ((U.a0 * TS) & 3), U.nt, ws, acc);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {

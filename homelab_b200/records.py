@@ -29,23 +29,17 @@ def scale_bytes(n: int, k: int, layout: int) -> int:
 
 
 def record_layout(hidden: int, inter: int, layout: int = SCALE_128X128):
-    """(geometry, stride) of an FP8 expert record."""
+    """(geometry, stride) of an FP8 expert record: gate, up, down, then their
+    scales, each part at a PART_ALIGN offset, the stride rounded up to ALIGN
+    (the library's oomb_fp8_record_layout)."""
+    import ctypes as C
+
+    from . import _lib
     g = Fp8Record()
-    g.hidden, g.inter, g.layout = hidden, inter, layout
-    o = 0
-    g.gate_weight = o
-    o = _up(o + inter * hidden, PART_ALIGN)
-    g.up_weight = o
-    o = _up(o + inter * hidden, PART_ALIGN)
-    g.down_weight = o
-    o = _up(o + hidden * inter, PART_ALIGN)
-    g.gate_scale = o
-    o = _up(o + scale_bytes(inter, hidden, layout), PART_ALIGN)
-    g.up_scale = o
-    o = _up(o + scale_bytes(inter, hidden, layout), PART_ALIGN)
-    g.down_scale = o
-    o = _up(o + scale_bytes(hidden, inter, layout), PART_ALIGN)
-    return g, _up(o, ALIGN)
+    stride = C.c_size_t()
+    _lib.check(_lib.lib().oomb_fp8_record_layout(hidden, inter, layout, C.byref(g), C.byref(stride)),
+               "record_layout")
+    return g, int(stride.value)
 
 
 def weight_bytes(g: Fp8Record) -> int:
@@ -99,3 +93,39 @@ class ExpertBank:
         """A host copy of every record as numpy uint8 arrays (for the CPU oracle)."""
         host = self.buf.cpu().numpy()
         return [host[e * self.stride:(e + 1) * self.stride] for e in range(self.experts)]
+
+
+class SharedExpertBank:
+    """A layer's shared expert(s) on the device: one FP8 SwiGLU MLP of width `inter`
+    (all shared experts side by side; gate rows then up rows of gate_up [2 * inter,
+    hidden], down [hidden, inter]) and a bf16 gate-logit row [hidden] (or none),
+    with the oomb_shared_expert view the layer entry point takes."""
+
+    def __init__(self, hidden: int, inter: int, layout: int = SCALE_128X128, device: torch.device | str = "cuda",
+                 gated: bool = True):
+        self.hidden, self.inter, self.layout = hidden, inter, layout
+        dev = torch.device(device)
+        nb_h, nb_i = (hidden + 127) // 128, (inter + 127) // 128
+        self.gate_up_q = torch.zeros((2 * inter, hidden), dtype=torch.uint8, device=dev)
+        self.gate_up_s = torch.zeros((scale_rows(2 * inter, layout), nb_h), dtype=torch.float32, device=dev)
+        self.down_q = torch.zeros((hidden, inter), dtype=torch.uint8, device=dev)
+        self.down_s = torch.zeros((scale_rows(hidden, layout), nb_i), dtype=torch.float32, device=dev)
+        self.gate_w = torch.zeros(hidden, dtype=torch.bfloat16, device=dev) if gated else None
+
+    def fill_random(self, gpu, seed: int, sigma: float = 0.02):
+        """Quantize N(0, sigma) bf16 weights on the device; the gate row N(0, sigma) in bf16."""
+        gen = torch.Generator(device=self.gate_up_q.device)
+        gen.manual_seed(seed)
+        for (q, s, n, k) in ((self.gate_up_q, self.gate_up_s, 2 * self.inter, self.hidden),
+                             (self.down_q, self.down_s, self.hidden, self.inter)):
+            w = (torch.randn((n, k), generator=gen, device=q.device) * sigma).to(torch.bfloat16)
+            gpu.quantize_fp8(w.view(torch.int16), n, k, self.layout, q, s)
+        if self.gate_w is not None:
+            self.gate_w.copy_((torch.randn(self.hidden, generator=gen, device=q.device) * sigma).to(torch.bfloat16))
+
+    def view(self):
+        from ._lib import SharedExpert
+        return SharedExpert(hidden=self.hidden, inter=self.inter, scale_layout=self.layout,
+                            gate_up_q=self.gate_up_q.data_ptr(), gate_up_scale=self.gate_up_s.data_ptr(),
+                            down_q=self.down_q.data_ptr(), down_scale=self.down_s.data_ptr(),
+                            gate_w=self.gate_w.data_ptr() if self.gate_w is not None else None)

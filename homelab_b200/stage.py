@@ -120,3 +120,85 @@ def stage_records(transfer: Transfer, arena: HostArena, which, slots_addr, after
     for i, dst in zip(which, slots_addr):
         transfer.copy_to_device(int(dst), arena.address(int(i)), arena.stride)
     return transfer.record_copies()
+
+
+class Policy:
+    """A replacement policy of the expert cache (oomb_policy: the Policy trait of
+    crates/oominf-tiers/src/policy.rs:9-129): "lru", "lfu" or "lrfu:<half_life>".
+    Host-only (no GPU needed)."""
+
+    def __init__(self, spec: str = "lru"):
+        self.L = _lib.lib()
+        h = C.c_void_p()
+        check(self.L.oomb_policy_create(spec.encode(), C.byref(h)), f"policy {spec!r}")
+        self.h = h.value
+
+    def touch(self, key: int, now: int):
+        check(self.L.oomb_policy_touch(self.h, key, now), "policy_touch")
+
+    def remove(self, key: int):
+        check(self.L.oomb_policy_remove(self.h, key), "policy_remove")
+
+    def victim(self, pinned=()) -> int | None:
+        arr = (C.c_uint32 * max(len(pinned), 1))(*pinned)
+        v = self.L.oomb_policy_victim(self.h, arr, len(pinned))
+        return None if v < 0 else int(v)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.oomb_policy_destroy(self.h)
+            self.h = None
+
+
+class ExpertTier:
+    """Expert records of `layers` x `experts` in a pinned host arena, served from
+    `slots` device slots (oomb_tier): the ExpertSource two-phase fetch
+    (crates/oominf-core/src/experts.rs:12-41) with the cache policy `policy`.
+
+        addrs, ready = tier.begin_fetch(layer, experts)   # ready[i]: usable by work issued now
+        ... issue the work of the ready experts ...
+        tier.finish_fetch()                                # the rest are usable after this
+        ... issue the work of the others ...
+    """
+
+    def __init__(self, arena: HostArena, layers: int, experts: int, slots: int, device=0, policy: str = "lru"):
+        if arena.count < layers * experts:
+            raise ValueError("the arena holds fewer records than layers x experts")
+        self.L = _lib.lib()
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        self.arena, self.stride = arena, arena.stride
+        self.slots = torch.empty(slots * arena.stride, dtype=torch.uint8, device=self.device)
+        h = C.c_void_p()
+        check(self.L.oomb_tier_create(arena.buf.data_ptr(), arena.stride, layers, experts, self.slots.data_ptr(),
+                                      slots, policy.encode(), C.byref(h)), "tier_create")
+        self.h = h.value
+
+    def _compute(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def begin_fetch(self, layer: int, experts):
+        n = len(experts)
+        ids = (C.c_int32 * max(n, 1))(*[int(e) for e in experts])
+        addrs = (C.c_uint64 * max(n, 1))()
+        ready = (C.c_uint8 * max(n, 1))()
+        check(self.L.oomb_tier_begin_fetch(self.h, self._compute(), layer, ids, n, addrs, ready), "tier_begin_fetch")
+        return [int(addrs[i]) for i in range(n)], [bool(ready[i]) for i in range(n)]
+
+    def finish_fetch(self):
+        check(self.L.oomb_tier_finish_fetch(self.h, self._compute()), "tier_finish_fetch")
+
+    def stats(self) -> dict:
+        v = (C.c_uint64 * 5)()
+        check(self.L.oomb_tier_stats(self.h, v), "tier_stats")
+        return dict(zip(("requests", "hits", "misses", "evictions", "bytes_copied"), (int(x) for x in v)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.oomb_tier_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

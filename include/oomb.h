@@ -60,7 +60,13 @@ typedef struct CUstream_st* oomb_stream;
  * "fp8-e4m3-b1x128"), the FP8 counterpart of Nvfp4Record / Bf16Record
  * (backend.rs:783-807): gate and up e4m3 [inter, hidden], down e4m3
  * [hidden, inter], each with its own fp32 scales in `layout`.  Offsets are in
- * bytes from the record start and must be multiples of 16. */
+ * bytes from the record start and must be multiples of 16.  The record format
+ * of experts.bin (docs/dev/format.md:37-76): parts at OOMB_PART_ALIGN offsets
+ * in the order gate.weight, up.weight, down.weight, gate.weight_scale,
+ * up.weight_scale, down.weight_scale, the stride rounded up to
+ * OOMB_RECORD_ALIGN (oomb_fp8_record_layout computes it). */
+#define OOMB_PART_ALIGN 256
+#define OOMB_RECORD_ALIGN 4096
 typedef struct {
     int64_t hidden;
     int64_t inter;
@@ -117,15 +123,17 @@ int oomb_gemm_fp8(const void* x, int x_dtype, const uint8_t* q, const float* sca
                   size_t workspace_bytes, oomb_stream stream);
 
 /* The same product on the tensor cores (tcgen05, kind::f8f6f4): the weights go
- * from HBM to shared memory by TMA and straight into the MMA; each 128-column
- * block of x is split exactly into e4m3 terms with power-of-two scales (two for
- * bf16 x, four for fp32 x) that form the MMA's B operand, and the per-block
- * weight and term scales are applied in fp32 as each 128-column block
- * completes.  Needs n % 128 == 0, k % 128 == 0, 1 <= t <= 64, and a workspace of
- * oomb_gemm_fp8_workspace_bytes(t, n, k, x_dtype) bytes (split-K partial sums
- * and self-resetting counters) zeroed once before first use.  Returns
- * OOMB_E_SHAPE for other shapes (use oomb_gemm_fp8).  Calls sharing a
- * workspace must be ordered on one stream. */
+ * from HBM to shared memory by TMA and straight into the MMA.  A first small
+ * kernel splits x once into e4m3 terms with power-of-two scales per 128-column
+ * block (two terms for bf16 x, exact; six for fp32 x, which keep every value
+ * to within 2^-24 of its block's largest magnitude: 24 significant bits) into
+ * the workspace; the terms form the MMA's B operand, and the per-block weight
+ * and term scales are applied in fp32 as each 128-column block completes.
+ * Needs n % 128 == 0, k % 128 == 0, 1 <= t <= 64 (bf16 x) or <= 32 (fp32 x),
+ * and a workspace of oomb_gemm_fp8_workspace_bytes(t, n, k, x_dtype) bytes
+ * (split-K partial sums, self-resetting counters, the split activations)
+ * zeroed once before first use.  Returns OOMB_E_SHAPE for other shapes (use
+ * oomb_gemm_fp8).  Calls sharing a workspace must be ordered on one stream. */
 #define OOMB_Q_ROWS 0  /* q row-major [n, k] (Weight::Fp8) */
 #define OOMB_Q_TILES 1 /* q in the packed tile layout of oomb_pack_fp8_tiles */
 size_t oomb_gemm_fp8_workspace_bytes(int t, int n, int k, int x_dtype);
@@ -199,20 +207,52 @@ int oomb_moe_combine(const float* routed, const float* shared, const float* gate
  * (scale_layout) at s_off.  Replaces Experts::moe_tiled (backend.rs:873-886;
  * crates/oominf-cuda/src/experts.rs:211-266; moe.cu:204-335) for FP8 records:
  * the projection (w_off, s_off, s2_idx) becomes (w_off, s_off, scale_layout),
- * and the result is the Exact precision's (activations split exactly into
- * e4m3 terms: bf16 x exact, fp32 x to 16 significant bits; fp32 accumulate).
- * x: [*, k] fp32 or bf16; y: [A, n] fp32.  n, k multiples of 128; n_experts <=
- * 4096; w_off % 16 == 0.  max_per_expert picks the chunk size (assignments per
- * MMA, <= 64); any group size is correct, 0 if unknown. */
+ * and the result is the Exact precision's: every activation row is split once
+ * into e4m3 terms (bf16 x: two terms, exact; fp32 x: six terms, 24 significant
+ * bits of each 128-column block, as the reference's three exact bf16 terms),
+ * fp32 accumulate.  x: [*, k] fp32 or bf16; y: [A, n] fp32.  n, k multiples of
+ * 128; n_experts <= 4096; w_off % 16 == 0.  max_per_expert picks the chunk size
+ * (assignments per MMA, <= 64 for bf16 x and <= 32 for fp32 x); any group size
+ * is correct, 0 if unknown.  max_assignments bounds A = off[n_experts] (it is
+ * read on the device) and sizes the workspace: at least
+ * oomb_moe_tiled_fp8_workspace_bytes(max_assignments, k, x_dtype) bytes, which
+ * hold the split activations (no zeroing needed).  Calls sharing a workspace
+ * must be ordered on one stream. */
+size_t oomb_moe_tiled_fp8_workspace_bytes(int max_assignments, int k, int x_dtype);
 int oomb_moe_tiled_fp8(const uint64_t* recs, const int32_t* off, const int32_t* rows, int n_experts,
-                       int max_per_expert, const void* x, int x_dtype, float* y, int n, int k,
-                       int64_t w_off, int64_t s_off, int scale_layout, oomb_stream stream);
+                       int max_per_expert, int max_assignments, const void* x, int x_dtype, float* y, int n,
+                       int k, int64_t w_off, int64_t s_off, int scale_layout, void* workspace,
+                       size_t workspace_bytes, oomb_stream stream);
 
 /* h[i] = silu(g[i]) * u[i] for i in [start, end), silu(v) = v / (1 + exp(-v)).
  * Replaces Experts::moe_swiglu_range (backend.rs; experts.rs:269-297;
  * moe.cu:337-341), the step between the tiled gate/up and down projections. */
 int oomb_moe_swiglu_range(const float* g, const float* u, float* h, int64_t start, int64_t end,
                           oomb_stream stream);
+
+/* ---- decode attention ------------------------------------------------------ */
+/* Grouped-query attention of one query token per sequence over a bf16 KV
+ * cache (flash-decode, split over the positions, merged in the same launch):
+ *   out[b, h, :] = sum_j softmax_j(scale * q[b, h, :] . K[b, j, h / G, :]) V[b, j, h / G, :]
+ * for j < kv_len[b], G = heads / kv_heads, fp32 softmax and accumulation.  The
+ * decode case of Attention::attention (backend.rs:551-568; reference kernels
+ * attn_decode_partial_g12 + attn_decode_combine, crates/oominf-cuda/kernels/
+ * attention.cu:592-700) with a bf16 cache (a KvFormat beside the reference's
+ * fp32 one) and every position below kv_len visible (the causal mask of a
+ * decode step).  q, out: [batch, heads, head_dim] (fp32 or bf16).  Cache:
+ * sequence b at b * seq_stride elements of k_cache / v_cache, row j of kv head
+ * c at (j * kv_heads + c) * head_dim elements (the reference's row layout),
+ * rows 0 .. kv_max - 1 allocated.  kv_len: device int32 [batch], or NULL to
+ * use kv_len_all for every sequence; a sequence with no visible position gets
+ * zeros.  head_dim 128; G in {1, 2, 4, 8}.  Workspace: at least
+ * oomb_attention_decode_workspace_bytes(...) bytes (partials and self-resetting
+ * arrival counters) zeroed once before first use; calls sharing it must be
+ * ordered on one stream. */
+size_t oomb_attention_decode_workspace_bytes(int batch, int heads, int kv_heads, int head_dim, int kv_max);
+int oomb_attention_decode(const void* q, int q_dtype, const uint16_t* k_cache, const uint16_t* v_cache,
+                          int64_t seq_stride, const int32_t* kv_len, int kv_len_all, void* out, int out_dtype,
+                          int batch, int heads, int kv_heads, int head_dim, int kv_max, float scale,
+                          void* workspace, size_t workspace_bytes, oomb_stream stream);
 
 /* ---- fused decode step of one resident MoE layer ------------------------ */
 /* Router GEMV, softmax top-k, grouping of the step's assignments by expert
@@ -238,6 +278,42 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* layer, const void* x, int x_dtype,
                         int out_dtype, int32_t* ids, float* weights, void* workspace,
                         size_t workspace_bytes, oomb_stream stream);
 int oomb_workspace_clear(void* workspace, size_t bytes, oomb_stream stream);
+
+/* ---- a whole MoE layer: shared expert(s) + routed experts ----------------- */
+/* The shared expert(s) of a layer in FP8: all shared experts side by side as
+ * one SwiGLU MLP of width `inter` (gate rows then up rows of gate_up_q
+ * [2 * inter, hidden], down_q [hidden, inter], block scales in scale_layout),
+ * and the bf16 gate-logit row gate_w [1, hidden] (NULL: no gate). */
+typedef struct {
+    int32_t hidden;
+    int32_t inter;
+    int32_t scale_layout;
+    int32_t pad_;
+    const uint8_t* gate_up_q;
+    const float* gate_up_scale;
+    const uint8_t* down_q;
+    const float* down_scale;
+    const uint16_t* gate_w;
+} oomb_shared_expert;
+
+/* One MoE layer's decode step: the shared expert (gate/up GEMV, SwiGLU, down
+ * GEMV, gate logit: Moe::shared, crates/oominf-models-qwen/src/moe.rs:
+ * 498-527), the routed experts (as oomb_moe_decode_fp8) and the combine
+ * out = routed + sigmoid(gate) * shared (Experts::moe_combine, backend.rs:
+ * 909-917; ops.cu:311-316; out = routed + shared without a gate): the body of
+ * Moe::forward (moe.rs:479-495) as one stream-ordered sequence, no host round
+ * trip.  x and out are device memory ([t, hidden]); ids / weights optional as
+ * for oomb_moe_decode_fp8.  The shared GEMVs run on the tensor cores from two
+ * tokens.  Workspace: oomb_moe_layer_workspace_bytes(t, layer, shared, x_dtype)
+ * bytes, zeroed once before first use (and after a device error); calls
+ * sharing it must be ordered on one stream.  Bit-identical to calling
+ * oomb_gemm_fp8, oomb_silu_mul_rows, oomb_gemm_fp8, oomb_router_logits,
+ * oomb_moe_decode_fp8 and oomb_moe_combine in that order. */
+size_t oomb_moe_layer_workspace_bytes(int t, const oomb_moe_layer* layer, const oomb_shared_expert* shared,
+                                      int x_dtype);
+int oomb_moe_layer_decode_fp8(const oomb_moe_layer* layer, const oomb_shared_expert* shared, const void* x,
+                              int x_dtype, int t, void* out, int out_dtype, int32_t* ids, float* weights,
+                              void* workspace, size_t workspace_bytes, oomb_stream stream);
 
 /* ---- fused decode step that allocates nothing --------------------------- */
 /* No counterpart in the reference: an addition of this library.  For callers
@@ -392,7 +468,58 @@ int oomb_event_wait(oomb_event ev);                           /* blocks the host
 int oomb_event_destroy(oomb_event ev);
 int oomb_copies_sync(oomb_copy_queue queue);                  /* blocks the host */
 
+/* ---- expert tiers: the two-phase fetch over device slots ----------------- */
+/* Replacement policy of an expert cache (crates/oominf-tiers/src/policy.rs:
+ * 9-129, the Policy trait: touch / remove / victim).  Keys are layer *
+ * experts + expert.  spec: "lru", "lfu" (LRFU with half-life 1e12) or
+ * "lrfu:<half_life>" (each access adds 2^(now / half_life) to a key's score;
+ * the lowest score is the victim).  Host-only: needs no GPU. */
+typedef struct oomb_policy_st* oomb_policy;
+int oomb_policy_create(const char* spec, oomb_policy* policy);
+int oomb_policy_destroy(oomb_policy policy);
+int oomb_policy_touch(oomb_policy policy, uint32_t key, uint64_t now);
+int oomb_policy_remove(oomb_policy policy, uint32_t key);
+/* The best victim among resident keys not in pinned[0 .. n_pinned), or -1. */
+int64_t oomb_policy_victim(oomb_policy policy, const uint32_t* pinned, int n_pinned);
+
+/* A device tier of expert records: `slots` records of record_stride bytes at
+ * device_slots (caller-owned device memory), filled on demand from the pinned
+ * host arena (record (layer, e) at host_arena + (layer * experts + e) *
+ * record_stride; cudaHostAlloc / oomb_pin_host memory), victims chosen by the
+ * policy `policy` (as oomb_policy_create).  The ExpertSource two-phase fetch
+ * (crates/oominf-core/src/experts.rs:12-41) as TieredExperts drives its device
+ * tier (crates/oominf-tiers/src/tiered.rs:1155-1421, 1494-1510):
+ *   oomb_tier_begin_fetch: addrs[i] = the device address of experts[i]'s
+ *     record of `layer`, ready[i] = 1 if compute issued now may read it (it was
+ *     resident), 0 if its copy was queued (the copy queue first waits for the
+ *     compute issued on `compute` so far: a kernel issued earlier may still
+ *     read the victim's slot).  Victims are never records this fetch wants.
+ *     Returns OOMB_E_SHAPE when the slots cannot hold one fetch's experts.
+ *   oomb_tier_finish_fetch: compute issued on `compute` after it may read
+ *     every record of the last begin_fetch (one stream wait on the copies).
+ * Work on the ready records, issued between the two calls, overlaps the
+ * copies.  A begin_fetch while a fetch is open finishes it first.  One host
+ * thread per tier.  stats: requests, hits, misses, evictions, bytes copied. */
+typedef struct oomb_tier_st* oomb_tier;
+int oomb_tier_create(const void* host_arena, size_t record_stride, int layers, int experts, void* device_slots,
+                     int slots, const char* policy, oomb_tier* tier);
+int oomb_tier_destroy(oomb_tier tier);
+int oomb_tier_begin_fetch(oomb_tier tier, oomb_stream compute, int layer, const int32_t* experts, int n,
+                          uint64_t* addrs, uint8_t* ready);
+int oomb_tier_finish_fetch(oomb_tier tier, oomb_stream compute);
+int oomb_tier_stats(oomb_tier tier, uint64_t* stats5);
+
 /* ---- weight preparation ------------------------------------------------- */
+/* The record layout of an FP8 expert (hidden, inter multiples of 16): part
+ * offsets into *geo, the record stride (bytes) into *stride. */
+int oomb_fp8_record_layout(int64_t hidden, int64_t inter, int scale_layout, oomb_fp8_record* geo, size_t* stride);
+/* Load-time conversion of one expert into its record on the device: bf16
+ * gate, up [inter, hidden] and down [hidden, inter] quantized (as
+ * oomb_quantize_fp8) into the parts of `record` laid out by *geo.  Padding
+ * bytes are left as they are (zero the record first for a file image).  The
+ * converter adapter's per-expert step (crates/oominf-convert). */
+int oomb_quantize_fp8_record(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                             const oomb_fp8_record* geo, uint8_t* record, oomb_stream stream);
 /* The load-time quantizer on the device, byte-identical to fp8::quantize_blocks
  * (crates/oominf-core/src/fp8.rs:52-88) for OOMB_SCALE_1X128 and to its 2-D
  * block generalisation for OOMB_SCALE_128X128.  w: bf16 [n, k]. */

@@ -95,6 +95,33 @@ def e4m3_table() -> np.ndarray:
     return np.array([e4m3_to_f32(b) for b in range(256)], dtype=np.float32)
 
 
+def split_terms(x: np.ndarray, terms: int) -> np.ndarray:
+    """The tensor-core paths' activation split, restated (xsplit_kernel in
+    homelab_b200/csrc/tc.cuh): each 128-column block of every row of fp32 x as
+    `terms` e4m3 terms q_i with power-of-two scales s_i, s_i = 2^(floor(log2 m)
+    - 7) for m the block's largest residual magnitude, q_i = e4m3(residual /
+    s_i) (round to nearest even, saturating), residual -= q_i * s_i in fp32.
+    Returns the represented values sum_i s_i * q_i in float64."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    t, k = x.shape
+    tab = e4m3_table().astype(np.float64)
+    enc = np.vectorize(e4m3_from_f32, otypes=[np.int64])
+    out = np.zeros((t, k))
+    for r in range(t):
+        for b in range(0, k, 128):
+            v = x[r, b:b + 128].copy()
+            acc = np.zeros(v.shape)
+            for _ in range(terms):
+                m = np.float32(np.abs(v).max())
+                e = 0 if m == 0 else max(-100, min(100, int((m.view(np.uint32) >> 23) & 0xff) - 127 - 7))
+                sc = np.float32(2.0 ** e)
+                qv = tab[enc(v * np.float32(2.0 ** -e))]
+                acc += qv * float(sc)
+                v = (v - (qv.astype(np.float32) * sc)).astype(np.float32)
+            out[r, b:b + 128] = acc
+    return out
+
+
 def bf16_from_f32(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even bf16 bits of fp32 values (vectorised)."""
     b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
@@ -243,6 +270,55 @@ def moe_experts_f64(recs: list, geo: Fp8Record, off: np.ndarray, assign_tok: np.
     lib().oo_moe_experts_f64(C.cast(ptrs, C.c_void_p), C.addressof(geo), _p(off), _p(assign_tok),
                              n_e, _p(x), _p(y))
     return y[:a]
+
+
+def record_matrix(rec: np.ndarray, geo: Fp8Record, part: str) -> np.ndarray:
+    """The exactly decoded float64 matrix of one part ("gate", "up" or "down") of an FP8 record."""
+    H, I = int(geo.hidden), int(geo.inter)
+    n, k = (H, I) if part == "down" else (I, H)
+    w_off, s_off = int(getattr(geo, part + "_weight")), int(getattr(geo, part + "_scale"))
+    q = rec[w_off:w_off + n * k].reshape(n, k)
+    sc = rec[s_off:s_off + 4 * scale_count(n, k, int(geo.layout))].view(np.float32)
+    return dequantize(q, sc, int(geo.layout))
+
+
+def moe_experts_f64_fast(recs: list, geo: Fp8Record, off: np.ndarray, assign_tok: np.ndarray,
+                         x: np.ndarray) -> np.ndarray:
+    """moe_experts_f64 through numpy float64 matmuls, expert by expert (large shapes):
+    h = silu(x Wg^T) * (x Wu^T), y = h Wd^T, silu(v) = v / (1 + exp(-v))."""
+    xd = np.asarray(x, dtype=np.float64)
+    a = int(off[-1])
+    y = np.zeros((max(a, 1), int(geo.hidden)), dtype=np.float64)
+    for i, rec in enumerate(recs):
+        a0, a1 = int(off[i]), int(off[i + 1])
+        if a1 == a0:
+            continue
+        xr = xd[np.asarray(assign_tok[a0:a1])]
+        g = xr @ record_matrix(rec, geo, "gate").T
+        u = xr @ record_matrix(rec, geo, "up").T
+        h = g / (1.0 + np.exp(-g)) * u
+        y[a0:a1] = h @ record_matrix(rec, geo, "down").T
+    return y[:a]
+
+
+def attention_decode_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, kv_len, scale: float) -> np.ndarray:
+    """Decode attention in float64: q [B, H, D]; k, v [B, kv_max, Hkv, D] (exact values);
+    out[b, h] = softmax_j(scale * q[b, h] . k[b, j, h // G]) v[b, j, h // G] over j < kv_len[b]."""
+    B, H, D = q.shape
+    Hkv = k.shape[2]
+    G = H // Hkv
+    lens = np.full(B, int(kv_len)) if np.isscalar(kv_len) else np.asarray(kv_len)
+    out = np.zeros((B, H, D))
+    for b in range(B):
+        L = int(lens[b])
+        if L == 0:
+            continue
+        for h in range(H):
+            kk = k[b, :L, h // G].astype(np.float64)
+            s = kk @ q[b, h].astype(np.float64) * scale
+            p = np.exp(s - s.max())
+            out[b, h] = (p / p.sum()) @ v[b, :L, h // G].astype(np.float64)
+    return out
 
 
 def combine_slots(y: np.ndarray, slot_assign: np.ndarray, w: np.ndarray, t: int, h: int, k: int):

@@ -2,7 +2,8 @@
 
 Bars: within the fp32-accumulation bound of a float64 evaluation over the
 exactly decoded weights, |y - y64| <= 4e-6 * sum|x*w| (the activation split
-into e4m3 terms is exact for bf16 inputs, to 16 bits for fp32 inputs), and the
+into e4m3 terms is exact for bf16 inputs and keeps 24 bits of each 128-column
+block for fp32 inputs), and the
 BASELINE max relative error 1e-3; bf16 outputs equal RN of the fp32 result;
 repeated calls on one workspace give identical bits (self-resetting split-K
 counters, fixed summation order).
@@ -92,11 +93,48 @@ def test_tc_gemm_matches_oracle(gpu, t, n, k, layout, xbf16, tiles):
     assert torch.equal(yb, y.to(torch.bfloat16))
 
 
+def small_value_case(seed, t, n, k):
+    """Weights whose first column of every 128-column block is zero, and fp32
+    activations whose block maximum (a full-mantissa value in [1, 2)) sits in
+    that column while every other value lies in [2^-20, 2^-19): sum|x*w| comes
+    from values below 2^-16 of their block's largest, which a split keeping 16
+    bits of each block (four e4m3 terms) represents with a few bits only (it
+    misses the fp32 bound several times over), while six terms (24 bits) meet it."""
+    w = O.bf16_to_f32(O.normal_bf16(seed, n * k, 0.0, 0.02)).reshape(n, k)
+    w[:, ::128] = 0.0
+    wb = O.bf16_from_f32(w.reshape(-1))
+    rng = np.random.default_rng(seed + 1)
+    x = (2.0 ** -20 * (1.0 + rng.random((t, k))) * rng.choice([-1.0, 1.0], (t, k))).astype(np.float32)
+    x[:, ::128] = (1.0 + rng.random((t, k // 128))).astype(np.float32)
+    return wb, x
+
+
+@pytest.mark.parametrize("t", [1, 5, 32])
+def test_tc_fp32_split_keeps_24_bits(gpu, t):
+    n, k = 256, 128
+    wb, x32 = small_value_case(870 + t, t, n, k)
+    q, s = O.quantize_blocks(wb, n, k, SCALE_128X128)
+    ws = gpu.gemm_fp8_workspace(t, n, k, torch.float32)
+    y = torch.empty((t, n), dtype=torch.float32, device=DEV)
+    gpu.gemm_fp8_tc(dev(x32), dev(q), dev(s), y, t, n, k, SCALE_128X128, ws)
+    torch.cuda.synchronize()
+    truth, mag = O.gemv_fp8_f64(x32, q, s, SCALE_128X128)
+    bound = mag * FP32_BOUND + 1e-30
+    worst = float((np.abs(y.cpu().numpy().astype(np.float64) - truth) / bound).max())
+    assert worst <= 1.0, f"error {worst:.3g}x the fp32 bound"
+    # the case discriminates: the same split with four terms (16 bits) misses the bound
+    wq = O.dequantize(q, s, SCALE_128X128).astype(np.float64)
+    y4 = O.split_terms(x32, 4) @ wq.T
+    assert float((np.abs(y4 - truth) / bound).max()) > 2.0
+
+
 def test_tc_rejects_unsupported_shapes(gpu):
     from homelab_b200 import _lib
     L = _lib.lib()
     assert L.oomb_gemm_fp8_workspace_bytes(1, 100, 1024, _lib.BF16) == 0
     assert L.oomb_gemm_fp8_workspace_bytes(65, 128, 1024, _lib.BF16) == 0
+    assert L.oomb_gemm_fp8_workspace_bytes(33, 128, 1024, _lib.F32) == 0
+    assert L.oomb_gemm_fp8_workspace_bytes(32, 128, 1024, _lib.F32) > 0
     assert L.oomb_gemm_fp8_workspace_bytes(1, 128, 1000, _lib.BF16) == 0
 
 

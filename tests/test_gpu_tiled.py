@@ -4,7 +4,8 @@ oracle, through the C ABI.
 
 Bars, as for the dense tensor-core GEMM: every projection output within the
 fp32-accumulation bound of a float64 evaluation over the exactly decoded weights,
-|y - y64| <= 4e-6 * sum|x*w|, and the BASELINE max relative error 1e-3; the
+|y - y64| <= 4e-6 * sum|x*w| (fp32 activations keep 24 bits of each 128-column
+block, the reference Exact precision's bar), and the BASELINE max relative error 1e-3; the
 tiled gate -> up -> swiglu -> down chain within 1e-4 of the oracle's float64
 experts (the bar of the CUDA-core expert kernels); repeated calls give
 identical bits; an assignment's output does not depend on the chunk size.
@@ -216,6 +217,36 @@ def test_tiled_groups_with_empty_experts_and_offset_start(gpu, banks):
     check_bound(got[base:], truth[base:], mag[base:], "gate")
 
 
+def test_tiled_fp32_split_keeps_24_bits(gpu):
+    """The down projection with fp32 h whose values lie 2^-20..2^-19 below their
+    block's largest (bits a 16-bit split loses), over weights that are zero in
+    the block-maximum column: within the fp32 bound of float64."""
+    from test_gpu_tc import small_value_case
+    H, I, E = 1024, 128, 3
+    bank = ExpertBank(E, H, I, SCALE_128X128, DEV)
+    bank.fill_random(gpu, seed=90)
+    counts = [5, 0, 17]
+    off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    A = int(off[-1])
+    h32 = None
+    for e in range(E):
+        wb, xe = small_value_case(900 + e, max(counts[e], 1), H, I)
+        dq, ds = bank.views(e)[4], bank.views(e)[5]
+        gpu.quantize_fp8(torch.from_numpy(wb.view(np.int16)).to(DEV), H, I, SCALE_128X128, dq, ds)
+        if counts[e]:
+            h32 = xe if h32 is None else np.concatenate([h32, xe])
+    torch.cuda.synchronize()
+    g = bank.geo
+    recs = bank.addrs.contiguous()
+    y = torch.empty((A, H), dtype=torch.float32, device=DEV)
+    gpu.moe_tiled(recs, dev(off), None, E, max(counts), dev(h32), y, H, I, (g.down_weight, g.down_scale),
+                  SCALE_128X128)
+    torch.cuda.synchronize()
+    truth, mag = projection_truth(bank.host_records(), np.arange(E), off, None, h32, g.down_weight, g.down_scale,
+                                  H, I, SCALE_128X128)
+    check_bound(y.cpu().numpy(), truth, mag, "down, fp32 h with small values")
+
+
 def test_tiled_rejects_bad_arguments(gpu, banks):
     from homelab_b200 import _lib
     L = _lib.lib()
@@ -225,13 +256,17 @@ def test_tiled_rejects_bad_arguments(gpu, banks):
     off = torch.zeros(2, dtype=torch.int32, device=DEV)
     recs = banks[SCALE_128X128].addrs[:1].contiguous()
     args = dict(n=768, k=2048)
-    call = lambda n, k, w_off=g.gate_weight: L.oomb_moe_tiled_fp8(  # noqa: E731
-        recs.data_ptr(), off.data_ptr(), None, 1, 0, x.data_ptr(), _lib.BF16, y.data_ptr(), n, k, w_off,
-        g.gate_scale, g.layout, None)
+    nws = L.oomb_moe_tiled_fp8_workspace_bytes(4, 2048, _lib.BF16)
+    ws = torch.empty(nws, dtype=torch.uint8, device=DEV)
+    call = lambda n, k, w_off=g.gate_weight, wsb=nws, amax=4: L.oomb_moe_tiled_fp8(  # noqa: E731
+        recs.data_ptr(), off.data_ptr(), None, 1, 0, amax, x.data_ptr(), _lib.BF16, y.data_ptr(), n, k, w_off,
+        g.gate_scale, g.layout, ws.data_ptr(), wsb, None)
     assert call(**args) == 0
     assert call(700, 2048) == _lib.E_SHAPE
     assert call(768, 2000) == _lib.E_SHAPE
     assert call(768, 2048, g.gate_weight + 8) == _lib.E_ALIGN
+    assert call(768, 2048, wsb=nws - 1) == _lib.E_WORKSPACE
+    assert call(768, 2048, amax=0) == _lib.E_SHAPE
     torch.cuda.synchronize()
 
 

@@ -212,3 +212,51 @@ def test_combine_slots_is_slot_ordered_fma():
     out = O.combine_slots(y, slot, w, t, h, k)
     truth = O.combine_slots_f64(y.astype(np.float64), slot, w, t, h, k)
     assert np.abs(out - truth).max() < 1e-5
+
+
+def test_split_terms_exactness():
+    """The tensor-core activation split: two e4m3 terms reproduce bf16 activations
+    exactly; six terms keep fp32 activations to within 2^-24 of their 128-column
+    block's largest magnitude, including values far below it (2^-20), which four
+    terms (16 bits) leave with a few bits only."""
+    xb = O.bf16_to_f32(O.normal_bf16(1300, 4 * 256)).reshape(4, 256)
+    assert np.array_equal(O.split_terms(xb, 2), xb.astype(np.float64))
+    rng = np.random.default_rng(1301)
+    x = rng.standard_normal((3, 256)).astype(np.float32)
+    x[1] = (2.0 ** -20 * (1.0 + rng.random(256))).astype(np.float32)
+    x[1, ::128] = (1.0 + rng.random(2)).astype(np.float32)
+    bm = np.abs(x.reshape(3, 2, 128)).max(2).repeat(128, 1).astype(np.float64)
+    err6 = np.abs(O.split_terms(x, 6) - x) / bm
+    assert err6.max() <= 2.0 ** -24
+    small = np.ones(256, dtype=bool)
+    small[::128] = False
+    rel4 = np.abs(O.split_terms(x[1:2], 4)[0] - x[1]) / np.abs(x[1])
+    rel6 = np.abs(O.split_terms(x[1:2], 6)[0] - x[1]) / np.abs(x[1])
+    assert rel4[small].max() > 2.0 ** -13  # four terms: about 12 bits of the small values
+    assert rel6[small].max() < 2.0 ** -20  # six terms: the bits down to 2^-24 of the block's largest
+
+
+def test_fast_expert_truth_matches_c_loop():
+    """The numpy float64 expert truth (large shapes) agrees with the C loop."""
+    from homelab_b200.records import record_layout
+    H, I = 256, 128
+    geo, stride = record_layout(H, I, O.SCALE_128X128)
+    g = O.Fp8Record()
+    for f, _ in O.Fp8Record._fields_:
+        setattr(g, f, getattr(geo, f))
+    recs = []
+    for e in range(3):
+        r = np.zeros(stride, np.uint8)
+        for part, (n, k) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+            q, sc = O.quantize_blocks(O.normal_bf16(1400 + 3 * e + len(part), n * k, 0.0, 0.02), n, k,
+                                      O.SCALE_128X128)
+            wo, so = getattr(g, part + "_weight"), getattr(g, part + "_scale")
+            r[wo:wo + n * k] = q.reshape(-1)
+            r[so:so + 4 * sc.size] = sc.view(np.uint8)
+        recs.append(r)
+    x = O.normal_f32(1410, 2 * H).reshape(2, H)
+    off = np.array([0, 2, 3, 4], np.int32)
+    tok = np.array([0, 1, 1, 0], np.int32)
+    a = O.moe_experts_f64(recs, g, off, tok, x)
+    b = O.moe_experts_f64_fast(recs, g, off, tok, x)
+    assert np.abs(a - b).max() <= 1e-12 * np.abs(a).max()
