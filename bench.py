@@ -78,6 +78,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU work of the cpu_baseline / reference sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--quick", action="store_true", help="skip the extra per-config measurements")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="run N eager decode steps of the workload and exit (a small driver for ncu)")
     ap.add_argument("--profile-mlp", type=int, default=0, metavar="B",
@@ -456,11 +457,15 @@ def run_ours(args, rank, world, local_rank):
     gemv1 = measure_gemv_config1(gpu, dev, s)
     del layers
     torch.cuda.empty_cache()
-    mlp3 = measure_mlp_config3(gpu, dev, s) if world == 1 else None
-    experts5 = measure_experts_config5(gpu, dev, s) if world == 1 else None
-    staging = measure_staging(dev) if world == 1 else None
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
+    extras = world == 1 and not args.quick
+    mlp3 = measure_mlp_config3(gpu, dev, s) if extras else None
+    experts5 = measure_experts_config5(gpu, dev, s) if extras else None
+    staging = measure_staging(dev) if extras else None
+    attn4 = measure_attention_config4(gpu, dev, s, peak=peak) if extras else None
+    layers4 = measure_layers_config4(gpu, dev, s, peak=peak) if extras else None
+    offload5 = measure_offload_config5(gpu, dev, s) if extras else None
 
     result = None
     if rank == 0:
@@ -487,6 +492,9 @@ def run_ours(args, rank, world, local_rank):
             "batched_dense_config3": mlp3,
             "grouped_experts_config5": experts5,
             "offload_staging_config5": staging,
+            "attention_config4": attn4,
+            "decode_layers_config4": layers4,
+            "offload_overlap_config5": offload5,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
             # per step: one decode_kernel (the chain route, gate/up, down, combine when
@@ -807,6 +815,310 @@ def measure_gemv_config1(gpu, dev, s, copies=16, launches=320):
     return {"gbs": nbytes / (us * 1e-6) / 1e9, "bytes": nbytes, "us": us}
 
 
+def _graph_time(s, fn, launches, reps=3):
+    """Best per-call time (us) of `launches` calls of fn captured in one CUDA graph."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(launches):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = float("inf")
+    for _ in range(reps):
+        with torch.cuda.stream(s):
+            ev0.record(s)
+            g.replay()
+            ev1.record(s)
+        ev1.synchronize()
+        best = min(best, ev0.elapsed_time(ev1) / launches)
+    del g
+    return best * 1e3
+
+
+def measure_attention_config4(gpu, dev, s, batches=(1, 8, 32), ctx=4096, peak=6541.5):
+    """BASELINE config 4's attention: 32 query heads over 8 kv heads, head_dim 128,
+    bf16 KV cache, context 4096, one query token per sequence.  Enough cache copies
+    rotate that every launch reads from HBM (>= 256 MB a rotation)."""
+    import torch
+    H, Hkv, D = 32, 8, 128
+    out = {}
+    for B in batches:
+        per = B * ctx * Hkv * D * 2 * 2
+        copies = max(1, -(-256 * 2 ** 20 // per))
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(17 + B)
+        caches = [(torch.randn((B, ctx, Hkv, D), generator=gen, device=dev).to(torch.bfloat16),
+                   torch.randn((B, ctx, Hkv, D), generator=gen, device=dev).to(torch.bfloat16)) for _ in range(copies)]
+        q = torch.randn((B, H, D), generator=gen, device=dev).to(torch.bfloat16)
+        o = torch.empty((B, H, D), dtype=torch.bfloat16, device=dev)
+        ws = gpu.attention_workspace(B, H, Hkv, D, ctx)
+
+        def one(i):
+            k, v = caches[i % copies]
+            gpu.attention_decode(q, k, v, o, ctx, 1.0 / D ** 0.5, ws, Hkv)
+
+        for i in range(4):
+            one(i)
+        us = _graph_time(s, one, max(40, 4 * copies))
+        nbytes = per + 2 * B * H * D * 2
+        out[f"B{B}"] = {"us": us, "gbs": nbytes / (us * 1e-6) / 1e9, "frac": nbytes / (us * 1e-6) / 1e9 / peak,
+                        "algorithmic_bytes": nbytes}
+        del caches
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_layers_config4(gpu, dev, s, batches=(1, 8, 32), layers=32, ctx=4096, steps=3, peak=6541.5):
+    """BASELINE config 4 as a decode step over `layers` layers: per layer the q and
+    kv projections (FP8 4096 x 4096 and 2048 x 4096, the projection shapes assumed:
+    BASELINE gives none), the KV append of the new token, GQA attention (32 / 8
+    heads, head_dim 128, bf16 cache at context 4096), the output projection (FP8
+    4096 x 4096) and the MoE layer (router, 64 experts top-6, intermediate 1408, 2
+    shared experts with a sigmoid gate).  Norms, rotary embedding and residual adds
+    are not part of the path and are left out.  Weights random-init; every layer
+    has its own allocations (one random bank is quantized, then copied)."""
+    import torch
+
+    import homelab_b200 as hb
+    from homelab_b200.records import ExpertBank, SharedExpertBank
+    Hd, E, K, I, SI, NH, NKV, D = 4096, 64, 6, 1408, 2816, 32, 8, 128
+    Bmax = max(batches)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(23)
+    src = ExpertBank(E, Hd, I, hb.SCALE_128X128, dev)
+    src.fill_random(gpu, seed=24)
+    sh_src = SharedExpertBank(Hd, SI, hb.SCALE_128X128, dev)
+    sh_src.fill_random(gpu, seed=25)
+    proj = []
+    for (n, k) in ((Hd, Hd), (2 * NKV * D, Hd), (Hd, Hd)):
+        w = (torch.randn((n, k), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        proj.append(gpu.quantize_fp8(w.view(torch.int16), n, k, hb.SCALE_128X128))
+    kc0 = torch.randn((Bmax, ctx, NKV, D), generator=gen, device=dev).to(torch.bfloat16)
+    vc0 = torch.randn((Bmax, ctx, NKV, D), generator=gen, device=dev).to(torch.bfloat16)
+    L = []
+    for li in range(layers):
+        bank = ExpertBank(E, Hd, I, hb.SCALE_128X128, dev)
+        bank.buf.copy_(src.buf)
+        sh = SharedExpertBank(Hd, SI, hb.SCALE_128X128, dev)
+        for a, b in ((sh.gate_up_q, sh_src.gate_up_q), (sh.gate_up_s, sh_src.gate_up_s), (sh.down_q, sh_src.down_q),
+                     (sh.down_s, sh_src.down_s), (sh.gate_w, sh_src.gate_w)):
+            a.copy_(b)
+        router = (torch.randn((E, Hd), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        ml = hb.MoeLayer(hidden=Hd, experts=E, top_k=K, router_w=router.data_ptr(), recs=bank.addrs.data_ptr())
+        ml.geo = bank.geo
+        w = [(q.clone(), sc.clone()) for q, sc in proj]
+        L.append(dict(bank=bank, sh=sh, S=sh.view(), router=router, ml=ml, w=w, kc=kc0.clone(), vc=vc0.clone()))
+    del src, sh_src, kc0, vc0
+    torch.cuda.empty_cache()
+    out = {}
+    for B in batches:
+        xs = [torch.randn((B, Hd), generator=gen, device=dev).to(torch.bfloat16) for _ in range(2)]
+        q = torch.empty((B, Hd), dtype=torch.float32, device=dev)
+        kv = torch.empty((B, 2 * NKV * D), dtype=torch.float32, device=dev)
+        att = torch.empty((B, NH, D), dtype=torch.bfloat16, device=dev)
+        o = torch.empty((B, Hd), dtype=torch.bfloat16, device=dev)
+        nxt = [torch.empty((B, Hd), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        wsq = gpu.gemm_fp8_workspace(B, Hd, Hd) if B >= 2 else None
+        wskv = gpu.gemm_fp8_workspace(B, 2 * NKV * D, Hd) if B >= 2 else None
+        wso = gpu.gemm_fp8_workspace(B, Hd, Hd) if B >= 2 else None
+        wsa = gpu.attention_workspace(B, NH, NKV, D, ctx)
+        wsl = gpu.moe_layer_workspace(L[0]["ml"], L[0]["S"], B)
+
+        def step(i):
+            x = xs[i % 2]
+            for li, ly in enumerate(L):
+                (wq, sq), (wkv, skv), (wo, so) = ly["w"]
+                kc, vc = ly["kc"][:B], ly["vc"][:B]
+                gpu.gemm_fp8(x, wq, sq, q, B, Hd, Hd, hb.SCALE_128X128, wsq)
+                gpu.gemm_fp8(x, wkv, skv, kv, B, 2 * NKV * D, Hd, hb.SCALE_128X128, wskv)
+                gpu.kv_append(kv[:, :NKV * D], kc, ctx - 1)
+                gpu.kv_append(kv[:, NKV * D:], vc, ctx - 1)
+                gpu.attention_decode(q.view(B, NH, D), kc, vc, att, ctx, 1.0 / D ** 0.5, wsa, NKV)
+                gpu.gemm_fp8(att.view(B, Hd), wo, so, o, B, Hd, Hd, hb.SCALE_128X128, wso)
+                y = nxt[li % 2]
+                gpu.moe_layer_decode(ly["ml"], ly["S"], o, B, y, wsl)
+                x = y
+
+        for i in range(2):
+            step(i)
+        torch.cuda.synchronize()
+        us = _graph_time(s, step, steps, reps=2)
+        distinct = E * (1.0 - ((E - K) / E) ** B)  # expected distinct routed experts a layer
+        wb = L[0]["bank"].stride  # upper bound of an expert's bytes (record stride)
+        from homelab_b200.records import weight_bytes
+        eb = weight_bytes(L[0]["bank"].geo)
+        per_layer = (2 * Hd * Hd + 2 * NKV * D * Hd + B * ctx * NKV * D * 2 * 2 + E * Hd * 2 +
+                     (2 * SI * Hd + Hd * SI) + distinct * eb)
+        nbytes = layers * per_layer
+        out[f"B{B}"] = {"us_per_step": us, "tokens_per_s": B / (us * 1e-6), "gbs": nbytes / (us * 1e-6) / 1e9,
+                        "frac": nbytes / (us * 1e-6) / 1e9 / peak, "expected_distinct_experts": distinct,
+                        "algorithmic_bytes_per_step": nbytes, "record_stride": wb}
+    del L
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_offload_config5(gpu, dev, s, batch=8, experts=64, cold=(0, 2, 4, 8), reps=3):
+    """BASELINE config 5's offload: expert records of hidden 4096 / intermediate 2048
+    (25.2 MB each) in a pinned host arena served by the expert tier
+    (homelab_b200.stage.ExpertTier: the two-phase fetch).  A step routes `batch`
+    tokens over `experts` experts (top-8), fetches them with `c` of them cold (their
+    records copy in on the copy queue while the resident ones compute), then runs
+    the cold ones and the slot combine.  Reported per c: the whole step on the
+    compute stream, the same step with every record resident, and the c records'
+    copies alone."""
+    import numpy as np
+    import torch
+
+    import homelab_b200 as hb
+    from homelab_b200.records import ExpertBank
+    from homelab_b200.stage import ExpertTier, HostArena, Transfer, stage_records
+    Hd, I, K = 4096, 2048, 8
+    bank = ExpertBank(experts, Hd, I, hb.SCALE_128X128, dev)
+    bank.fill_random(gpu, seed=41)
+    arena = HostArena(experts, bank.stride)
+    arena.buf.copy_(bank.buf.cpu())
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(42)
+    router = (torch.randn((experts, Hd), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    x = torch.randn((batch, Hd), generator=gen, device=dev).to(torch.bfloat16)
+    logits = torch.empty((batch, experts), dtype=torch.float32, device=dev)
+    ids = torch.empty((batch, K), dtype=torch.int32, device=dev)
+    w = torch.empty((batch, K), dtype=torch.float32, device=dev)
+    gpu.router_logits(x, router, logits, batch, experts, Hd)
+    gpu.router_topk(logits, ids, w, batch, experts, K)
+    ids_h = ids.cpu().numpy()
+    active = np.unique(ids_h)
+    geo = bank.geo
+    tier = ExpertTier(arena, 1, experts, slots=len(active) + max(cold), device=dev)
+    out = {"batch": batch, "distinct_experts": int(len(active)), "record_bytes": bank.stride}
+
+    def tables(addrs, ready):
+        order = [i for i in range(len(active)) if ready[i]] + [i for i in range(len(active)) if not ready[i]]
+        off, tok, slot = [0], [], np.empty(batch * K, dtype=np.int32)
+        for i in order:
+            for tt in range(batch):
+                for sl in range(K):
+                    if ids_h[tt, sl] == active[i]:
+                        slot[tt * K + sl] = len(tok)
+                        tok.append(tt)
+            off.append(len(tok))
+        return (torch.tensor([addrs[i] for i in order], dtype=torch.int64, device=dev),
+                torch.tensor(off, dtype=torch.int32, device=dev), torch.tensor(tok, dtype=torch.int32, device=dev),
+                torch.from_numpy(slot).to(dev), sum(ready))
+
+    A = batch * K
+    h = torch.empty((A, I), dtype=torch.float32, device=dev)
+    y = torch.empty((A, Hd), dtype=torch.float32, device=dev)
+    o = torch.empty((batch, Hd), dtype=torch.float32, device=dev)
+
+    def run(recs, offd, tokd, slotd, nr):
+        n = len(active)
+        if nr:
+            gpu.moe_gate_up(recs[:nr], offd[:nr + 1], tokd, nr, x, h, geo)
+            gpu.moe_down(recs[:nr], offd[:nr + 1], nr, h, y, geo)
+        tier.finish_fetch()
+        if nr < n:
+            gpu.moe_gate_up(recs[nr:], offd[nr:], tokd, n - nr, x, h, geo)
+            gpu.moe_down(recs[nr:], offd[nr:], n - nr, h, y, geo)
+        gpu.moe_combine_slots(y, slotd, w, o, batch, Hd, K)
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tr = Transfer(dev)
+    q = torch.cuda.ExternalStream(tr.queue, device=dev)
+    for c in cold:
+        best, best_h2d = float("inf"), float("inf")
+        for r in range(reps + 1):
+            # make every active record resident, then evict c of them by fetching others
+            tier.begin_fetch(0, active)
+            tier.finish_fetch()
+            others = [e for e in range(experts) if e not in set(active.tolist())][:c]
+            if c:
+                tier.begin_fetch(0, list(active[c:]) + others)
+                tier.finish_fetch()
+            torch.cuda.synchronize()
+            with torch.cuda.stream(torch.cuda.current_stream(dev)):
+                ev0.record()
+                addrs, ready = tier.begin_fetch(0, active)
+                run(*tables(addrs, ready))
+                ev1.record()
+            ev1.synchronize()
+            if r:
+                best = min(best, ev0.elapsed_time(ev1) * 1e3)
+            if c and r:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                slots = torch.empty(c * bank.stride, dtype=torch.uint8, device=dev)
+                e0.record(q)
+                stage_records(tr, arena, list(range(c)), [slots.data_ptr() + j * bank.stride for j in range(c)])
+                e1.record(q)
+                e1.synchronize()
+                best_h2d = min(best_h2d, e0.elapsed_time(e1) * 1e3)
+                del slots
+        out[f"cold{c}"] = {"us_per_step": best, "h2d_only_us": best_h2d if c else 0.0,
+                           "ready": int(len(active) - c)}
+    tier.close()
+    tr.close()
+    del bank
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_reference_gemv_config1(gpu, dev, s, copies=16, launches=320):
+    """The reference's own FP8 GEMV kernel (gemv_fp8_t1, crates/oominf-cuda/kernels/
+    ops.cu:338-440, built from the reference sources by oracle/ref/Makefile and
+    launched with the plan of Gpu::gemv_at, linear.rs:259-350) beside ours, on
+    config 1 with the reference's 1x128 scales and fp32 x / y (its types),
+    back-to-back launches over `copies` weight copies.  None if the reference
+    build is absent."""
+    import ctypes as C
+
+    import torch
+
+    import homelab_b200 as hb
+    import oracle.refk as refk
+    if not refk.available():
+        return None
+    ref = refk.RefKernels(dev)
+    n = k = 4096
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12)
+    qs, ss = [], []
+    for c in range(copies):
+        wt = (torch.randn((n, k), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        q, sc = gpu.quantize_fp8(wt.view(torch.int16), n, k, hb.SCALE_1X128)
+        qs.append(q)
+        ss.append(sc)
+    x = torch.randn((1, k), generator=gen, device=dev)
+    y = torch.empty((1, n), dtype=torch.float32, device=dev)
+    splits, _, tiles = ref.gemv_plan(1, n, k)
+    partial = torch.empty(max(splits * n, 1), dtype=torch.float32, device=dev)
+    tickets = torch.zeros(max(tiles, 1), dtype=torch.int32, device=dev)
+
+    def theirs(i):
+        rc = ref.L.orl_gemv_fp8(x.data_ptr(), qs[i % copies].data_ptr(), ss[i % copies].data_ptr(), y.data_ptr(),
+                                partial.data_ptr(), tickets.data_ptr(), 1, n, k,
+                                C.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+        if rc != 0:
+            raise RuntimeError(f"reference gemv failed ({rc})")
+
+    def ours(i):
+        gpu.gemm_fp8(x, qs[i % copies], ss[i % copies], y, 1, n, k, hb.SCALE_1X128)
+
+    for i in range(8):
+        theirs(i)
+        ours(i)
+    nbytes = n * k + n * (k // 128) * 4 + k * 4 + n * 4
+    res = {}
+    for name, fn in (("reference_gemv_fp8_t1", theirs), ("ours", ours)):
+        us = _graph_time(s, fn, launches)
+        res[name] = {"us": us, "gbs": nbytes / (us * 1e-6) / 1e9}
+    res["workload"] = "config1 4096x4096 e4m3 with 1x128 scales, x fp32 batch 1, fp32 out"
+    res["algorithmic_bytes"] = nbytes
+    return res
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -830,6 +1142,13 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         per, threads, sample, _ = time_cpu(args.batch, args.cpu_seconds)
         per1, _, sample1, _ = time_cpu(args.batch, args.cpu_seconds / 3, threads=1)
+        try:
+            import torch
+            from homelab_b200.backend import Gpu
+            result["reference_gpu_gemv_config1"] = measure_reference_gemv_config1(
+                Gpu(0), torch.device("cuda", 0), torch.cuda.Stream(torch.device("cuda", 0)))
+        except Exception as e:  # the reference's kernels are a baseline: report, do not fail the run
+            result["reference_gpu_gemv_config1"] = {"error": str(e)[:200]}
         result["cpu_baseline"] = {"value": args.batch / per, "unit": "tokens/s", "cores": threads,
                                   "kind": "port", "cpu_model": cpu_model(), "value_1_thread": args.batch / per1,
                                   "sample": sample + "; oominf-cpu host expert path restated in C++/AVX-512; "

@@ -136,6 +136,7 @@ SIGNATURES = [
     ("oomb_moe_decode_fp8_noalloc", I, [C.POINTER(MoeLayer), P, I, I, P, I, P, P, S]),
     ("oomb_quantize_fp8", I, [P, I, I, I, P, P, S]),
     ("oomb_attention_decode_workspace_bytes", Z, [I, I, I, I, I]),
+    ("oomb_kv_append", I, [P, I, C.c_int64, P, C.c_int64, P, I, I, I, I, I, I, S]),
     ("oomb_fp8_record_layout", I, [C.c_int64, C.c_int64, I, C.POINTER(Fp8Record), C.POINTER(C.c_size_t)]),
     ("oomb_quantize_fp8_record", I, [P, P, P, C.POINTER(Fp8Record), P, S]),
     ("oomb_policy_create", I, [C.c_char_p, C.POINTER(C.c_void_p)]),

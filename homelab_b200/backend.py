@@ -234,6 +234,15 @@ class Gpu:
                                            kv_heads, D, kv_max, float(scale), _ptr(workspace), workspace.numel(),
                                            self._stream()), "attention_decode")
 
+    def kv_append(self, src, cache, start, t: int = 1):
+        """cache[b, start(b) + i] = bf16(src rows of sequence b) (Attention::kv_append, backend.rs:518-531).
+        src: [B * t, kv_heads * D] rows (any row stride, fp32 or bf16); cache bf16 [B, kv_max, kv_heads, D];
+        start: an int for every sequence, or a device int32 tensor [B]."""
+        B, kv_max, Hkv, D = cache.shape
+        starts, all_start = (None, int(start)) if isinstance(start, int) else (_ptr(start), 0)
+        check(self.L.oomb_kv_append(_ptr(src), _dtype_code(src), src.stride(0), _ptr(cache), cache.stride(0), starts,
+                                    all_start, B, t, Hkv, D, kv_max, self._stream()), "kv_append")
+
     def device_error(self, clear: bool = True) -> int:
         code = C.c_int(0)
         self.L.oomb_device_error(C.byref(code), int(clear))

@@ -230,4 +230,58 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0u;
 }
 
+// Appends t tokens of one kind (keys or values) per sequence to a bf16 cache:
+// cache[b][start(b) + i][c][:] = bf16(src row (b * t + i), kv head c) for i < t,
+// src rows src_row_stride elements apart, each [kv_heads, D] (fp32 or bf16).
+// Eight elements a thread (one 16-byte store).
+struct KvAppendParams {
+    const void* src;
+    int src_bf16;
+    int64_t src_row_stride;
+    uint16_t* cache;
+    int64_t seq_stride;
+    const int32_t* start;  // [B] first position to write, or null: start_all
+    int start_all;
+    int B, t, Hkv, D, kv_max;
+    unsigned* err;
+};
+
+__global__ void kv_append_kernel(const KvAppendParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int per_row = p.Hkv * p.D / 8;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(p.B) * p.t * per_row) return;
+    const int64_t row = i / per_row;
+    const int c8 = static_cast<int>(i - row * per_row) * 8;
+    const int b = static_cast<int>(row / p.t), ti = static_cast<int>(row - static_cast<int64_t>(b) * p.t);
+    const int pos = (p.start ? __ldcg(p.start + b) : p.start_all) + ti;
+    if (pos < 0 || pos >= p.kv_max) {
+        record_error(p.err, ERR_ATTN_LEN);
+        return;
+    }
+    float v[8];
+    if (p.src_bf16) {
+        const uint4 w = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.src) + row * p.src_row_stride + c8));
+        const unsigned ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            v[2 * q] = __uint_as_float(ww[q] << 16);
+            v[2 * q + 1] = __uint_as_float(ww[q] & 0xffff0000u);
+        }
+    } else {
+        const float* sp = static_cast<const float*>(p.src) + row * p.src_row_stride + c8;
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(sp)), b4 = __ldcg(reinterpret_cast<const float4*>(sp) + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b4.x, v[5] = b4.y, v[6] = b4.z, v[7] = b4.w;
+    }
+    uint4 o;
+    unsigned* ow = reinterpret_cast<unsigned*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+        ow[q] = *reinterpret_cast<unsigned*>(&h);
+    }
+    *reinterpret_cast<uint4*>(p.cache + static_cast<int64_t>(b) * p.seq_stride + static_cast<int64_t>(pos) * p.Hkv * p.D + c8) = o;
+}
+
 }  // namespace oomb

@@ -1020,6 +1020,38 @@ int oomb_attention_decode(const void* q, int q_dtype, const uint16_t* k_cache, c
     }
 }
 
+int oomb_kv_append(const void* src, int src_dtype, int64_t src_row_stride, uint16_t* cache, int64_t seq_stride,
+                   const int32_t* start, int start_all, int batch, int t, int kv_heads, int head_dim, int kv_max,
+                   oomb_stream stream) {
+    if (!src || !cache) return OOMB_E_ARG;
+    if (src_dtype != OOMB_F32 && src_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (batch < 0 || t < 0 || kv_heads <= 0 || head_dim <= 0 || kv_max <= 0 || (kv_heads * head_dim) % 8 ||
+        src_row_stride < static_cast<int64_t>(kv_heads) * head_dim ||
+        (batch > 1 && seq_stride < static_cast<int64_t>(kv_max) * kv_heads * head_dim))
+        return OOMB_E_SHAPE;
+    if (!start && (start_all < 0 || start_all + t > kv_max)) return OOMB_E_SHAPE;
+    if (!aligned16(src) || !aligned16(cache) || (src_row_stride % 8) || (seq_stride % 8)) return OOMB_E_ALIGN;
+    if (batch == 0 || t == 0) return OOMB_OK;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    KvAppendParams p{};
+    p.src = src;
+    p.src_bf16 = src_dtype == OOMB_BF16;
+    p.src_row_stride = src_row_stride;
+    p.cache = cache;
+    p.seq_stride = seq_stride;
+    p.start = start;
+    p.start_all = start_all;
+    p.B = batch;
+    p.t = t;
+    p.Hkv = kv_heads;
+    p.D = head_dim;
+    p.kv_max = kv_max;
+    p.err = d->err;
+    const int64_t n = static_cast<int64_t>(batch) * t * kv_heads * head_dim / 8;
+    return launch(kv_append_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream, p);
+}
+
 // ---- fused decode ------------------------------------------------------------
 
 namespace {

@@ -254,6 +254,19 @@ int oomb_attention_decode(const void* q, int q_dtype, const uint16_t* k_cache, c
                           int batch, int heads, int kv_heads, int head_dim, int kv_max, float scale,
                           void* workspace, size_t workspace_bytes, oomb_stream stream);
 
+/* Appends t tokens of keys (or values) per sequence to a bf16 cache laid out as
+ * oomb_attention_decode reads it: cache[b][start[b] + i][c][:] = bf16 of source
+ * row b * t + i, kv head c, i < t.  Source rows (fp32 or bf16, [kv_heads,
+ * head_dim] each) are src_row_stride elements apart, so keys and values can be
+ * read straight out of a fused projection's output.  start: device int32
+ * [batch] (the sequences' lengths before the step), or NULL for start_all.
+ * Attention::kv_append (backend.rs:518-531) for a bf16 cache, batched over
+ * sequences.  Positions outside [0, kv_max) are skipped and recorded in the
+ * device error word. */
+int oomb_kv_append(const void* src, int src_dtype, int64_t src_row_stride, uint16_t* cache, int64_t seq_stride,
+                   const int32_t* start, int start_all, int batch, int t, int kv_heads, int head_dim, int kv_max,
+                   oomb_stream stream);
+
 /* ---- fused decode step of one resident MoE layer ------------------------ */
 /* Router GEMV, softmax top-k, grouping of the step's assignments by expert
  * (expert order, slots in slot order: Moe::begin_routed / finish_routed,

@@ -136,3 +136,42 @@ def test_expert_parallel_peer_entry_points_check_arguments():
     q2 = _lib.EpPeer(fake, fake, 2, 0, 4, 8, 1024, _lib.BF16)
     assert L.oomb_moe_decode_ep_fp8(C.byref(layer), C.byref(q2), fake, _lib.BF16, 1, fake, 0, None, None, fake,
                                     1 << 30, None) == _lib.E_SHAPE
+
+
+def test_integration_rust_block_names_every_entry_point():
+    """The Rust FFI block a maintainer adds declares every entry
+    point of include/oomb.h, and nothing else."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    blocks = re.findall(r"```rust\n(.*?)```", doc, re.S)
+    ffi = next(b for b in blocks if 'extern "C"' in b and "#[link" in b)
+    rust = set(re.findall(r"pub fn (oomb_[a-z0-9_]+)\s*\(", ffi))
+    assert rust == declared_symbols(), sorted(rust ^ declared_symbols())
+
+
+def test_new_entry_points_check_arguments():
+    L = hb.lib()
+    fake = 0x10000
+    # attention: head_dim 128 only, G in {1, 2, 4, 8}, uniform length within kv_max
+    assert L.oomb_attention_decode(fake, 0, fake, fake, 0, None, 5, fake, 0, 1, 32, 8, 128, 4, 1.0, fake, 1 << 20,
+                                   None) == _lib.E_SHAPE
+    assert L.oomb_attention_decode(fake, 3, fake, fake, 0, None, 1, fake, 0, 1, 32, 8, 128, 4, 1.0, fake, 1 << 20,
+                                   None) == _lib.E_ARG
+    assert L.oomb_attention_decode(fake + 4, 0, fake, fake, 0, None, 1, fake, 0, 1, 32, 8, 128, 4, 1.0, fake,
+                                   1 << 20, None) == _lib.E_ALIGN
+    # kv append: positions past the cache, odd strides
+    assert L.oomb_kv_append(fake, 0, 1024, fake, 0, None, 4, 1, 1, 8, 128, 4, None) == _lib.E_SHAPE
+    assert L.oomb_kv_append(fake, 0, 1028, fake, 0, None, 0, 1, 1, 8, 128, 4, None) == _lib.E_ALIGN
+    # grouped tensor-core GEMM: a workspace is required
+    assert L.oomb_moe_tiled_fp8(fake, fake, None, 1, 0, 4, fake, 1, fake, 768, 2048, 0, 0, 1, None, 0,
+                                None) == _lib.E_ARG
+    assert L.oomb_moe_tiled_fp8_workspace_bytes(4, 2048, _lib.BF16) >= 4 * 2 * 2048
+    assert L.oomb_moe_tiled_fp8_workspace_bytes(4, 2048, _lib.F32) >= 4 * 6 * 2048
+    # the MoE layer entry: a shared expert of another width is refused
+    layer = hb.MoeLayer(hidden=2048, experts=64, top_k=8, router_w=fake, recs=fake)
+    from homelab_b200.records import record_layout
+    layer.geo, _ = record_layout(2048, 768)
+    sh = hb.SharedExpert(hidden=1024, inter=1536, scale_layout=1, gate_up_q=fake, gate_up_scale=fake, down_q=fake,
+                         down_scale=fake, gate_w=fake)
+    assert L.oomb_moe_layer_workspace_bytes(1, C.byref(layer), C.byref(sh), _lib.BF16) == 0
+    assert L.oomb_moe_layer_decode_fp8(C.byref(layer), C.byref(sh), fake, 1, 1, fake, 1, None, None, fake, 1 << 30,
+                                       None) == _lib.E_SHAPE

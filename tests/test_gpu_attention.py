@@ -102,3 +102,37 @@ def test_rejects_bad_arguments(gpu):
     assert L.oomb_attention_decode_workspace_bytes(1, 30, 8, 128, 128) == 0  # heads % kv_heads
     assert L.oomb_attention_decode_workspace_bytes(1, 48, 4, 128, 128) == 0  # G = 12 unsupported
     assert L.oomb_attention_decode_workspace_bytes(1, 32, 8, 128, 128) > 0
+
+
+@pytest.mark.parametrize("src_bf16", [False, True])
+def test_kv_append_then_attend(gpu, src_bf16):
+    """Keys and values of a new token appended (from a fused projection's output,
+    rows strided) at ragged positions; the cache holds bf16(src) there, nothing
+    else changes, and attention over the grown sequences matches float64."""
+    B, Hkv, H, kv_max = 3, 8, 32, 64
+    (kd, k32), (vd, v32) = cache(3000, B, kv_max, Hkv)
+    lens = [10, 0, 63]
+    kv = torch.from_numpy(O.normal_f32(3100, B * 3 * Hkv * D).reshape(B, 3 * Hkv * D)).to(DEV)
+    if src_bf16:
+        kv = kv.to(torch.bfloat16)
+    start = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    k_before = kd.clone()
+    gpu.kv_append(kv[:, Hkv * D:2 * Hkv * D], kd, start)
+    gpu.kv_append(kv[:, 2 * Hkv * D:], vd, start)
+    torch.cuda.synchronize()
+    kvf = kv.float().cpu().numpy()
+    kb16 = torch.from_numpy(kvf).to(torch.bfloat16).float().numpy()
+    for b, L in enumerate(lens):
+        assert np.array_equal(kd[b, L].float().cpu().numpy().reshape(-1), kb16[b, Hkv * D:2 * Hkv * D])
+        assert np.array_equal(vd[b, L].float().cpu().numpy().reshape(-1), kb16[b, 2 * Hkv * D:])
+        others = [j for j in range(kv_max) if j != L]
+        assert torch.equal(kd[b, others], k_before[b, others])
+    q32 = O.normal_f32(3200, B * H * D).reshape(B, H, D)
+    ws = gpu.attention_workspace(B, H, Hkv, D, kv_max)
+    out = torch.empty((B, H, D), dtype=torch.float32, device=DEV)
+    newlen = torch.tensor([L + 1 for L in lens], dtype=torch.int32, device=DEV)
+    gpu.attention_decode(torch.from_numpy(q32).to(DEV), kd, vd, out, newlen, 1.0 / np.sqrt(D), ws, Hkv)
+    torch.cuda.synchronize()
+    truth = O.attention_decode_f64(q32, kd.float().cpu().numpy(), vd.float().cpu().numpy(),
+                                   [L + 1 for L in lens], 1.0 / np.sqrt(D))
+    check(out.cpu().numpy(), truth)
