@@ -467,6 +467,9 @@ def run_ours(args, rank, world, local_rank):
     layers4 = measure_layers_config4(gpu, dev, s, peak=peak) if extras else None
     offload5 = measure_offload_config5(gpu, dev, s) if extras else None
 
+    ep5 = None
+    if world > 1 and not args.quick:
+        ep5 = measure_ep_config5(gpu, dev, s, rank, world)
     result = None
     if rank == 0:
         result = {
@@ -495,6 +498,7 @@ def run_ours(args, rank, world, local_rank):
             "attention_config4": attn4,
             "decode_layers_config4": layers4,
             "offload_overlap_config5": offload5,
+            "ep_config5": ep5,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
             # per step: one decode_kernel (the chain route, gate/up, down, combine when
@@ -1060,6 +1064,56 @@ def measure_offload_config5(gpu, dev, s, batch=8, experts=64, cold=(0, 2, 4, 8),
                            "ready": int(len(active) - c)}
     tier.close()
     tr.close()
+    del bank
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_ep_config5(gpu, dev, s, rank, world, batches=(32, 128), steps=8):
+    """BASELINE config 5 sharded over the ranks (expert parallelism): hidden 4096,
+    256 experts top-8, intermediate 2048, 128x128 block scales, experts e on rank
+    e / (256 / world) (32 per GPU at 8 GPUs); each rank decodes `batch` tokens per
+    step with the chain of kernels whose dispatch and return are stores into the
+    peers' mailboxes over NVLink (homelab_b200.ep.EpPeerMoeLayer).  Device-timed,
+    max over ranks; tokens/s over all ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import homelab_b200 as hb
+    from homelab_b200.ep import EpGpuOps, EpPeerMailboxes, EpPeerMoeLayer
+    from homelab_b200.records import ExpertBank
+    Hd, I, E, K = 4096, 2048, 256, 8
+    epr = E // world
+    bank = ExpertBank(epr, Hd, I, hb.SCALE_128X128, dev)
+    bank.fill_random(gpu, seed=100 + rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    router = (torch.randn((E, Hd), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    out = {"experts_per_gpu": epr, "transport": "peer mailboxes over NVLink, chain of kernels"}
+    for B in batches:
+        mb = EpPeerMailboxes(dist.group.WORLD, Hd, K, B, torch.bfloat16, dev)
+        layer = EpPeerMoeLayer(EpGpuOps(dev), mb, rank, Hd, E, K, I, router, bank.addrs, bank.geo, B)
+        gen.manual_seed(50 + rank)
+        xs = [torch.randn((B, Hd), generator=gen, device=dev).to(torch.bfloat16) for _ in range(4)]
+        o = torch.empty((B, Hd), dtype=torch.float32, device=dev)
+        with torch.cuda.stream(s):
+            for i in range(3):
+                layer.forward(xs[i % 4], B, o)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            ev0.record(s)
+            for i in range(steps):
+                layer.forward(xs[i % 4], B, o)
+            ev1.record(s)
+        ev1.synchronize()
+        ms = torch.tensor([ev0.elapsed_time(ev1) / steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        us = float(ms.item()) * 1e3
+        out[f"B{B}"] = {"batch_per_gpu": B, "us_per_step": us, "tokens_per_s": world * B / (us * 1e-6)}
+        torch.cuda.synchronize()
+        mb.close()
     del bank
     torch.cuda.empty_cache()
     return out

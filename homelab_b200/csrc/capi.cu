@@ -347,7 +347,7 @@ bool tc_plan(const DeviceState* d, int t, int n, int k, bool x_bf16, TcPlan& pl)
 template <bool XB, int MAXT>
 int tc_launch_t(const TcPlan& pl, const CUtensorMap& qmap, const CUtensorMap& xmap, const TcParams& tp,
                 cudaStream_t s) {
-    return launch(tc_gemm_kernel<XB, MAXT>, dim3(pl.grid), dim3(kTcThreads), pl.smem, s, qmap, xmap, tp);
+    return launch(tc_gemm_kernel<XB, MAXT>, dim3(pl.grid), dim3(EpiSplit<MAXT>::THREADS), pl.smem, s, qmap, xmap, tp);
 }
 
 template <bool XB>
@@ -400,11 +400,12 @@ bool tg_plan(int max_per_expert, bool x_bf16, int n_experts, TgParams& tp, size_
 template <bool XB>
 int tg_launch(const TgParams& tp, const CUtensorMap& xmap, int grid, size_t smem, cudaStream_t s) {
     switch (tp.chunk) {
-        case 8: return launch(tc_group_kernel<XB, 8>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
-        case 16: return launch(tc_group_kernel<XB, 16>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
-        case 32: return launch(tc_group_kernel<XB, 32>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
+        case 8: return launch(tc_group_kernel<XB, 8>, dim3(grid), dim3(EpiSplit<8>::THREADS), smem, s, xmap, tp);
+        case 16: return launch(tc_group_kernel<XB, 16>, dim3(grid), dim3(EpiSplit<16>::THREADS), smem, s, xmap, tp);
+        case 32: return launch(tc_group_kernel<XB, 32>, dim3(grid), dim3(EpiSplit<32>::THREADS), smem, s, xmap, tp);
         default:
-            if constexpr (XB) return launch(tc_group_kernel<XB, 64>, dim3(grid), dim3(kTcThreads), smem, s, xmap, tp);
+            if constexpr (XB)
+                return launch(tc_group_kernel<XB, 64>, dim3(grid), dim3(EpiSplit<64>::THREADS), smem, s, xmap, tp);
             return OOMB_E_SHAPE;
     }
 }

@@ -31,9 +31,11 @@
 // a row block split over several CTAs is summed by the last CTA to finish, in
 // CTA order (deterministic), through a caller workspace.
 //
-// Warp roles (7 warps): 0 weight TMA producer, 1 MMA issuer and tensor-memory
-// owner, 2-5 epilogue (warp w reads tensor-memory lanes 32*(w%4)..+31), 6 the
-// B loader (split activations and term scales, after the dependency wait).
+// Warp roles (11 warps): 0 weight TMA producer, 1 MMA issuer and tensor-memory
+// owner, 2-5 and 7-10 two epilogue warpgroups (warp w reads tensor-memory lanes
+// 32*(w%4)..+31; with 8 or more token slots each warpgroup folds half of the
+// tokens), 6 the B loader (split activations and term scales, after the
+// dependency wait).
 // Every wait is bounded and records an error code.
 #pragma once
 
@@ -43,7 +45,7 @@
 
 namespace oomb {
 
-constexpr int kTcThreads = 224;             // 7 warps: TMA producer, MMA, 4 epilogue, B loader
+constexpr int kTcThreads = 352;             // 11 warps: TMA producer, MMA, 2 x 4 epilogue, B loader
 constexpr int kTcTile = 128;                 // rows of a weight tile, and columns of a K block
 constexpr int kTcTileBytes = kTcTile * kTcTile;
 constexpr int kTcMaxStages = 8;              // ring depth
@@ -219,18 +221,6 @@ __global__ void pack_fp8_tiles_kernel(const uint8_t* q, int k, uint8_t* tiles) {
     }
 }
 
-template <int MAXT>
-__device__ __forceinline__ void tc_store_row(const TcParams& p, const float (&acc)[MAXT], int rb, int r) {
-#pragma unroll
-    for (int t = 0; t < MAXT; t++) {
-        if (t < p.T) {
-            const int64_t yi = static_cast<int64_t>(t) * p.nrows + rb * kTcTile + r;
-            if (p.y_bf16) static_cast<__nv_bfloat16*>(p.y)[yi] = __float2bfloat16_rn(acc[t]);
-            else static_cast<float*>(p.y)[yi] = acc[t];
-        }
-    }
-}
-
 // ---- the activation split (one pass per call) ------------------------------------------
 
 struct XsParams {
@@ -306,39 +296,45 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const XsParams p) {
     }
 }
 
-// Folds one K block from tensor memory into acc: column c = t * TS + term of
-// the buffer at taddr, for tokens t < n, with term scales sx[c]:
-//   acc[t] = fma(ws, s_0 D_0 + s_1 D_1 + ... (left to right), acc[t]).
+// Folds one K block from tensor memory into acc for tokens [t0, t0 + NT) of
+// the n present: column c = t * TS + term of the buffer at taddr, term scales
+// sx[c]:  acc[t - t0] = fma(ws, s_0 D_0 + s_1 D_1 + ... (left to right), acc).
 // Columns are read 32 at a time (one wait per 32), the tail 8 at a time, never
-// past the last 8-column group that holds a token (the buffer's end).  Called
-// by every lane of a warp with the same n.
-template <int TS, int MAXN>
-__device__ __forceinline__ void tc_fold(uint32_t taddr, const float* sx, int n, float ws, float (&acc)[MAXN]) {
-    const int ncol = (n * TS + 7) & ~7;
+// past the last 8-column group holding a present token (t0 * TS must be a
+// multiple of 8 when t0 > 0).  Entries of acc past the present tokens take
+// whatever the read columns hold and are never stored.  Called by every lane
+// of a warp with the same n.
+template <int TS, int NT>
+__device__ __forceinline__ void tc_fold(uint32_t taddr, const float* sx, int t0, int n, float ws, float (&acc)[NT]) {
+    const int nt = n - t0 < NT ? n - t0 : NT;
+    if (nt <= 0) return;
+    const int base = t0 * TS;
+    const int ncol = (nt * TS + 7) & ~7;
+    const float* sxb = sx + base;
     float u = 0.0f;
     auto fold = [&](int c, float d) {
         const int t = c / TS, term = c - (c / TS) * TS;
-        if (t < MAXN && t < n) {
-            const float v = sx[c] * d;
+        if (t < NT) {
+            const float v = sxb[c] * d;
             u = term == 0 ? v : __fadd_rn(u, v);
             if (term == TS - 1) acc[t] = fmaf(ws, u, acc[t]);
         }
     };
 #pragma unroll
-    for (int c0 = 0; c0 < MAXN * TS; c0 += 32) {
+    for (int c0 = 0; c0 < NT * TS; c0 += 32) {
         if (c0 < ncol) {
             if (c0 + 32 <= ncol) {
                 float d[32];
-                tc_ld32(taddr + static_cast<uint32_t>(c0), d);
+                tc_ld32(taddr + static_cast<uint32_t>(base + c0), d);
                 tc_wait_ld();
 #pragma unroll
                 for (int q = 0; q < 32; q++) fold(c0 + q, d[q]);
             } else {
 #pragma unroll
-                for (int c1 = c0; c1 < c0 + 32 && c1 < MAXN * TS; c1 += 8) {
+                for (int c1 = c0; c1 < c0 + 32 && c1 < NT * TS; c1 += 8) {
                     if (c1 < ncol) {
                         float d[8];
-                        tc_ld8(taddr + static_cast<uint32_t>(c1), d);
+                        tc_ld8(taddr + static_cast<uint32_t>(base + c1), d);
                         tc_wait_ld();
 #pragma unroll
                         for (int q = 0; q < 8; q++) fold(c1 + q, d[q]);
@@ -348,6 +344,17 @@ __device__ __forceinline__ void tc_fold(uint32_t taddr, const float* sx, int n, 
         }
     }
 }
+
+// The epilogue's token split: with at least 8 token slots the two warpgroups
+// take halves (their first column, HALF * TS, a multiple of 8), else warpgroup 0
+// takes all and warpgroup 1 idles.
+template <int MAXN>
+struct EpiSplit {
+    static constexpr int HALF = MAXN >= 8 ? MAXN / 2 : MAXN;
+    static constexpr bool SPLIT = MAXN >= 8;
+    static constexpr int WARPS = SPLIT ? 8 : 4;                    // epilogue warps launched
+    static constexpr int THREADS = SPLIT ? kTcThreads : 7 * 32;  // without the split: warps 0-6 only
+};
 
 template <bool XBF16, int MAXT>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -378,11 +385,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             mbar_init(&a_full[i], 1);
             mbar_init(&a_empty[i], 1);
             mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 4);
+            mbar_init(&b_empty[i], EpiSplit<MAXT>::WARPS);
         }
         for (int i = 0; i < p.nbufs; i++) {
             mbar_init(&mma_done[i], 1);
-            mbar_init(&tmem_empty[i], 4);
+            mbar_init(&tmem_empty[i], EpiSplit<MAXT>::WARPS);
         }
         fence_barrier_init();
     }
@@ -451,13 +458,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             }
         }
     } else {
-        // ================= epilogue warpgroup (warps 2..5) =================
+        // ================= epilogue warpgroups (warps 2..5 and 7..10) =================
+        using SP = EpiSplit<MAXT>;
+        const int wg = warp >= 7 ? 1 : 0;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;  // row of the tile this thread owns
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        float acc[MAXT];
+        const int t0 = wg * SP::HALF;       // this warpgroup's first token
+        const bool idle = wg == 1 && !SP::SPLIT;
+        float acc[SP::HALF];
 #pragma unroll
-        for (int t = 0; t < MAXT; t++) acc[t] = 0.0f;
+        for (int t = 0; t < SP::HALF; t++) acc[t] = 0.0f;
         // weight scales of this thread's row, fetched four tiles ahead
         auto tile_scale = [&](int i) {
             const int rb = i / p.kblocks, kb = i - rb * p.kblocks;
@@ -467,6 +478,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         float ws_ring[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) ws_ring[u] = lo + u < hi ? tile_scale(lo + u) : 0.0f;
+        // stores this warpgroup's tokens of row r of row block rb from v
+        auto store_row = [&](const float (&v)[SP::HALF], int rb) {
+#pragma unroll
+            for (int t = 0; t < SP::HALF; t++) {
+                if (t0 + t < p.T) {
+                    const int64_t yi = static_cast<int64_t>(t0 + t) * p.nrows + rb * kTcTile + r;
+                    if (p.y_bf16) static_cast<__nv_bfloat16*>(p.y)[yi] = __float2bfloat16_rn(v[t]);
+                    else static_cast<float*>(p.y)[yi] = v[t];
+                }
+            }
+        };
         for (int i = lo; i < hi; i++) {
             const int s = (i - lo) % S;
             const int j = i - lo, buf = j % p.nbufs;
@@ -478,8 +500,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             ws_ring[3] = i + 4 < hi ? tile_scale(i + 4) : 0.0f;
             if (!mbar_wait(&mma_done[buf], (j / p.nbufs) & 1, p.err, ERR_TC_WAIT + 6)) break;
             tc_fence_after();
-            tc_fold<TS, MAXT>(tmem_base + lane_base + static_cast<uint32_t>(buf * nmma), sx_ring + s * L.sx_slot, T,
-                              ws, acc);
+            if (!idle)
+                tc_fold<TS, SP::HALF>(tmem_base + lane_base + static_cast<uint32_t>(buf * nmma), sx_ring + s * L.sx_slot,
+                                      t0, T, ws, acc);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -490,15 +513,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             if (i + 1 == hi || (i + 1) % p.kblocks == 0) {
                 const int rb0 = rb * p.kblocks;
                 if ((i + 1) % p.kblocks == 0 && lo <= rb0) {
-                    tc_store_row<MAXT>(p, acc, rb, r);
+                    if (!idle) store_row(acc, rb);
                 } else {
                     // partial slot 0 when rb is where this CTA starts, else 1; each warp
-                    // fixes up its own 32 rows (counters per row block and lane quarter)
+                    // writes its tokens of its 32 rows, and the last of the 2 x (CTAs of the
+                    // row block) warps of its lane quarter to arrive sums every token
                     const int side = lo / p.kblocks == rb ? 0 : 1;
                     float* pp = p.partial + (static_cast<int64_t>(blockIdx.x) * 2 + side) * T * kTcTile;
+                    if (!idle) {
 #pragma unroll
-                    for (int t = 0; t < MAXT; t++)
-                        if (t < T) pp[t * kTcTile + r] = acc[t];
+                        for (int t = 0; t < SP::HALF; t++)
+                            if (t0 + t < T) pp[(t0 + t) * kTcTile + r] = acc[t];
+                    }
                     __threadfence();
                     __syncwarp();
                     const int c_first = tc_owner(p.tiles, rb0, grid);
@@ -506,24 +532,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     unsigned prev = 0;
                     if (lane == 0) prev = atomicAdd(p.counters + rb * 4 + quarter, 1u);
                     prev = __shfl_sync(0xffffffffu, prev, 0);
-                    if (prev == static_cast<unsigned>(c_last - c_first)) {
+                    constexpr unsigned PER_CTA = SP::SPLIT ? 2u : 1u;  // arrivals per CTA and lane quarter
+                    if (prev == PER_CTA * static_cast<unsigned>(c_last - c_first + 1) - 1u) {
                         __threadfence();
-                        float sum[MAXT];
+                        for (int tt = 0; tt < T; tt += 8) {
+                            float sum[8];
 #pragma unroll
-                        for (int t = 0; t < MAXT; t++) sum[t] = 0.0f;
-                        for (int c = c_first; c <= c_last; c++) {
-                            const int sd = tc_lo(p.tiles, c, grid) / p.kblocks == rb ? 0 : 1;
-                            const float* q = p.partial + (static_cast<int64_t>(c) * 2 + sd) * T * kTcTile + r;
+                            for (int u = 0; u < 8; u++) sum[u] = 0.0f;
+                            for (int c = c_first; c <= c_last; c++) {
+                                const int sd = tc_lo(p.tiles, c, grid) / p.kblocks == rb ? 0 : 1;
+                                const float* q = p.partial + (static_cast<int64_t>(c) * 2 + sd) * T * kTcTile + r;
 #pragma unroll
-                            for (int t = 0; t < MAXT; t++)
-                                if (t < T) sum[t] += __ldcg(q + t * kTcTile);
+                                for (int u = 0; u < 8; u++)
+                                    if (tt + u < T) sum[u] += __ldcg(q + (tt + u) * kTcTile);
+                            }
+#pragma unroll
+                            for (int u = 0; u < 8; u++) {
+                                if (tt + u < T) {
+                                    const int64_t yi = static_cast<int64_t>(tt + u) * p.nrows + rb * kTcTile + r;
+                                    if (p.y_bf16) static_cast<__nv_bfloat16*>(p.y)[yi] = __float2bfloat16_rn(sum[u]);
+                                    else static_cast<float*>(p.y)[yi] = sum[u];
+                                }
+                            }
                         }
-                        tc_store_row<MAXT>(p, sum, rb, r);
                         if (lane == 0) p.counters[rb * 4 + quarter] = 0u;
                     }
                 }
 #pragma unroll
-                for (int t = 0; t < MAXT; t++) acc[t] = 0.0f;
+                for (int t = 0; t < SP::HALF; t++) acc[t] = 0.0f;
             }
         }
     }

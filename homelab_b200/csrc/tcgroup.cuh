@@ -36,8 +36,9 @@
 // instruction, coalesced), commits one group per tile and releases a tile to the
 // MMA kTgLag tiles later, after cp.async.wait_group and a proxy fence.
 //
-// Warp roles (7 warps): 0 weight copies, 1 MMA issuer and tensor-memory owner,
-// 2-5 epilogue, 6 the B loader.  Every wait is bounded and records an error code.
+// Warp roles (11 warps): 0 weight copies, 1 MMA issuer and tensor-memory owner,
+// 2-5 and 7-10 epilogue (two warpgroups, each a half of a chunk's assignments),
+// 6 the B loader.  Every wait is bounded and records an error code.
 #pragma once
 
 #include "tc.cuh"
@@ -116,11 +117,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const __grid_co
             mbar_init(&a_full[i], 1);
             mbar_init(&a_empty[i], 1);
             mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 4);
+            mbar_init(&b_empty[i], EpiSplit<CH>::WARPS);
         }
         for (int i = 0; i < p.nbufs; i++) {
             mbar_init(&mma_done[i], 1);
-            mbar_init(&tmem_empty[i], 4);
+            mbar_init(&tmem_empty[i], EpiSplit<CH>::WARPS);
         }
         fence_barrier_init();
     }
@@ -271,13 +272,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const __grid_co
             }
         }
     } else {
-        // ================= epilogue warpgroup (warps 2..5) =================
+        // ================= epilogue warpgroups (warps 2..5 and 7..10) =================
+        using SP = EpiSplit<CH>;
+        const int wg = warp >= 7 ? 1 : 0;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;  // row of the tile this thread owns
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        float acc[CH];
+        const int t0 = wg * SP::HALF;       // this warpgroup's first assignment of a chunk
+        const bool idle = wg == 1 && !SP::SPLIT;
+        float acc[SP::HALF];
 #pragma unroll
-        for (int t = 0; t < CH; t++) acc[t] = 0.0f;
+        for (int t = 0; t < SP::HALF; t++) acc[t] = 0.0f;
         TgUnit U{};
         const float* sp = nullptr;
         for (int j = 0; j < ntiles; j++) {
@@ -293,8 +298,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const __grid_co
                                       : __ldg(sp + static_cast<int64_t>(U.rb * kTcTile + r) * KB + kb);
             if (!mbar_wait(&mma_done[buf], (j / p.nbufs) & 1, p.err, ERR_TG_WAIT + 6)) break;
             tc_fence_after();
-            tc_fold<TS, CH>(tmem_base + lane_base + static_cast<uint32_t>(buf * p.nmma),
-                            sx_ring + s * L.sx_slot + ((U.a0 * TS) & 3), U.nt, ws, acc);
+            if (!idle)
+                tc_fold<TS, SP::HALF>(tmem_base + lane_base + static_cast<uint32_t>(buf * p.nmma),
+                                      sx_ring + s * L.sx_slot + ((U.a0 * TS) & 3), t0, U.nt, ws, acc);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -303,8 +309,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const __grid_co
             }
             if (kb == KB - 1) {
 #pragma unroll
-                for (int t = 0; t < CH; t++) {
-                    if (t < U.nt) p.y[static_cast<int64_t>(U.a0 + t) * p.N + U.rb * kTcTile + r] = acc[t];
+                for (int t = 0; t < SP::HALF; t++) {
+                    if (!idle && t0 + t < U.nt) p.y[static_cast<int64_t>(U.a0 + t0 + t) * p.N + U.rb * kTcTile + r] = acc[t];
                     acc[t] = 0.0f;
                 }
             }
