@@ -83,6 +83,8 @@ def parse():
                     help="run N eager decode steps of the workload and exit (a small driver for ncu)")
     ap.add_argument("--profile-mlp", type=int, default=0, metavar="B",
                     help="with --profile: run N config-3 MLP steps at batch B instead (tensor-core path)")
+    ap.add_argument("--profile-attn", type=int, default=0, metavar="B",
+                    help="with --profile: run N config-4 decode attention launches (context 4096) at batch B instead")
     ap.add_argument("--profile-tiled", type=int, default=0, metavar="B",
                     help="with --profile: run N grouped tensor-core expert steps (config-5 shapes, 32 experts) "
                          "at batch B instead")
@@ -268,6 +270,22 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     gpu = Gpu(local_rank)
     B = args.batch
+    if args.profile and args.profile_attn:
+        # a small ncu driver: config-4 attention alone (B x 16.8 MB of cache)
+        import torch as _t
+        Bq, ctx, NH, NKV, D = args.profile_attn, 4096, 32, 8, 128
+        g = _t.Generator(device=dev)
+        g.manual_seed(3)
+        kc = _t.randn((Bq, ctx, NKV, D), generator=g, device=dev).to(_t.bfloat16)
+        vc = _t.randn((Bq, ctx, NKV, D), generator=g, device=dev).to(_t.bfloat16)
+        q = _t.randn((Bq, NH, D), generator=g, device=dev).to(_t.bfloat16)
+        o = _t.empty((Bq, NH, D), dtype=_t.bfloat16, device=dev)
+        ws = gpu.attention_workspace(Bq, NH, NKV, D, ctx)
+        for _ in range(args.profile):
+            gpu.attention_decode(q, kc, vc, o, ctx, 1.0 / D ** 0.5, ws, NKV)
+        _t.cuda.synchronize()
+        assert gpu.device_error() == 0
+        return None, None
     if args.profile and args.profile_tiled:
         # a small ncu driver: the 32-expert grouped case alone (805 MB of records)
         measure_experts_config5(gpu, dev, torch.cuda.current_stream(dev), batches=(args.profile_tiled,),
@@ -452,7 +470,9 @@ def run_ours(args, rank, world, local_rank):
     # algorithmic bytes over the device-timed step are that kernel's achieved bandwidth;
     # the stand-alone gate/up kernel is timed beside it ----
     step_bytes = E * H * 2 + 8 * B * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
-    fused = world == 1 and B <= 16 and os.environ.get("OOMB_DECODE_CHAIN") != "1"
+    chain_env = os.environ.get("OOMB_DECODE_CHAIN") == "1"
+    fused = world == 1 and B < 12 and not chain_env     # one decode_kernel launch a step
+    tiled = world == 1 and B >= 12 and not chain_env     # route, 2 splits, 3 grouped GEMMs, SwiGLU, combine
     roof = measure_gate_up(gpu, layers, dev, s, B, LAYERS)
     gemv1 = measure_gemv_config1(gpu, dev, s)
     del layers
@@ -501,14 +521,16 @@ def run_ours(args, rank, world, local_rank):
             "ep_config5": ep5,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
-            # per step: one decode_kernel (the chain route, gate/up, down, combine when
-            # OOMB_DECODE_CHAIN=1 or B > 16); expert-parallel over peer memory: router
+            # per step: one decode_kernel below 12 tokens; from 12 tokens the grouped
+            # tensor-core path (route, split x, gate, up, SwiGLU, split h, down, combine);
+            # the chain route, gate/up, down, combine with OOMB_DECODE_CHAIN=1;
+            # expert-parallel over peer memory: one launch per rank (fused), or router
             # logits, top-k, dispatch, group, gate/up, down, return, combine; over NCCL:
             # logits, top-k, meta, group, gate/up, down, scatter, combine (NCCL's own
             # kernels not counted)
             "gpu_launches": (1 if fused or (world > 1 and args.ep_transport == "peer" and args.ep_step == "fused"
                                            and B <= 16)
-                             else (4 if world == 1 else 8)) * K,
+                             else 8 if tiled else (4 if world == 1 else 8)) * K,
             "clocks": clocks,
         }
     return result, roof
@@ -996,22 +1018,27 @@ def measure_offload_config5(gpu, dev, s, batch=8, experts=64, cold=(0, 2, 4, 8),
     ids_h = ids.cpu().numpy()
     active = np.unique(ids_h)
     geo = bank.geo
-    tier = ExpertTier(arena, 1, experts, slots=len(active) + max(cold), device=dev)
+    # exactly the step's experts fit: fetching c others evicts c of them (LRU)
+    tier = ExpertTier(arena, 1, experts, slots=len(active), device=dev)
     out = {"batch": batch, "distinct_experts": int(len(active)), "record_bytes": bank.stride}
+    flat = ids_h.reshape(-1)
+    pos = np.searchsorted(active, flat)  # expert index of every slot
 
     def tables(addrs, ready):
-        order = [i for i in range(len(active)) if ready[i]] + [i for i in range(len(active)) if not ready[i]]
-        off, tok, slot = [0], [], np.empty(batch * K, dtype=np.int32)
-        for i in order:
-            for tt in range(batch):
-                for sl in range(K):
-                    if ids_h[tt, sl] == active[i]:
-                        slot[tt * K + sl] = len(tok)
-                        tok.append(tt)
-            off.append(len(tok))
-        return (torch.tensor([addrs[i] for i in order], dtype=torch.int64, device=dev),
-                torch.tensor(off, dtype=torch.int32, device=dev), torch.tensor(tok, dtype=torch.int32, device=dev),
-                torch.from_numpy(slot).to(dev), sum(ready))
+        """Resident groups first, then the loading ones (Moe::begin_routed's order); numpy, O(A)."""
+        ready = np.asarray(ready, dtype=bool)
+        rank_of = np.empty(len(active), dtype=np.int64)
+        order = np.concatenate([np.flatnonzero(ready), np.flatnonzero(~ready)])
+        rank_of[order] = np.arange(len(order))
+        a_order = np.argsort(rank_of[pos], kind="stable")  # assignments grouped, slots in slot order
+        slot = np.empty(batch * K, dtype=np.int32)
+        slot[a_order] = np.arange(batch * K, dtype=np.int32)
+        counts = np.bincount(rank_of[pos], minlength=len(active))
+        off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+        tok = (a_order // K).astype(np.int32)
+        recs = np.asarray(addrs, dtype=np.int64)[order]
+        return (torch.from_numpy(recs).to(dev), torch.from_numpy(off).to(dev), torch.from_numpy(tok).to(dev),
+                torch.from_numpy(slot).to(dev), int(ready.sum()))
 
     A = batch * K
     h = torch.empty((A, I), dtype=torch.float32, device=dev)

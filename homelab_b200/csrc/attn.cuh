@@ -22,10 +22,11 @@
 // the CP x G partial dot products of a chunk are summed over the lanes by one
 // multi-value butterfly (lane l ends with the score of (position l / G, head
 // l % G)); the chunk's softmax runs one score per lane; the weights reach
-// every lane through shared memory for the V update.  Each warp's partial
-// goes to the workspace; the last CTA of a (sequence, kv head) to finish (an
-// arrival counter that resets itself) merges them in warp order and writes
-// the output: deterministic.
+// every lane through shared memory for the V update.  The CTA merges its
+// warps' partials in shared memory (warp order) and writes one partial to the
+// workspace; the last CTA of a (sequence, kv head) to finish (an arrival
+// counter that resets itself) merges the splits' partials in split order and
+// writes the output: deterministic.
 #pragma once
 
 #include "common.cuh"
@@ -34,6 +35,7 @@ namespace oomb {
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnMaxSplits = 32;  // CTAs per (sequence, kv head): the last one merges at most this many
 
 enum : unsigned {
     ERR_ATTN_LEN = 0x800,  // a kv_len entry was outside [0, kv_max] (clamped)
@@ -52,7 +54,7 @@ struct AttnParams {
     int B, H, Hkv, kv_max;
     int splits;            // CTAs per (sequence, kv head)
     float scale;
-    float* part;           // [B][Hkv][splits * kAttnWarps][G][D + 4]: acc, m, l (rows 16-byte aligned)
+    float* part;           // [B][Hkv][splits][G][D + 4]: acc, m, l of each CTA (rows 16-byte aligned)
     unsigned* counters;    // [B * Hkv] arrivals, zero between launches
     unsigned* err;
 };
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         if (threadIdx.x == 0) record_error(p.err, ERR_ATTN_LEN);
         L = max(0, min(L, p.kv_max));
     }
-    const int W = p.splits * kAttnWarps, wi = split * kAttnWarps + warp;
+    const int W = p.splits * kAttnWarps, wi = split * kAttnWarps + warp;  // this warp's share of [0, L)
     const int j0 = static_cast<int>(static_cast<int64_t>(L) * wi / W);
     const int j1 = static_cast<int>(static_cast<int64_t>(L) * (wi + 1) / W);
 
@@ -184,17 +186,39 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         __syncwarp();
     }
 
-    // this warp's partial: acc, m, l of each head
-    const int64_t pbase = (static_cast<int64_t>(b) * p.Hkv + kvh) * W;
-    float* mine = p.part + (pbase + wi) * G * PS;
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        float* o = mine + g * PS;
-        *reinterpret_cast<float4*>(o + lane * E) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-    }
+    // ---- the CTA's partial: its warps' partials merged in warp order ----
+    __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
+    __shared__ __align__(16) float wacc[kAttnWarps][G][D];
     if (lane < G) {
-        mine[lane * PS + D] = m_run;
-        mine[lane * PS + D + 1] = l_run;
+        wm[warp][lane] = m_run;  // lane g holds head g's running max and sum
+        wl[warp][lane] = l_run;
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        *reinterpret_cast<float4*>(&wacc[warp][g][lane * E]) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    __syncthreads();
+    const int64_t pbase = (static_cast<int64_t>(b) * p.Hkv + kvh) * p.splits;
+    float* mine = p.part + (pbase + split) * G * PS;
+    for (int o = threadIdx.x; o < G * D; o += kAttnThreads) {
+        const int g = o / D, d = o - g * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wm[w][g]);
+        float a = 0.0f, l = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; w++) {
+                if (wm[w][g] == -INFINITY) continue;
+                const float f = __expf(wm[w][g] - M);
+                a = fmaf(f, wacc[w][g][d], a);
+                l = fmaf(f, wl[w][g], l);
+            }
+        }
+        mine[g * PS + d] = a;
+        if (d == 0) {
+            mine[g * PS + D] = M;
+            mine[g * PS + D + 1] = l;
+        }
     }
     __threadfence();
     __syncthreads();
@@ -205,22 +229,31 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // merge the W partials of this (sequence, kv head) in warp order
+    // ---- the last CTA of the (sequence, kv head): merge the splits' partials in split order ----
+    constexpr int kMaxSplitsSmem = kAttnWarps * D;  // factors e^(m_s - M) staged per head in wacc
     const float* all = p.part + pbase * G * PS;
+    float* fac = &wacc[0][0][0];  // [G][splits]
+    for (int g = warp; g < G; g += kAttnWarps) {
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < p.splits; s2 += 32) M = fmaxf(M, __ldcg(all + (static_cast<int64_t>(s2) * G + g) * PS + D));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        for (int s2 = lane; s2 < p.splits && s2 < kMaxSplitsSmem / G; s2 += 32) {
+            const float ms = __ldcg(all + (static_cast<int64_t>(s2) * G + g) * PS + D);
+            fac[g * (kMaxSplitsSmem / G) + s2] = (M == -INFINITY || ms == -INFINITY) ? 0.0f : __expf(ms - M);
+        }
+    }
+    __syncthreads();
     for (int o = threadIdx.x; o < G * D; o += kAttnThreads) {
         const int g = o / D, d = o - g * D;
-        float M = -INFINITY;
-        for (int w = 0; w < W; w++) M = fmaxf(M, __ldcg(all + (static_cast<int64_t>(w) * G + g) * PS + D));
+        const float* fg = fac + g * (kMaxSplitsSmem / G);
         float num = 0.0f, den = 0.0f;
-        if (M != -INFINITY) {
-            for (int w = 0; w < W; w++) {
-                const float* pr = all + (static_cast<int64_t>(w) * G + g) * PS;
-                const float mw = __ldcg(pr + D);
-                if (mw == -INFINITY) continue;
-                const float f = __expf(mw - M);
-                num = fmaf(f, __ldcg(pr + d), num);
-                den = fmaf(f, __ldcg(pr + D + 1), den);
-            }
+#pragma unroll 8
+        for (int s2 = 0; s2 < p.splits; s2++) {
+            const float* pr = all + (static_cast<int64_t>(s2) * G + g) * PS;
+            const float f = fg[s2];
+            num = fmaf(f, __ldcg(pr + d), num);
+            den = fmaf(f, __ldcg(pr + D + 1), den);
         }
         const float r = den > 0.0f ? num / den : 0.0f;  // no visible position: zeros
         const int64_t oi = (static_cast<int64_t>(b) * p.H + kvh * G + g) * D + d;

@@ -411,6 +411,37 @@ int tg_launch(const TgParams& tp, const CUtensorMap& xmap, int grid, size_t smem
 }
 
 
+// One projection of the grouped tensor-core GEMM over split activations already
+// in ws (layout xl, terms of the activation dtype x_bf16): y[a] = x[row(a)] .
+// W_e^T for every assignment of the groups; the group count is n_dev[0] (on the
+// device, at most n_experts) or n_experts.
+int tiled_projection(const DeviceState* d, const uint64_t* recs, const int32_t* off, const int32_t* n_dev,
+                     int n_experts, int max_per_expert, int a_max, bool x_bf16, uint8_t* ws, const XsLayout& xl,
+                     float* y, int n, int k, int64_t w_off, int64_t s_off, int layout, cudaStream_t stream) {
+    TgParams tp{};
+    size_t smem = 0;
+    if (!tg_plan(max_per_expert, x_bf16, n_experts, tp, smem)) return OOMB_E_SHAPE;
+    CUtensorMap xmap;
+    if (!encode_u8_tiles(&xmap, ws + xl.xs_off, xl.rows_alloc, k, tp.nmma)) return OOMB_E_LAUNCH;
+    tp.recs = recs;
+    tp.off = off;
+    tp.n_experts = n_experts;
+    tp.n_dev = n_dev;
+    tp.a_max = a_max;
+    tp.K = k;
+    tp.N = n;
+    tp.w_off = w_off;
+    tp.s_off = s_off;
+    tp.layout = layout;
+    tp.y = y;
+    tp.sx = reinterpret_cast<const float*>(ws + xl.sx_off);
+    tp.sx_stride = xl.sx_stride;
+    tp.rblocks = n / kTcTile;
+    tp.kblocks = k / kTcTile;
+    tp.err = d->err;
+    return x_bf16 ? tg_launch<true>(tp, xmap, d->sms, smem, stream) : tg_launch<false>(tp, xmap, d->sms, smem, stream);
+}
+
 // The one-launch decode (decode.cuh) for up to kDecodeMaxT tokens and routers of
 // at most kRouteSmallE experts: its plan, or false when the layer or batch is
 // outside what it covers (the chain of kernels serves those).
@@ -688,12 +719,10 @@ int oomb_moe_tiled_fp8(const uint64_t* recs, const int32_t* off, const int32_t* 
     if (workspace_bytes < xl.end) return OOMB_E_WORKSPACE;
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
-    TgParams tp{};
+    TgParams probe{};
     size_t smem = 0;
-    if (!tg_plan(max_per_expert, xb, n_experts, tp, smem)) return OOMB_E_SHAPE;
+    if (!tg_plan(max_per_expert, xb, n_experts, probe, smem)) return OOMB_E_SHAPE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    CUtensorMap xmap;
-    if (!encode_u8_tiles(&xmap, ws + xl.xs_off, xl.rows_alloc, k, tp.nmma)) return OOMB_E_LAUNCH;
     // 1. split every assignment's row (through `rows`) once into e4m3 terms;
     //    the assignment count is off[n_experts], on the device
     XsParams xp{};
@@ -712,22 +741,8 @@ int oomb_moe_tiled_fp8(const uint64_t* recs, const int32_t* off, const int32_t* 
     int rc = launch_xsplit(xb, xp, stream);
     if (rc) return rc;
     // 2. the grouped GEMM
-    tp.recs = recs;
-    tp.off = off;
-    tp.n_experts = n_experts;
-    tp.a_max = max_assignments;
-    tp.K = k;
-    tp.N = n;
-    tp.w_off = w_off;
-    tp.s_off = s_off;
-    tp.layout = scale_layout;
-    tp.y = y;
-    tp.sx = xp.sx;
-    tp.sx_stride = xp.sx_stride;
-    tp.rblocks = n / kTcTile;
-    tp.kblocks = k / kTcTile;
-    tp.err = d->err;
-    return xb ? tg_launch<true>(tp, xmap, d->sms, smem, stream) : tg_launch<false>(tp, xmap, d->sms, smem, stream);
+    return tiled_projection(d, recs, off, nullptr, n_experts, max_per_expert, max_assignments, xb, ws, xl, y, n, k,
+                            w_off, s_off, scale_layout, stream);
 }
 
 int oomb_moe_swiglu_range(const float* g, const float* u, float* h, int64_t start, int64_t end,
@@ -958,10 +973,10 @@ bool attn_plan(const DeviceState* d, int batch, int heads, int kv_heads, int hea
     const int64_t most = (static_cast<int64_t>(kv_max) + cp * kAttnWarps - 1) / (cp * kAttnWarps);
     pl.splits = static_cast<int>(want < most ? want : (most > 0 ? most : 1));
     if (pl.splits < 1) pl.splits = 1;
-    if (pl.splits > 65535) pl.splits = 65535;
+    if (pl.splits > kAttnMaxSplits) pl.splits = kAttnMaxSplits;  // the merge stages a factor per split
     pl.counters_off = 0;
     pl.part_off = (static_cast<size_t>(pairs) * 4 + 255) & ~static_cast<size_t>(255);
-    pl.ws_bytes = pl.part_off + static_cast<size_t>(pairs) * pl.splits * kAttnWarps * G * (head_dim + 4) * 4;
+    pl.ws_bytes = pl.part_off + static_cast<size_t>(pairs) * pl.splits * G * (head_dim + 4) * 4;
     return true;
 }
 }  // namespace
@@ -1058,8 +1073,23 @@ int oomb_kv_append(const void* src, int src_dtype, int64_t src_row_stride, uint1
 namespace {
 struct DecodeLayout {
     size_t ticket, sync, logits, ids, weights, n_active, active, off, assign_tok, slot_assign, recs_active,
-        h, y, total;
+        h, y, xs, xs_bytes, total;
 };
+
+// Batches from this size take the grouped tensor-core path in oomb_moe_decode_fp8
+// (route, split x once, gate and up, SwiGLU, split h, down, combine) when the
+// layer's shapes allow it; below it the one-launch kernel (or the CUDA-core chain).
+// The environment variable OOMB_DECODE_TILED_MIN_T overrides it (>= 2).
+constexpr int kDecodeTiledMinT = 12;  // measured crossover: configs 2 and 4 at 8 tokens tie, at 16 the tensor cores win 1.2-1.9x
+
+int decode_tiled_min_t() {
+    const char* env = getenv("OOMB_DECODE_TILED_MIN_T");
+    if (env && env[0]) {
+        const int v = atoi(env);
+        if (v >= 2) return v;
+    }
+    return kDecodeTiledMinT;
+}
 
 size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
@@ -1084,6 +1114,16 @@ DecodeLayout decode_layout(int t, const oomb_moe_layer* L, int ranks = 1) {
     d.recs_active = o; o = up256(o + E * 8);
     d.h = o; o = up256(o + AH * I * 4);
     d.y = o; o = up256(o + A * H * 4);
+    d.xs = o;
+    d.xs_bytes = 0;
+    if (ranks == 1 && t >= 2 && H % kTcTile == 0 && I % kTcTile == 0) {
+        // the grouped tensor-core path's split activations: x (up to six terms, fp32 x) for
+        // gate and up, then h (fp32, six terms) for down, one after the other in one region
+        const size_t a = xs_layout(0, static_cast<int>(A) * tc_ts(false), static_cast<int>(H)).end;
+        const size_t b = xs_layout(0, static_cast<int>(A) * tc_ts(false), static_cast<int>(I)).end;
+        d.xs_bytes = a > b ? a : b;
+        o = up256(o + d.xs_bytes);
+    }
     d.total = o;
     return d;
 }
@@ -1153,8 +1193,19 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
         x = xv;
     }
 
+    const bool xb = x_dtype == OOMB_BF16;
+    const int I = static_cast<int>(L->geo.inter);
+    bool tiled = t >= decode_tiled_min_t() && lay.xs_bytes > 0 && H >= 2 * I && E <= kTgMaxExperts &&
+                 (getenv("OOMB_DECODE_CHAIN") == nullptr || getenv("OOMB_DECODE_CHAIN")[0] != '1');
+    if (tiled) {
+        const size_t need = xs_layout(0, A * tc_ts(xb), H).end;
+        TgParams probe{};
+        size_t smem = 0;
+        tiled = need <= lay.xs_bytes && tg_plan(t, xb, A < E ? A : E, probe, smem) &&
+                tg_plan(t, false, A < E ? A : E, probe, smem);
+    }
     FusedDecode f;
-    if (fused_decode_plan(d, L, t, x_dtype == OOMB_BF16, f)) {
+    if (!tiled && fused_decode_plan(d, L, t, x_dtype == OOMB_BF16, f)) {
         // the whole step in one persistent launch
         DecodeParams& q = f.prm;
         q.r.x = x;
@@ -1210,17 +1261,65 @@ int oomb_moe_decode_fp8(const oomb_moe_layer* L, const void* x, int x_dtype, int
                        : launch(route_kernel<false>, dim3(grid), dim3(kRouteThreads), smem, stream, rp);
         if (rc) return rc;
     }
-    // 2. gate/up + SiLU over the active experts (an expert gets at most one
-    //    assignment per token, so at most t)
     const int max_e = A < E ? A : E;
     float* h = reinterpret_cast<float*>(ws + lay.h);
     float* y = reinterpret_cast<float*>(ws + lay.y);
+    if (tiled) {
+        // The grouped tensor-core path (Moe::run_group's tiled branch, moe.rs:746-758):
+        // x rows split once for gate and up, g and u in the y region (x staged there
+        // from host memory is dead once split), SwiGLU into h, h split, down into y.
+        // An expert gets at most one assignment per token: at most t per group.
+        uint8_t* xsr = ws + lay.xs;
+        float* g = y;
+        float* u = y + static_cast<size_t>(A) * I;
+        const XsLayout xl1 = xs_layout(0, A * tc_ts(xb), H);
+        XsParams xp{};
+        xp.x = x;
+        xp.rows = rp.assign_tok;
+        xp.a_host = A;
+        xp.a_cover = A;
+        xp.K = H;
+        xp.kblocks = H / kTcTile;
+        xp.xs = xsr + xl1.xs_off;
+        xp.rows_alloc = xl1.rows_alloc;
+        xp.sx = reinterpret_cast<float*>(xsr + xl1.sx_off);
+        xp.sx_stride = xl1.sx_stride;
+        if ((rc = launch_xsplit(xb, xp, stream))) return rc;
+        if ((rc = tiled_projection(d, rp.recs_active, rp.off, rp.n_active, max_e, t, A, xb, xsr, xl1, g, I, H,
+                                   L->geo.gate_weight, L->geo.gate_scale, L->geo.layout, stream)))
+            return rc;
+        if ((rc = tiled_projection(d, rp.recs_active, rp.off, rp.n_active, max_e, t, A, xb, xsr, xl1, u, I, H,
+                                   L->geo.up_weight, L->geo.up_scale, L->geo.layout, stream)))
+            return rc;
+        const int64_t n_h = static_cast<int64_t>(A) * I;
+        if ((rc = launch(swiglu_range_kernel, dim3(static_cast<unsigned>((n_h + 255) / 256)), dim3(256), 0, stream,
+                         static_cast<const float*>(g), static_cast<const float*>(u), h, int64_t{0}, n_h)))
+            return rc;
+        const XsLayout xl2 = xs_layout(0, A * tc_ts(false), I);
+        xp = XsParams{};
+        xp.x = h;
+        xp.a_host = A;
+        xp.a_cover = A;
+        xp.K = I;
+        xp.kblocks = I / kTcTile;
+        xp.xs = xsr + xl2.xs_off;
+        xp.rows_alloc = xl2.rows_alloc;
+        xp.sx = reinterpret_cast<float*>(xsr + xl2.sx_off);
+        xp.sx_stride = xl2.sx_stride;
+        if ((rc = launch_xsplit(false, xp, stream))) return rc;
+        if ((rc = tiled_projection(d, rp.recs_active, rp.off, rp.n_active, max_e, t, A, false, xsr, xl2, y, H, I,
+                                   L->geo.down_weight, L->geo.down_scale, L->geo.layout, stream)))
+            return rc;
+    } else {
+    // 2. gate/up + SiLU over the active experts (an expert gets at most one
+    //    assignment per token, so at most t)
     rc = launch_gate_up(d, rp.recs_active, rp.off, rp.assign_tok, rp.n_active, 0, max_e, x, rp.x_bf16 != 0, h,
                         &L->geo, t, false, stream);
     if (rc) return rc;
     // 3. down; its producer starts streaming weights while gate/up finishes
     rc = launch_down(d, rp.recs_active, rp.off, rp.n_active, 0, max_e, h, y, &L->geo, t, true, stream);
     if (rc) return rc;
+    }
     // 4. slot-order combine
     const int64_t quads = static_cast<int64_t>(t) * H / 4;
     const dim3 cgrid(static_cast<unsigned>((quads + 255) / 256));

@@ -55,7 +55,8 @@ enum : unsigned {
 struct TgParams {
     const uint64_t* recs;  // [n_experts] record addresses
     const int32_t* off;    // [n_experts + 1] CSR offsets of the groups
-    int n_experts;
+    int n_experts;         // groups (an upper bound when n_dev is set)
+    const int32_t* n_dev;  // device word holding the group count, or null: n_experts
     int a_max;             // assignments the split covered (off[n_experts] must not exceed it)
     int K, N;
     int64_t w_off, s_off;  // byte offsets of the projection's e4m3 weights and fp32 scales in a record
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const __grid_co
     pdl_wait();
     if (warp == 0) {
         // cs[e] = chunks of the groups before e (exclusive prefix), cs[n_experts] = all chunks
-        const int E = p.n_experts, per = (E + 31) / 32;
+        const int E = p.n_dev ? min(max(__ldcg(p.n_dev), 0), p.n_experts) : p.n_experts, per = (E + 31) / 32;
         const int e0 = min(E, lane * per), e1 = min(E, e0 + per);
         int mine = 0;
         for (int e = e0; e < e1; e++) {
@@ -154,14 +155,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_group_kernel(const __grid_co
             const int c = __ldcg(p.off + e + 1) - __ldcg(p.off + e);
             run += c > 0 ? (c + p.chunk - 1) / p.chunk : 0;
         }
-        if (lane == 31) {
-            // more assignments than the split covered: do nothing, report it
-            if (__ldcg(p.off + E) > p.a_max) {
-                record_error(p.err, ERR_BAD_TABLE);
-                incl = 0;
-            }
-            cs[E] = incl;
+        // more assignments than the split covered: do nothing, report it
+        if (__ldcg(p.off + E) > p.a_max) {
+            if (lane == 31) record_error(p.err, ERR_BAD_TABLE);
+            incl = 0;
         }
+        // groups past the device count (when it is on the device) hold no chunk
+        incl = __shfl_sync(0xffffffffu, incl, 31);
+        for (int e = E + lane; e <= p.n_experts; e += 32) cs[e] = incl;
     }
     tc_fence_before();
     __syncthreads();

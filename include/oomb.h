@@ -283,9 +283,16 @@ int oomb_kv_append(const void* src, int src_dtype, int64_t src_row_stride, uint1
  * The workspace must hold oomb_moe_decode_workspace_bytes(t, layer) bytes and
  * be zeroed once before first use (oomb_workspace_clear), and again after a
  * device error (oomb_device_error); calls that share a workspace must be
- * ordered on one stream.  Up to 16 tokens and 256 experts the step is one
- * persistent launch; setting the environment variable OOMB_DECODE_CHAIN=1
- * selects the chain of separate kernels instead (same results). */
+ * ordered on one stream.  Paths: below 12 tokens (up to 256 experts) the step
+ * is one persistent launch on the CUDA cores; from 12 tokens, when hidden and
+ * intermediate are multiples of 128 and hidden >= 2 * intermediate, it is the
+ * grouped tensor-core path (route, the token rows split once into e4m3 terms,
+ * gate and up, SwiGLU, down, combine: the same bits as oomb_moe_tiled_fp8 for
+ * gate, up and down, oomb_moe_swiglu_range and oomb_moe_combine_slots on the
+ * same routing); otherwise the chain of CUDA-core kernels.  The environment
+ * variable OOMB_DECODE_CHAIN=1 selects the CUDA-core chain for every batch
+ * (the bits of the one-launch step and of the expert-parallel ranks), and
+ * OOMB_DECODE_TILED_MIN_T=n moves the tensor-core threshold to n tokens. */
 size_t oomb_moe_decode_workspace_bytes(int t, const oomb_moe_layer* layer);
 int oomb_moe_decode_fp8(const oomb_moe_layer* layer, const void* x, int x_dtype, int t, void* out,
                         int out_dtype, int32_t* ids, float* weights, void* workspace,
@@ -339,7 +346,7 @@ int oomb_moe_layer_decode_fp8(const oomb_moe_layer* layer, const oomb_shared_exp
  * library; it calls no allocator.
  *   - Limit: a call fits when oomb_moe_decode_workspace_bytes(t, layer) <=
  *     OOMB_NOALLOC_SCRATCH_BYTES (8 MiB; with hidden 2048, 128 experts, top-8
- *     and intermediate 768 that is t <= 92); larger calls return
+ *     and intermediate 768 that is t <= 43); larger calls return
  *     OOMB_E_WORKSPACE before any launch.
  *   - The first call on each device, made with that device current, does a
  *     one-time set-up: it looks up the array's device address and zeroes the

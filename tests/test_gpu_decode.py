@@ -96,7 +96,7 @@ def same(a, b):
 
 @pytest.mark.parametrize("name", list(LAYERS))
 @pytest.mark.parametrize("xbf16", [True, False])
-@pytest.mark.parametrize("t", [1, 2, 5, 16])
+@pytest.mark.parametrize("t", [1, 2, 5, 11])
 def test_one_launch_equals_chain(gpu, name, xbf16, t):
     lay = get_layer(gpu, name)
     H = lay["L"].hidden
@@ -114,14 +114,20 @@ def test_repeated_launches_and_batch_sizes_share_a_workspace(gpu):
     H = lay["L"].hidden
     ws = gpu.moe_decode_workspace(lay["L"], 16)
     xs = {t: make_x(H, t, True, 900 + t) for t in (1, 3, 16)}
-    want = {t: run(gpu, lay, xs[t], t, torch.float32, chain=True) for t in xs}
+    # each path on a fresh workspace (t = 16 takes the tensor-core path unless chained)
+    want = {t: run(gpu, lay, xs[t], t, torch.float32, chain=False) for t in xs}
+    want_chain = {t: run(gpu, lay, xs[t], t, torch.float32, chain=True) for t in xs}
     for i, t in enumerate((1, 1, 16, 3, 1, 16, 16, 3)):
         got = run(gpu, lay, xs[t], t, torch.float32, chain=False, ws=ws)
+        got_chain = None
         if i % 3 == 2:  # the chain of kernels on the same workspace in between
-            run(gpu, lay, xs[t], t, torch.float32, chain=True, ws=ws)
+            got_chain = run(gpu, lay, xs[t], t, torch.float32, chain=True, ws=ws)
         torch.cuda.synchronize()
         for g, w in zip(got, want[t]):
             assert same(g, w)
+        if got_chain is not None:
+            for g, w in zip(got_chain, want_chain[t]):
+                assert same(g, w)
 
 
 def test_graph_replays_give_the_same_bits(gpu):
@@ -250,3 +256,43 @@ def test_pageable_host_memory_is_refused(gpu):
     with pytest.raises(hb.OombError):
         gpu.moe_decode(L, x.to(DEV), 1, torch.empty((1, H), dtype=torch.bfloat16), ws)
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("name,xbf16,t", [("small", True, 12), ("small", False, 16), ("wide", True, 12)])
+def test_tiled_decode_equals_tiled_calls_and_float64(gpu, name, xbf16, t):
+    """From 12 tokens the decode step runs the grouped tensor-core path: route, x
+    split once for gate and up, SwiGLU, down, combine.  Its bits equal the public
+    calls in that order (oomb_moe_tiled_fp8 for gate, up and down,
+    oomb_moe_swiglu_range, oomb_moe_combine_slots on the same routing), and it is
+    within 1e-4 of the float64 step."""
+    lay = get_layer(gpu, name)
+    L = lay["L"]
+    H, E, K, I = L.hidden, L.experts, L.top_k, L.geo.inter
+    if H % 128 or I % 128 or H < 2 * I:
+        pytest.skip("layer shape outside the grouped tensor-core path")
+    x = make_x(H, t, xbf16, 1500 + t)
+    out, ids, wts = run(gpu, lay, x, t, torch.float32, chain=False)
+    torch.cuda.synchronize()
+    x32 = x.float().cpu().numpy()
+    want_ids, want_w = O.router_topk(O.router_logits(x32, lay["router"].reshape(E, H)), K)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    active, off, tok, slot = O.group_assignments(want_ids, E)
+    A = t * K
+    b, g = lay["bank"], L.geo
+    recs = b.addrs[torch.from_numpy(active).long().to(DEV)].contiguous()
+    offd, tokd = torch.from_numpy(off).to(DEV), torch.from_numpy(tok).to(DEV)
+    gg = torch.empty((A, I), dtype=torch.float32, device=DEV)
+    uu, hh = torch.empty_like(gg), torch.empty_like(gg)
+    y = torch.empty((A, H), dtype=torch.float32, device=DEV)
+    gpu.moe_tiled(recs, offd, tokd, len(active), t, x, gg, I, H, (g.gate_weight, g.gate_scale), g.layout)
+    gpu.moe_tiled(recs, offd, tokd, len(active), t, x, uu, I, H, (g.up_weight, g.up_scale), g.layout)
+    gpu.moe_swiglu_range(gg, uu, hh, 0, A * I)
+    gpu.moe_tiled(recs, offd, None, len(active), t, hh, y, H, I, (g.down_weight, g.down_scale), g.layout)
+    want = torch.empty((t, H), dtype=torch.float32, device=DEV)
+    gpu.moe_combine_slots(y, torch.from_numpy(slot).to(DEV), wts, want, t, H, K)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want), "the decode step's tensor-core path differs from the public calls"
+    host = lay["bank"].host_records()
+    yv = O.moe_experts_f64([host[e] for e in active], L.geo, off, tok, x32)
+    truth = O.combine_slots_f64(yv, slot, want_w, t, H, K)
+    assert np.abs(out.cpu().numpy() - truth).max() / np.abs(truth).max() <= 1e-4

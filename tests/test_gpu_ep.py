@@ -2,10 +2,14 @@
 
 The virtual ranks share the device; their all-to-alls are tensor copies
 (exchange_local).  Every rank's output must equal, bit for bit, the rows of the
-fused single-GPU decode (oomb_moe_decode_fp8) of the whole batch, and an
-expert's output for an assignment must not depend on which other assignments
-share its launch.
+single-GPU decode (oomb_moe_decode_fp8) of the whole batch on the same CUDA-core
+expert kernels (OOMB_DECODE_CHAIN=1: batches of 12 and more otherwise take the
+grouped tensor-core path, whose summation order differs), and an expert's
+output for an assignment must not depend on which other assignments share its
+launch.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -40,6 +44,15 @@ def layer():
     assert gpu.device_error() == 0
 
 
+def cuda_core_decode(gpu, L, x, T, out, ws, ids=None, wts=None):
+    """The single-GPU decode on the CUDA-core expert kernels (the arithmetic the ranks use)."""
+    os.environ["OOMB_DECODE_CHAIN"] = "1"
+    try:
+        gpu.moe_decode(L, x, T, out, ws, ids, wts)
+    finally:
+        os.environ.pop("OOMB_DECODE_CHAIN", None)
+
+
 def run_virtual(layer, x, G, t):
     """The expert-parallel step over G virtual ranks, t tokens each."""
     bank, router = layer["bank"], layer["router"]
@@ -66,7 +79,7 @@ def test_expert_parallel_equals_single_gpu(layer, G, t):
     want = torch.empty((T, H), dtype=torch.float32, device=DEV)
     ids = torch.empty((T, K), dtype=torch.int32, device=DEV)
     wts = torch.empty((T, K), dtype=torch.float32, device=DEV)
-    gpu.moe_decode(L, x, T, want, ws, ids, wts)
+    cuda_core_decode(gpu, L, x, T, want, ws, ids, wts)
     outs, routing = run_virtual(layer, x, G, t)
     torch.cuda.synchronize()
     for g in range(G):
@@ -138,7 +151,7 @@ def test_peer_expert_parallel_equals_single_gpu(layer, G, t):
         want = torch.empty((T, H), dtype=torch.float32, device=DEV)
         ids = torch.empty((T, K), dtype=torch.int32, device=DEV)
         wts = torch.empty((T, K), dtype=torch.float32, device=DEV)
-        gpu.moe_decode(L, x, T, want, ws, ids, wts)
+        cuda_core_decode(gpu, L, x, T, want, ws, ids, wts)
         torch.cuda.synchronize()
         for g in range(G):
             assert torch.equal(routing[g][0], ids[g * t:(g + 1) * t])

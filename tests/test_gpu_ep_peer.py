@@ -73,7 +73,11 @@ def _worker(rank, world, port, t, result_dir, fused):
             out = torch.full((t, H), float("nan"), dtype=torch.float32, device=dev)
             layer.forward(xall[rank * t:(rank + 1) * t].contiguous(), t, out)
             want = torch.empty((world * t, H), dtype=torch.float32, device=dev)
-            gpu.moe_decode(full, xall, world * t, want, ws)
+            os.environ["OOMB_DECODE_CHAIN"] = "1"  # the CUDA-core expert kernels the ranks use
+            try:
+                gpu.moe_decode(full, xall, world * t, want, ws)
+            finally:
+                os.environ.pop("OOMB_DECODE_CHAIN", None)
             torch.cuda.synchronize()
             same &= bool(torch.equal(out, want[rank * t:(rank + 1) * t]))
         ok = same and gpu.device_error() == 0

@@ -247,9 +247,10 @@ def test_moe_decode_matches_oracle(gpu, layer2, t, out_bf16):
 
 
 def test_moe_decode_equals_separate_calls(gpu, layer2):
-    """The fused step gives the same bits as the reference-style sequence of calls."""
+    """The fused step gives the same bits as the reference-style sequence of calls
+    (below 12 tokens; larger batches take the grouped tensor-core path)."""
     H, E, K, I = 2048, 128, 8, 768
-    t = 5
+    t = 3
     L, b = layer2["layer"], layer2["bank"]
     xd = bf16_tensor(O.normal_bf16(77, t * H)).view(t, H)
     ws = gpu.moe_decode_workspace(L, t)
