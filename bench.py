@@ -1200,6 +1200,68 @@ def measure_reference_gemv_config1(gpu, dev, s, copies=16, launches=320):
     return res
 
 
+def measure_reference_mlp_config3(gpu, dev, s, B=64, launches=40):
+    """The reference's own path above 16 tokens (Linear::gemm_fp8, crates/oominf-cuda/
+    src/linear.rs:35-81, 140-205) on config 3's MLP at batch B: its fp8_dequantize_blocks
+    kernel (ops.cu:583-590) makes bf16 weights, its f32_to_bf16 rounds the activations,
+    cuBLAS multiplies in bf16 with fp32 output (gemm_ex, here torch.mm), and its
+    silu_mul_rows joins the two GEMMs; 1x128 scales (its format).  Two forms: the bf16
+    weights already dequantized (the reference keeps up to 512 MB of them, one layer of
+    this model) and dequantized on every call (a model of many layers cycles that
+    cache).  Reference kernels built from its sources by oracle/ref/Makefile; None if
+    that build is absent."""
+    import torch
+
+    import homelab_b200 as hb
+    import oracle.refk as refk
+    if not refk.available():
+        return None
+    ref = refk.RefKernels(dev)
+    H, I2 = 4096, 28672
+    I = I2 // 2
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(31)
+    w_gu = (torch.randn((I2, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    q_gu, s_gu = gpu.quantize_fp8(w_gu.view(torch.int16), I2, H, hb.SCALE_1X128)
+    del w_gu
+    w_d = (torch.randn((H, I), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    q_d, s_d = gpu.quantize_fp8(w_d.view(torch.int16), H, I, hb.SCALE_1X128)
+    del w_d
+    bf_gu = torch.empty((I2, H), dtype=torch.bfloat16, device=dev)
+    bf_d = torch.empty((H, I), dtype=torch.bfloat16, device=dev)
+    ref.dequant_fp8(q_gu, s_gu, bf_gu, I2, H)
+    ref.dequant_fp8(q_d, s_d, bf_d, H, I)
+    x = torch.randn((B, H), generator=gen, device=dev)
+    xb = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    gu = torch.empty((B, I2), dtype=torch.float32, device=dev)
+    h = torch.empty((B, I), dtype=torch.float32, device=dev)
+    hb16 = torch.empty((B, I), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((B, H), dtype=torch.float32, device=dev)
+
+    def mlp(dequant):
+        if dequant:
+            ref.dequant_fp8(q_gu, s_gu, bf_gu, I2, H)
+        ref.f32_to_bf16(x, xb, B * H)
+        torch.mm(xb, bf_gu.t(), out_dtype=torch.float32, out=gu)
+        ref.silu_mul_rows(gu, h, B, I)
+        if dequant:
+            ref.dequant_fp8(q_d, s_d, bf_d, H, I)
+        ref.f32_to_bf16(h, hb16, B * I)
+        torch.mm(hb16, bf_d.t(), out_dtype=torch.float32, out=y)
+
+    mlp(True)
+    torch.cuda.synchronize()
+    res = {"workload": f"config3 MLP batch {B}: fused gate/up [28672, 4096] + SwiGLU + down [4096, 14336], "
+                       "FP8 e4m3 1x128 scales, x fp32",
+           "weight_bytes_fp8": I2 * H + H * I, "weight_bytes_bf16": 2 * (I2 * H + H * I)}
+    for name, dq in (("bf16_weights_cached", False), ("dequantized_each_call", True)):
+        us = _graph_time(s, lambda i, dq=dq: mlp(dq), launches)
+        res[name] = {"us_per_mlp": us, "tokens_per_s": B / (us * 1e-6)}
+    del bf_gu, bf_d
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -1230,6 +1292,11 @@ def main():
                 Gpu(0), torch.device("cuda", 0), torch.cuda.Stream(torch.device("cuda", 0)))
         except Exception as e:  # the reference's kernels are a baseline: report, do not fail the run
             result["reference_gpu_gemv_config1"] = {"error": str(e)[:200]}
+        try:
+            result["reference_gpu_mlp_config3"] = measure_reference_mlp_config3(
+                Gpu(0), torch.device("cuda", 0), torch.cuda.Stream(torch.device("cuda", 0)))
+        except Exception as e:
+            result["reference_gpu_mlp_config3"] = {"error": str(e)[:200]}
         result["cpu_baseline"] = {"value": args.batch / per, "unit": "tokens/s", "cores": threads,
                                   "kind": "port", "cpu_model": cpu_model(), "value_1_thread": args.batch / per1,
                                   "sample": sample + "; oominf-cpu host expert path restated in C++/AVX-512; "

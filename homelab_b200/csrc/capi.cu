@@ -24,6 +24,24 @@
 #include "tcgroup.cuh"
 #include "tiers.h"
 
+// CTAs per SM of a stand-alone dense GEMV launch.  Two: both CTAs' consumers
+// work at once (twice the warps hiding shared-memory and FMA latency), at the
+// cost of the next launch of a dependent chain no longer fitting beside this one
+// to stream its weights early; measured on B200, config 1 (4096 x 4096, batch 1,
+// back-to-back): 6.08 us with one CTA per SM, 5.33 with two.
+#ifndef OOMB_DENSE_CTAS_PER_SM
+#define OOMB_DENSE_CTAS_PER_SM 2
+#endif
+// The same for the stand-alone expert kernels (gate/up, down): two, measured on
+// B200 at config 2 (gate/up+SiLU over 8 experts, back-to-back): 9.62 us with one
+// CTA per SM (the next kernel streaming beside it), 8.24 with two.  Either is
+// correct: an expert kernel lets its dependent launch only after its own
+// dependency wait, so a kernel reading tables two launches back finds them
+// complete whatever the occupancy.
+#ifndef OOMB_MOE_CTAS_PER_SM
+#define OOMB_MOE_CTAS_PER_SM 2
+#endif
+
 namespace oomb {
 namespace {
 
@@ -140,8 +158,9 @@ TbP tb_p(int maxn) {
     return {2, true};
 }
 
-// Completes the plan for (PARTS, P) and launches one CTA per SM, or one per
-// unit when there are fewer.  `groups` bounds the expert groups the kernel can
+// Completes the plan for (PARTS, P) and launches OOMB_MOE_CTAS_PER_SM (expert
+// kernels) or OOMB_DENSE_CTAS_PER_SM (dense) CTAs per SM, or one per unit when
+// there are fewer.  `groups` bounds the expert groups the kernel can
 // see (their count may live on the device); dense launches pass 1.
 template <int PARTS, int TB, int P, bool XB, bool MOE, bool EARLY>
 int stream_launch_tp(const DeviceState* d, int groups, StreamParams sp, cudaStream_t s) {
@@ -158,7 +177,8 @@ int stream_launch_tp(const DeviceState* d, int groups, StreamParams sp, cudaStre
     sp.slot_bytes = pl.slot_bytes;
     sp.gpe = (sp.nrows + pl.rpp - 1) / pl.rpp;
     const int64_t units = static_cast<int64_t>(groups) * sp.gpe;
-    const int grid = units < d->sms ? static_cast<int>(units > 0 ? units : 1) : d->sms;
+    const int max_grid = d->sms * (MOE ? OOMB_MOE_CTAS_PER_SM : OOMB_DENSE_CTAS_PER_SM);
+    const int grid = units < max_grid ? static_cast<int>(units > 0 ? units : 1) : max_grid;
     if (units * (grid + 1) >= (int64_t{1} << 32)) return OOMB_E_SHAPE;  // the kernel splits units in 32 bits
     if (sp.layout == OOMB_SCALE_128X128)
         return launch(stream_kernel<PARTS, TB, P, XB, MOE, EARLY, true>, dim3(grid), dim3(kThreads), pl.smem, s, sp);
@@ -500,13 +520,15 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     if (t < 1 || t > kDecodeMaxT || E > kRouteSmallE || H > kRouteMaxH) return false;
     const int TA = ranks > 0 ? ranks * t : t;  // tokens whose slots this rank groups
     if (ranks > 0 && (E % ranks || E / ranks > kThreads)) return false;
-    const TbP tp = tb_p(TA);
+    // expert parallelism groups every received slot on its own: one assignment per group
+    const TbP tp = ranks > 0 ? TbP{1, false} : tb_p(TA);
     f.tb = tp.chunked ? 2 : tp.tb;
     f.p = f.tb == 1 ? pass_len<1>() : 1;
     const StreamPlan pg = stream_plan(H, 2, f.p, layout), pd = stream_plan(I, 1, f.p, layout);
     if (pg.stage_bytes > kStageBytes || pd.stage_bytes > kStageBytes) return false;
     const int gpe_g = (I + pg.rpp - 1) / pg.rpp, gpe_d = (H + pd.rpp - 1) / pd.rpp;
-    if (gpe_d > kDecodeMaxGroups || static_cast<int64_t>(E) * (gpe_g > gpe_d ? gpe_g : gpe_d) * 1025 >= (int64_t{1} << 32))
+    const int64_t groups_max = ranks > 0 && static_cast<int64_t>(TA) * K > E ? static_cast<int64_t>(TA) * K : E;
+    if (gpe_d > kDecodeMaxGroups || groups_max * (gpe_g > gpe_d ? gpe_g : gpe_d) * 1025 >= (int64_t{1} << 32))
         return false;
     const int slot = pg.slot_bytes > pd.slot_bytes ? pg.slot_bytes : pd.slot_bytes;
     const int ms_g = f.p * 4 + f.p * 2 * pg.sr * pg.nb, ms_d = f.p * 4 + f.p * pd.sr * pd.nb;
@@ -1500,7 +1522,7 @@ int oomb_moe_decode_ep_fp8(const oomb_moe_layer* L, const oomb_ep_peer* q, const
     p.dn.x = ws + lay.h;
     p.dn.y = nullptr;
     p.dn.ep_peers = reinterpret_cast<const unsigned long long*>(q->peers);
-    p.dn.ep_back_off = static_cast<int64_t>(mb.back);
+    p.dn.ep_back_off = static_cast<int64_t>(mb.back_words);
     p.dn.ep_rank = q->rank;
     p.dn.ep_tk = t * L->top_k;
     p.sync = reinterpret_cast<unsigned*>(ws + lay.sync);

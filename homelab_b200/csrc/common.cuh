@@ -159,6 +159,19 @@ __device__ __forceinline__ uint64_t make_evict_first_policy() {
 
 // Blocks until the grids this one depends on have completed and their memory
 // is visible.  A no-op when the launch had no programmatic dependency.
+// A value and the step epoch that validates it, in one 8-byte word: an aligned
+// 64-bit store is single-copy atomic, so a reader that sees the epoch sees the
+// value stored with it, with no fence or flag between writer and reader.
+__device__ __forceinline__ void st_word_sys(unsigned long long* p, unsigned epoch, float v) {
+    const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Lets the next kernel in the stream start launching its CTAs.

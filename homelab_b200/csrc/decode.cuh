@@ -57,6 +57,12 @@ constexpr int kDecodeMaxT = 16;         // tokens per launch
 #define OOMB_DECODE_LAG 1
 #endif
 constexpr int kDecodeLag = OOMB_DECODE_LAG;
+// The same for the one-token down phase's weight stages (they do not depend on
+// h, so they can go out as soon as gate/up frees ring slots; 0: no limit).
+#ifndef OOMB_DECODE_DOWN_LAG
+#define OOMB_DECODE_DOWN_LAG OOMB_DECODE_LAG
+#endif
+constexpr int kDecodeDownLag = OOMB_DECODE_DOWN_LAG;
 constexpr int kDecodeMaxGroups = 512;   // down row groups (combine counters, bitmap bits)
 // sync-area words: the launch epoch; a ring of 4 slots of the grid barriers'
 // arrival counts (slot epoch % 4, three counts 32 words apart); the row-group counters
@@ -94,13 +100,14 @@ struct DecodeTabs {
 };
 
 // T: this rank's tokens; TA: tokens whose slots are grouped (T, or ranks * T
-// with expert parallelism).
+// with expert parallelism, where every received slot is a group of its own).
 __host__ __device__ inline DecodeTabs decode_tabs(int T, int K, int E, int TA) {
     DecodeTabs d{};
     const int A = TA * K;
+    const int NG = E > A ? E : A;  // groups at most: experts, or (expert parallelism) received slots
     int o = 0;
     d.recs = o; o += E * 8;
-    d.recs_active = o; o += E * 8;
+    d.recs_active = o; o += NG * 8;
     d.rbar = o; o += 8;
     d.xbar = o; o += 8;
     d.lg = o; o += T * E * 4;
@@ -110,8 +117,8 @@ __host__ __device__ inline DecodeTabs decode_tabs(int T, int K, int E, int TA) {
     d.w = o; o += A * 4;
     d.counts = o; o += E * 4;
     d.base = o; o += E * 4;
-    d.active = o; o += E * 4;
-    d.off = o; o += (E + 1) * 4;
+    d.active = o; o += NG * 4;
+    d.off = o; o += (NG + 1) * 4;
     d.assign_tok = o; o += A * 4;
     d.slot_assign = o; o += A * 4;
     d.n_active = o; o += 4;
@@ -166,6 +173,39 @@ __device__ __forceinline__ bool bar_wait(const unsigned* ctr, unsigned n, unsign
         }
     }
     return true;
+}
+
+// Expert parallelism: every received slot of a local expert (meta entry >= 0;
+// -1 marks another rank's) becomes a group of its own, in (source rank, token,
+// slot) order: assign_tok = the received token row, assign_ret = the slot's return
+// index.  Every group then holds one assignment, so the streaming phases run their
+// one-token form (an expert picked by two slots streams twice: rare at the batch
+// sizes this step serves).  One warp; all its lanes call this.
+__device__ void group_singletons(const RouteParams& p, const GroupOut& g, const int32_t* meta,
+                                 const uint64_t* recs_sm) {
+    const int lane = threadIdx.x & 31;
+    const int n = p.T * p.K;
+    int run = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const int e = i < n ? meta[i] : -1;
+        const bool valid = e >= 0 && e < p.E;
+        if (e >= p.E) record_error(p.err, ERR_BAD_TABLE);
+        const unsigned vm = __ballot_sync(0xffffffffu, valid);
+        if (valid) {
+            const int idx = run + __popc(vm & ((1u << lane) - 1u));
+            g.active[idx] = e;
+            g.off[idx] = idx;
+            g.assign_tok[idx] = i / p.K;
+            g.assign_ret[idx] = i;
+            g.recs_active[idx] = recs_sm[e];
+        }
+        run += __popc(vm);
+    }
+    if (lane == 0) {
+        g.off[run] = run;
+        *g.n_active = run;
+    }
 }
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory"); }
@@ -383,10 +423,10 @@ __device__ bool down1_consume(const DecodeParams& p, const int32_t* ids_sm, cons
 //   rank g's mailbox and raises the flag there; every CTA waits for all
 //   sources' flags and groups the received slots (local expert ids, -1 for
 //   another rank's) in (source, token, slot) order; the streaming phases run
-//   over the local experts, down's reduction storing each output row straight
-//   into its source rank's mailbox; a grid barrier, CTA g raises the return
-//   flag on rank g, and every CTA, once all ranks' flags are up, combines its
-//   share of this rank's outputs in slot order from the mailbox.
+//   over the local experts, down's reduction storing each output value into its
+//   source rank's mailbox as an (epoch, value) word over NVLink; the combine of
+//   each rank polls the words of its tokens' slots (bounded) and adds them in
+//   slot order: no barrier, fence or flag on the return.
 template <bool XBF16, bool BLK, int TB, int P, bool EP>
 __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -526,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
                           static_cast<const uint8_t*>(p.r.x), static_cast<size_t>(T) * H * p.ep.xb);
                 __syncthreads();
                 if (threadIdx.x == 0) {
-                    __threadfence_system();
+                    ep_fence_release_sys();
                     ep_st_relaxed_sys(reinterpret_cast<unsigned*>(dst + mb.flags_dispatch) + p.ep.rank, ep_ep);
                 }
             }
@@ -543,12 +583,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
             rq.E = p.epr;
             const GroupOut go{n_active, reinterpret_cast<int32_t*>(tabs + dt.active), off_sm, assign_tok, slot_sm,
                               recs_active, reinterpret_cast<int32_t*>(tabs + dt.aret)};
-            if (G * A <= 32) {
-                if (warp == 0) group_warp<true>(rq, go, rmeta, recs_sm);
-            } else {
-                group_assignments<kThreads, true>(rq, go, rmeta, reinterpret_cast<int32_t*>(tabs + dt.counts),
-                                                  reinterpret_cast<int32_t*>(tabs + dt.base), recs_sm);
-            }
+            if (warp == 0) group_singletons(rq, go, rmeta, recs_sm);
         } else {
             const GroupOut go{n_active, reinterpret_cast<int32_t*>(tabs + dt.active), off_sm, assign_tok, slot_sm,
                               recs_active, nullptr};
@@ -565,7 +600,8 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     // ---- 4. gate/up then down through one ring ----
     const int n_e = *n_active;
     const Tables tgu{recs_active, off_sm, assign_tok, n_e, nullptr};
-    const Tables tdn{recs_active, off_sm, nullptr, n_e, EP ? reinterpret_cast<const int32_t*>(tabs + dt.aret) : nullptr};
+    const Tables tdn{recs_active, off_sm, nullptr, n_e, EP ? reinterpret_cast<const int32_t*>(tabs + dt.aret) : nullptr,
+                     EP ? s_ep_epoch : 0u};
     int gu0, gu1, dn0, dn1, g10 = 0, g11 = 0;
     cta_units(n_e, p.gu.gpe, gu0, gu1);
     cta_units(n_e, p.dn.gpe, dn0, dn1);
@@ -576,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         if (lane != 0) return;
         int s = 0;
         if (stream_copy<2, P, true, true>(p.gu, tgu, rg, gu0, gu1, s, kDecodeLag)) {
-            if (D1 && p.dn1) down1_copy(p.dn, ids_sm, recs_sm, K, rg, g10, g11, s, kDecodeLag);
+            if (D1 && p.dn1) down1_copy(p.dn, ids_sm, recs_sm, K, rg, g10, g11, s, kDecodeDownLag);
             else stream_copy<1, P, true, true>(p.dn, tdn, rg, dn0, dn1, s, kDecodeLag);
         }
         return;
@@ -618,45 +654,53 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     if (s_fail) return;
 
     if constexpr (EP) {
-        // ---- 5 (expert parallel). the output rows are in their source ranks' mailboxes:
-        // a grid barrier, the return flags, and once every rank's are up, the combine ----
+        // ---- 5 (expert parallel). every output row of this rank's tokens arrives in
+        // its mailbox as (epoch, value) words, stored by the down phase of the expert's
+        // rank: the combine polls the words of its slots (bounded) and adds them in
+        // slot order as they are valid; no barrier, fence or flag between the ranks ----
         const EpMailbox mb = ep_mailbox(p.ep.ranks, p.ep.t_max, p.ep.k, p.ep.h, p.ep.xb);
         const unsigned ep_ep = s_ep_epoch;
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            bar_arrive(bars + 64);
-            if (!bar_wait(bars + 64, gridDim.x, p.r.err, ERR_GRID_WAIT)) s_fail = 1;
-            if (!s_fail && static_cast<int>(blockIdx.x) < G) {
-                __threadfence_system();
-                ep_st_relaxed_sys(reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(p.ep.peers[blockIdx.x]) +
-                                                              mb.flags_return) +
-                                      p.ep.rank,
-                                  ep_ep);
-            }
-            const unsigned* flags = reinterpret_cast<const unsigned*>(p.ep.mailbox + mb.flags_return);
-            for (int g = 0; g < G && !s_fail; g++) {
-                if (ep_ld_acquire_sys(flags + g) == ep_ep) continue;
-                const unsigned long long t0 = global_ns(), limit = wait_limit();
-                while (ep_ld_acquire_sys(flags + g) != ep_ep) {
-                    if (global_ns() - t0 > limit) {
-                        record_error(p.r.err, ERR_EP_RETURN_WAIT);
-                        s_fail = 1;
-                        break;
-                    }
-                }
-            }
-        }
-        consumers_sync();
-        if (s_fail) return;
-        const float* back = reinterpret_cast<const float*>(p.ep.mailbox + mb.back);
+        const unsigned long long* words = reinterpret_cast<const unsigned long long*>(p.ep.mailbox + mb.back_words);
         for (int o = blockIdx.x * (kWarps * 32) + threadIdx.x; o < T * H; o += gridDim.x * (kWarps * 32)) {
             const int t = o / H, c = o - t * H;
             float acc = 0.0f;
-            for (int s = 0; s < K; s++) {
-                const int e = ids_sm[t * K + s];
-                const int g = min(max(e / p.epr, 0), G - 1);
-                acc = fmaf(w_sm[t * K + s],
-                           __ldcg(back + (static_cast<int64_t>(g) * A + static_cast<int64_t>(t) * K + s) * H + c), acc);
+            for (int s0 = 0; s0 < K; s0 += 8) {
+                // slot s from expert rank g: word (g * T * K + t * K + s) * H + c
+                const unsigned long long* wp[8];
+                unsigned long long w[8];
+                unsigned pending = 0u;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int s = s0 + j;
+                    wp[j] = nullptr;
+                    w[j] = 0ull;
+                    if (s < K) {
+                        const int g = min(max(ids_sm[t * K + s] / p.epr, 0), G - 1);
+                        wp[j] = words + (static_cast<int64_t>(g) * A + static_cast<int64_t>(t) * K + s) * H + c;
+                        w[j] = ld_word_sys(wp[j]);
+                        if (static_cast<unsigned>(w[j] >> 32) != ep_ep) pending |= 1u << j;
+                    }
+                }
+                if (pending) {
+                    const unsigned long long t0 = global_ns(), limit = wait_limit();
+                    while (pending) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            if ((pending >> j) & 1u) {
+                                w[j] = ld_word_sys(wp[j]);
+                                if (static_cast<unsigned>(w[j] >> 32) == ep_ep) pending &= ~(1u << j);
+                            }
+                        if (!pending) break;
+                        __nanosleep(32);
+                        if (global_ns() - t0 > limit) {
+                            record_error(p.r.err, ERR_EP_RETURN_WAIT);
+                            return;  // this thread's outputs stay unwritten
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (s0 + j < K) acc = fmaf(w_sm[t * K + s0 + j], __uint_as_float(static_cast<unsigned>(w[j])), acc);
             }
             if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(acc);
             else static_cast<float*>(p.out)[o] = acc;

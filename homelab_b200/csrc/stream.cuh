@@ -5,9 +5,11 @@
 // of the reference's gemv_impl<T, true> (ops.cu:338-440) and moe_gate_up /
 // moe_down (moe.cu:52-151); only the summation order differs.
 //
-// One CTA per SM (two fit, so the next kernel of a dependent-launch chain can
-// start streaming while this one drains), persistent over a contiguous slice of
-// "units" (a unit is one row group: RPP rows of each part, all K columns).
+// Two CTAs fit per SM, and the stand-alone kernels launch two per SM, both
+// computing at once (measured faster than one per SM with the next kernel of a
+// dependent-launch chain streaming beside it).  Every CTA is persistent over
+// a contiguous slice of "units" (a unit is one row group: RPP rows of each part,
+// all K columns).
 // Warp roles:
 //   warp 8 (copy producer, one lane): streams each unit's rows (contiguous in
 //     row-major q) into a ring of shared-memory stages (up to 32 KB each, as
@@ -126,9 +128,10 @@ struct StreamParams {
     void* y;        // dense: [t, nrows] (y_bf16 ? bf16 : fp32); MoE: [A, nrows] fp32
     int y_bf16;
     unsigned* err;
-    // expert-parallel outputs (decode kernel): output row a goes to rank g's
-    // mailbox at ep_back_off, row (ep_rank * ep_tk + ts) of [*, nrows] fp32,
-    // where g * ep_tk + ts is the assignment's return index
+    // expert-parallel outputs (decode kernel): the output of assignment a, return
+    // index aret[a] = source rank g * ep_tk + slot, goes to rank g's mailbox at
+    // ep_back_off, word (ep_rank * ep_tk + slot) * nrows + row of [*, nrows]
+    // (epoch, value) words, stored over NVLink
     const unsigned long long* ep_peers;
     int64_t ep_back_off;
     int ep_rank, ep_tk;
@@ -251,6 +254,7 @@ struct Tables {
     const int32_t* assign_tok;
     int n_e;
     const int32_t* assign_ret;  // expert-parallel outputs: return index of each assignment
+    unsigned epoch;             // expert-parallel outputs: the step epoch stored with every value
 };
 
 template <bool TSMEM>
@@ -314,11 +318,12 @@ struct RingPos {
 // ---- per-pass reduction and output ----------------------------------------------------------
 
 // hdr[pi] = {a_begin, a_end, row0, nr} of the pass's units (shared memory).
-// EPOUT: MoE outputs go to the ranks whose assignments they are (aret: return
-// index of each assignment), else to p.y.
+// EPOUT: MoE outputs go to the mailboxes of the ranks whose assignments they
+// are (aret: return index of each assignment) as (epoch, value) words; else to p.y.
 template <int PARTS, int TB, int P, bool MOE, bool EPOUT = false>
 __device__ __forceinline__ void reduce_write(const StreamParams& p, const float (&acc)[P][kRows][TB], float* rb,
-                                             const int* hdr, int pn, int warp, int lane, const int32_t* aret = nullptr) {
+                                             const int* hdr, int pn, int warp, int lane, const int32_t* aret = nullptr,
+                                             unsigned epoch = 0u) {
     // The multi-value butterfly sums every partial over the 32 lanes by the same
     // tree (pairs at lane distance 16, then 8, 4, 2, 1; addition commutes), so
     // an output's arithmetic does not depend on its position in the pass: results
@@ -367,8 +372,9 @@ __device__ __forceinline__ void reduce_write(const StreamParams& p, const float 
             if (EPOUT) {
                 const int r = aret[a_begin + b];
                 const int g = r / p.ep_tk, ts = r - g * p.ep_tk;
-                float* dst = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peers[g]) + p.ep_back_off);
-                dst[(static_cast<int64_t>(p.ep_rank) * p.ep_tk + ts) * p.nrows + row] = val;
+                unsigned long long* dst = reinterpret_cast<unsigned long long*>(
+                    reinterpret_cast<uint8_t*>(p.ep_peers[g]) + p.ep_back_off);
+                st_word_sys(dst + (static_cast<int64_t>(p.ep_rank) * p.ep_tk + ts) * p.nrows + row, epoch, val);
             } else {
                 static_cast<float*>(p.y)[static_cast<int64_t>(a_begin + b) * p.nrows + row] = val;
             }
@@ -657,7 +663,7 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
                                 ch[3] = nr;
                             }
                             reduce_write<PARTS, TB, P, MOE, EPOUT>(p, acc, rg.red + rparity * kWarps * kRedV, ch, 1,
-                                                                   warp, lane, tb.assign_ret);
+                                                                   warp, lane, tb.assign_ret, tb.epoch);
                             rparity ^= 1;
 #pragma unroll
                             for (int j = 0; j < kRows; j++)
@@ -673,7 +679,7 @@ __device__ bool stream_consume(const StreamParams& p, const Tables& tb, const Ri
         }
         if (!chunked_any) {
             reduce_write<PARTS, TB, P, MOE, EPOUT>(p, acc, rg.red + rparity * kWarps * kRedV, hdr, pn, warp, lane,
-                                                   tb.assign_ret);
+                                                   tb.assign_ret, tb.epoch);
             rparity ^= 1;
         }
         // this warp is done with the pass's table: hand it back

@@ -10,6 +10,10 @@
 //   moe_gate_up_bf16   Experts::moe_gate_up_bf16 (src/experts.rs:95-140)
 //   moe_down_bf16      Experts::moe_down_bf16
 //   moe_combine_slots  Experts::moe_combine_slots (src/experts.rs:303-329)
+//   fp8_dequantize_blocks, f32_to_bf16, silu_mul_rows   the dense path above 16
+//                      tokens (Linear::gemm_fp8, src/linear.rs:35-81, 140-205) and the
+//                      SwiGLU between its two GEMMs (src/elementwise.rs:56-70); one
+//                      thread per element, grid(n, 256)
 // The modules (ops.cubin, moe.cubin) are built from the reference sources by
 // oracle/ref/Makefile; libcuda is opened at run time so this library loads on
 // machines without a GPU.
@@ -42,7 +46,7 @@ struct Driver {
 
 Driver g_drv;
 bool g_open = false;
-CUfunction g_gemv[4], g_router, g_gate_up_bf16, g_down_bf16, g_combine;
+CUfunction g_gemv[4], g_router, g_gate_up_bf16, g_down_bf16, g_combine, g_dequant, g_to_bf16, g_silu_rows;
 
 template <class F>
 bool sym(void* h, const char* name, F& f) {
@@ -96,6 +100,9 @@ int orl_open(const char* dir) {
     if (g_drv.module_get_function(&g_gate_up_bf16, moe, "moe_gate_up_bf16") != 0) return -3;
     if (g_drv.module_get_function(&g_down_bf16, moe, "moe_down_bf16") != 0) return -3;
     if (g_drv.module_get_function(&g_combine, moe, "moe_combine_slots") != 0) return -3;
+    if (g_drv.module_get_function(&g_dequant, ops, "fp8_dequantize_blocks") != 0) return -3;
+    if (g_drv.module_get_function(&g_to_bf16, ops, "f32_to_bf16") != 0) return -3;
+    if (g_drv.module_get_function(&g_silu_rows, ops, "silu_mul_rows") != 0) return -3;
     g_open = true;
     return 0;
 }
@@ -158,6 +165,38 @@ int orl_moe_combine_slots(const float* y, const int* slot_assign, const float* w
     unsigned blocks = static_cast<unsigned>((total + 255) / 256);
     void* args[] = {&y, &slot_assign, &w, &out, &t, &hidden, &k};
     return g_drv.launch(g_combine, blocks, 1, 1, 256, 1, 1, 0, stream, args, nullptr) == 0 ? 0 : -3;
+}
+
+// W[n, k] bf16 = e4m3 q[n, k] * scale[n, ceil(k/128)] (1x128 blocks).
+int orl_dequant_fp8(const uint8_t* q, const float* scale, void* w, int n, int k, void* stream) {
+    if (!g_open || n < 1 || k < 1) return -5;
+    const long long total = static_cast<long long>(n) * k;
+    if ((total + 255) / 256 > 0x7fffffffLL) return -5;
+    const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+    void* args[] = {&q, &scale, &w, &n, &k};
+    return g_drv.launch(g_dequant, blocks, 1, 1, 256, 1, 1, 0, stream, args, nullptr) == 0 ? 0 : -3;
+}
+
+// y[i] = bf16(x[i]), i < n.
+int orl_f32_to_bf16(const float* x, void* y, int n, void* stream) {
+    if (!g_open || n < 1) return -5;
+    void* args[] = {&x, &y, &n};
+    return g_drv.launch(g_to_bf16, static_cast<unsigned>((n + 255) / 256), 1, 1, 256, 1, 1, 0, stream, args,
+                        nullptr) == 0
+               ? 0
+               : -3;
+}
+
+// y[r, i] = silu(gu[r, i]) * gu[r, n + i], gu [rows, 2n] fp32.
+int orl_silu_mul_rows(const float* gu, float* y, int rows, int n, void* stream) {
+    if (!g_open || rows < 1 || n < 1) return -5;
+    const long long total = static_cast<long long>(rows) * n;
+    if (total > 0x7fffffffLL) return -5;
+    void* args[] = {&gu, &y, &rows, &n};
+    return g_drv.launch(g_silu_rows, static_cast<unsigned>((total + 255) / 256), 1, 1, 256, 1, 1, 0, stream, args,
+                        nullptr) == 0
+               ? 0
+               : -3;
 }
 
 }  // extern "C"

@@ -41,6 +41,9 @@ class RefKernels:
         L.orl_moe_gate_up_bf16.argtypes = [P, P, P, I, P, P, I, I, LL, LL, P]
         L.orl_moe_down_bf16.argtypes = [P, P, I, P, P, I, I, LL, P]
         L.orl_moe_combine_slots.argtypes = [P, P, P, P, I, I, I, P]
+        L.orl_dequant_fp8.argtypes = [P, P, P, I, I, P]
+        L.orl_f32_to_bf16.argtypes = [P, P, I, P]
+        L.orl_silu_mul_rows.argtypes = [P, P, I, I, P]
         rc = L.orl_open(REF_DIR.encode())
         if rc != 0:
             raise RuntimeError(f"loading the reference kernels failed ({rc})")
@@ -88,3 +91,13 @@ class RefKernels:
     def moe_combine_slots(self, y, slot_assign, w, out, t, hidden, k):
         self._check(self.L.orl_moe_combine_slots(y.data_ptr(), slot_assign.data_ptr(), w.data_ptr(), out.data_ptr(),
                                                  t, hidden, k, self._s()), "moe_combine_slots")
+
+    def dequant_fp8(self, q: torch.Tensor, scale: torch.Tensor, w: torch.Tensor, n: int, k: int):
+        """w[n, k] bf16 = e4m3 q * scale (1x128 blocks), the reference's fp8_dequantize_blocks."""
+        self._check(self.L.orl_dequant_fp8(q.data_ptr(), scale.data_ptr(), w.data_ptr(), n, k, self._s()), "dequant")
+
+    def f32_to_bf16(self, x: torch.Tensor, y: torch.Tensor, n: int):
+        self._check(self.L.orl_f32_to_bf16(x.data_ptr(), y.data_ptr(), n, self._s()), "f32_to_bf16")
+
+    def silu_mul_rows(self, gu: torch.Tensor, y: torch.Tensor, rows: int, n: int):
+        self._check(self.L.orl_silu_mul_rows(gu.data_ptr(), y.data_ptr(), rows, n, self._s()), "silu_mul_rows")
