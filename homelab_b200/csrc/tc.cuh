@@ -535,19 +535,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     constexpr unsigned PER_CTA = SP::SPLIT ? 2u : 1u;  // arrivals per CTA and lane quarter
                     if (prev == PER_CTA * static_cast<unsigned>(c_last - c_first + 1) - 1u) {
                         __threadfence();
-                        for (int tt = 0; tt < T; tt += 8) {
-                            float sum[8];
+                        // sums in CTA order; 16 tokens of up to 4 CTAs are loaded at once, so a
+                        // row block costs ceil(T / 16) * ceil(CTAs / 4) L2 round trips
+                        for (int tt = 0; tt < T; tt += 16) {
+                            float sum[16];
 #pragma unroll
-                            for (int u = 0; u < 8; u++) sum[u] = 0.0f;
-                            for (int c = c_first; c <= c_last; c++) {
-                                const int sd = tc_lo(p.tiles, c, grid) / p.kblocks == rb ? 0 : 1;
-                                const float* q = p.partial + (static_cast<int64_t>(c) * 2 + sd) * T * kTcTile + r;
+                            for (int u = 0; u < 16; u++) sum[u] = 0.0f;
+                            for (int c0 = c_first; c0 <= c_last; c0 += 4) {
+                                float v[4][16];
 #pragma unroll
-                                for (int u = 0; u < 8; u++)
-                                    if (tt + u < T) sum[u] += __ldcg(q + (tt + u) * kTcTile);
+                                for (int cc = 0; cc < 4; cc++) {
+                                    const int c = c0 + cc;
+                                    const bool have = c <= c_last;
+                                    const int sd = have && tc_lo(p.tiles, c, grid) / p.kblocks == rb ? 0 : 1;
+                                    const float* q =
+                                        p.partial + (static_cast<int64_t>(have ? c : c0) * 2 + sd) * T * kTcTile + r;
+#pragma unroll
+                                    for (int u = 0; u < 16; u++)
+                                        v[cc][u] = have && tt + u < T ? __ldcg(q + (tt + u) * kTcTile) : 0.0f;
+                                }
+#pragma unroll
+                                for (int cc = 0; cc < 4; cc++)
+                                    if (c0 + cc <= c_last)
+#pragma unroll
+                                        for (int u = 0; u < 16; u++) sum[u] += v[cc][u];
                             }
 #pragma unroll
-                            for (int u = 0; u < 8; u++) {
+                            for (int u = 0; u < 16; u++) {
                                 if (tt + u < T) {
                                     const int64_t yi = static_cast<int64_t>(tt + u) * p.nrows + rb * kTcTile + r;
                                     if (p.y_bf16) static_cast<__nv_bfloat16*>(p.y)[yi] = __float2bfloat16_rn(sum[u]);

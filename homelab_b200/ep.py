@@ -337,9 +337,9 @@ class EpPeerMoeLayer:
 class EpDecodeLayer:
     """The expert-parallel decode step in one launch per rank
     (oomb_moe_decode_ep_fp8): route, dispatch into the mailboxes, the local
-    experts with each output row kept in this rank's mailbox, and the
-    slot-order combine reading each slot's row from its expert's rank over
-    NVLink, for up to 16 tokens per rank and 256 experts.  Every
+    experts with each output value stored into its source rank's mailbox as an
+    (epoch, value) word, and the slot-order combine polling those words, for up
+    to 16 tokens per rank and 256 experts.  Every
     rank runs each step with the same t; the kernels of the ranks wait on one
     another (bounded waits), so each rank's runs on its own GPU."""
 

@@ -432,10 +432,11 @@ typedef struct oomb_ep_peer {
  * and 256 experts) with expert parallelism: layer->recs holds this rank's
  * experts [rank * E/ranks, (rank + 1) * E/ranks), layer->router_w the whole
  * router.  Route, dispatch to the mailboxes, grouping of the received slots,
- * gate/up and down over the local experts with each output row kept in this
- * rank's mailbox, and the slot-order combine reading every slot's row from its
- * expert's rank over NVLink, in one kernel per rank; every rank runs the step
- * with the same t.  Bit-identical to one GPU. */
+ * gate/up and down over the local experts (every received slot a group of its
+ * own) with each output value stored into its source rank's mailbox as an
+ * (epoch, value) 64-bit word, and the slot-order combine polling those words,
+ * in one kernel per rank; every rank runs the step with the same t.
+ * Bit-identical to one GPU. */
 size_t oomb_moe_decode_ep_workspace_bytes(int t, int ranks, const oomb_moe_layer* layer);
 int oomb_moe_decode_ep_fp8(const oomb_moe_layer* layer, const oomb_ep_peer* peer, const void* x, int x_dtype, int t,
                            void* out, int out_dtype, int32_t* ids, float* weights, void* workspace,
