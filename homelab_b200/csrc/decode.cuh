@@ -419,10 +419,13 @@ __device__ bool down1_consume(const DecodeParams& p, const int32_t* ids_sm, cons
 // token slots and units per pass of both streaming phases (as the stand-alone
 // kernels would take them for at most T assignments per expert).  EP: expert
 // parallelism, this rank holding experts [rank * epr, (rank + 1) * epr):
-//   after top-k, CTA g < ranks dispatches this rank's meta and activations into
-//   rank g's mailbox and raises the flag there; every CTA waits for all
-//   sources' flags and groups the received slots (local expert ids, -1 for
-//   another rank's) in (source, token, slot) order; the streaming phases run
+//   after top-k, CTA g < ranks stores this rank's meta and activations into
+//   rank g's mailbox as (epoch, payload) words, then unpacks source g's
+//   activation words into the plain layout and counts it in (GPU scope); every
+//   CTA polls all sources' meta words and groups the received slots (local
+//   expert ids, -1 for another rank's; every slot a group of its own) in
+//   (source, token, slot) order, and its consumers wait for the activations of
+//   every source before gate/up; the streaming phases run
 //   over the local experts, down's reduction storing each output value into its
 //   source rank's mailbox as an (epoch, value) word over NVLink; the combine of
 //   each rank polls the words of its tokens' slots (bounded) and adds them in
@@ -553,31 +556,65 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
             const unsigned ep_ep = s_ep_epoch;
             // every CTA read the mailbox epoch before the logits barrier: hand it to the next step
             if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<unsigned*>(p.ep.mailbox + mb.counter) = ep_ep;
+            const unsigned long long* meta_w =
+                reinterpret_cast<const unsigned long long*>(p.ep.mailbox + mb.meta_words);
+            const int xw_n = T * H * p.ep.xb / 4;  // 4-byte words of one rank's activations
             if (static_cast<int>(blockIdx.x) < G) {
-                // dispatch to rank g: meta (local expert ids on g, -1 elsewhere) and activations
+                // dispatch to rank g as (epoch, payload) words: the meta (local expert
+                // ids on g, -1 elsewhere), then the activations, 4 bytes a word; no
+                // fence or flag (a word that shows this step's epoch holds its payload)
                 const int g = blockIdx.x;
                 uint8_t* dst = reinterpret_cast<uint8_t*>(p.ep.peers[g]);
-                int32_t* meta = reinterpret_cast<int32_t*>(dst + mb.meta) + static_cast<size_t>(p.ep.rank) * A;
+                unsigned long long* mw =
+                    reinterpret_cast<unsigned long long*>(dst + mb.meta_words) + static_cast<size_t>(p.ep.rank) * A;
                 for (int i = threadIdx.x; i < A; i += kThreads) {
                     const int e = ids_sm[i];
-                    meta[i] = e / p.epr == g ? e - g * p.epr : -1;
+                    st_word32_sys(mw + i, ep_ep, static_cast<unsigned>(e / p.epr == g ? e - g * p.epr : -1));
                 }
-                ep_copy16(dst + mb.x + static_cast<size_t>(p.ep.rank) * T * H * p.ep.xb,
-                          static_cast<const uint8_t*>(p.r.x), static_cast<size_t>(T) * H * p.ep.xb);
+                unsigned long long* xw =
+                    reinterpret_cast<unsigned long long*>(dst + mb.x_words) + static_cast<size_t>(p.ep.rank) * xw_n;
+                const unsigned* xs = static_cast<const unsigned*>(p.r.x);
+                for (int i = threadIdx.x; i < xw_n; i += kThreads) st_word32_sys(xw + i, ep_ep, __ldcg(xs + i));
+                // and receive source g's activations: unpack its words into the plain
+                // layout the gate/up phase reads, then count this source in (GPU scope)
+                const unsigned long long* xr =
+                    reinterpret_cast<const unsigned long long*>(p.ep.mailbox + mb.x_words) + static_cast<size_t>(g) * xw_n;
+                unsigned* xo = reinterpret_cast<unsigned*>(p.ep.mailbox + mb.x) + static_cast<size_t>(g) * xw_n;
+                for (int i = threadIdx.x; i < xw_n && !s_fail; i += kThreads) {
+                    unsigned long long w = ld_word_sys(xr + i);
+                    if (static_cast<unsigned>(w >> 32) != ep_ep) {
+                        const unsigned long long t0 = global_ns(), limit = wait_limit();
+                        while (static_cast<unsigned>((w = ld_word_sys(xr + i)) >> 32) != ep_ep) {
+                            if (global_ns() - t0 > limit) {
+                                record_error(p.r.err, ERR_EP_DISPATCH_WAIT);
+                                s_fail = 1;
+                                break;
+                            }
+                        }
+                    }
+                    xo[i] = static_cast<unsigned>(w);
+                }
                 __syncthreads();
-                if (threadIdx.x == 0) {
-                    ep_fence_release_sys();
-                    ep_st_relaxed_sys(reinterpret_cast<unsigned*>(dst + mb.flags_dispatch) + p.ep.rank, ep_ep);
-                }
+                if (threadIdx.x == 0 && !s_fail) bar_arrive(bars + 64);
             }
-            // every source rank's slots for this rank's experts
-            if (!ep_wait_flags(reinterpret_cast<const unsigned*>(p.ep.mailbox + mb.flags_dispatch), G, ep_ep, p.r.err,
-                               ERR_EP_DISPATCH_WAIT))
-                return;
+            // every source rank's slots for this rank's experts, from their meta words
             int32_t* rmeta = reinterpret_cast<int32_t*>(tabs + dt.rmeta);
-            for (int i = threadIdx.x; i < G * A; i += kThreads)
-                rmeta[i] = __ldcg(reinterpret_cast<const int32_t*>(p.ep.mailbox + mb.meta) + i);
+            for (int i = threadIdx.x; i < G * A && !s_fail; i += kThreads) {
+                unsigned long long w = ld_word_sys(meta_w + i);
+                if (static_cast<unsigned>(w >> 32) != ep_ep) {
+                    const unsigned long long t0 = global_ns(), limit = wait_limit();
+                    while (static_cast<unsigned>((w = ld_word_sys(meta_w + i)) >> 32) != ep_ep) {
+                        if (global_ns() - t0 > limit) {
+                            record_error(p.r.err, ERR_EP_DISPATCH_WAIT);
+                            s_fail = 1;
+                            break;
+                        }
+                    }
+                }
+                rmeta[i] = static_cast<int32_t>(static_cast<unsigned>(w));
+            }
             __syncthreads();
+            if (s_fail) return;
             RouteParams rq = p.r;
             rq.T = G * T;
             rq.E = p.epr;
@@ -625,6 +662,12 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
     }
 
     RingPos pos{0, 0, 0};
+    if constexpr (EP) {
+        // the activations of every source rank are unpacked (CTAs 0 .. ranks - 1)
+        if (threadIdx.x == 0 && !bar_wait(bars + 64, static_cast<unsigned>(G), p.r.err, ERR_GRID_WAIT)) s_fail = 1;
+        consumers_sync();
+        if (s_fail) return;
+    }
     if (!stream_consume<2, TB, P, XBF16, true, BLK, true>(p.gu, tgu, rg, gu0, gu1, pos)) s_fail = 1;
     consumers_sync();  // the CTA's h rows are written
     if (threadIdx.x == 0 && !s_fail) {

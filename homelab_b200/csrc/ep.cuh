@@ -189,7 +189,7 @@ __global__ void ep_combine_kernel(const float* back, const int32_t* ids, const f
 // reading its step-n inputs.
 
 struct EpMailbox {
-    size_t counter, tickets, flags_dispatch, flags_return, meta, x, back, back_words, total;
+    size_t counter, tickets, flags_dispatch, flags_return, meta, x, back, back_words, meta_words, x_words, total;
 };
 
 // Layout for `ranks` ranks of up to t_max tokens, top-k slots, hidden h,
@@ -207,6 +207,9 @@ __host__ __device__ inline EpMailbox ep_mailbox(int ranks, int t_max, int k, int
     m.back = o; o = up(o + static_cast<size_t>(ranks) * t_max * k * static_cast<size_t>(h) * 4);
     // the one-launch step's returned rows: (epoch, value) words, [ranks][t * k][h]
     m.back_words = o; o = up(o + static_cast<size_t>(ranks) * t_max * k * static_cast<size_t>(h) * 8);
+    // the one-launch step's dispatch: (epoch, meta) and (epoch, 4 bytes of x) words
+    m.meta_words = o; o = up(o + static_cast<size_t>(ranks) * t_max * k * 8);
+    m.x_words = o; o = up(o + static_cast<size_t>(ranks) * t_max * static_cast<size_t>(h) * xb * 2);
     m.total = o;
     return m;
 }
