@@ -357,7 +357,9 @@ def run_ours(args, rank, world, local_rank):
     reps, rem = divmod(K, G)
     s = torch.cuda.Stream(dev)
 
-    host_io = world == 1  # the single-GPU entry point reads and writes pinned host buffers itself
+    # the decode entry points (single GPU, and the one-launch expert-parallel step) read and write
+    # pinned host buffers themselves
+    host_io = world == 1 or (args.ep_transport == "peer" and args.ep_step == "fused" and B <= 16)
 
     def capture(n, e2e=False, xh=None, oh=None, xdev=None):
         g = torch.cuda.CUDAGraph()
@@ -486,6 +488,10 @@ def run_ours(args, rank, world, local_rank):
     attn4 = measure_attention_config4(gpu, dev, s, peak=peak) if extras else None
     layers4 = measure_layers_config4(gpu, dev, s, peak=peak) if extras else None
     offload5 = measure_offload_config5(gpu, dev, s) if extras else None
+    fp8_peak = measure_fp8_peak(dev, s) if extras else None
+    if fp8_peak and "tflops" in fp8_peak and experts5:
+        for v in experts5.values():
+            v["tcgen05_grouped"]["frac_of_fp8_peak"] = v["tcgen05_grouped"]["tflops"] / fp8_peak["tflops"]
 
     ep5 = None
     if world > 1 and not args.quick:
@@ -518,6 +524,7 @@ def run_ours(args, rank, world, local_rank):
             "attention_config4": attn4,
             "decode_layers_config4": layers4,
             "offload_overlap_config5": offload5,
+            "fp8_tensor_peak": fp8_peak,
             "ep_config5": ep5,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
@@ -839,6 +846,32 @@ def measure_gemv_config1(gpu, dev, s, copies=16, launches=320):
     nbytes = n * k + (n // 128) * (k // 128) * 4 + k * 2 + n * 2
     us = best * 1e3
     return {"gbs": nbytes / (us * 1e-6) / 1e9, "bytes": nbytes, "us": us}
+
+
+def measure_fp8_peak(dev, s, n=8192, launches=20):
+    """The dense FP8 tensor-core peak of this GPU as a library reaches it: cuBLASLt's
+    e4m3 x e4m3 GEMM (torch._scaled_mm, unit scales, bf16 out) at n^3, the
+    denominator for the tensor-core kernels' TFLOP/s (MEASURED_PEAKS holds bf16
+    only).  None if the library call is unavailable."""
+    import torch
+    try:
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(17)
+        a = torch.randn((n, n), generator=gen, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn((n, n), generator=gen, device=dev).to(torch.float8_e4m3fn).t()  # column-major
+        one = torch.ones((), dtype=torch.float32, device=dev)
+        out = torch.empty((n, n), dtype=torch.bfloat16, device=dev)
+
+        def mm(i):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16, out=out)
+
+        mm(0)
+        torch.cuda.synchronize()
+        us = _graph_time(s, mm, launches)
+        return {"tflops": 2.0 * n ** 3 / (us * 1e-6) / 1e12, "us": us,
+                "how": f"torch._scaled_mm (cuBLASLt) e4m3 x e4m3, {n}^3, unit scales, bf16 out"}
+    except Exception as e:  # a measurement aid only
+        return {"error": str(e)[:200]}
 
 
 def _graph_time(s, fn, launches, reps=3):

@@ -1502,6 +1502,27 @@ int oomb_moe_decode_ep_fp8(const oomb_moe_layer* L, const oomb_ep_peer* q, const
     const DeviceState* d = device_state();
     if (!d) return OOMB_E_DEVICE;
     ep.err = d->err;
+    // x and out may be pinned host memory (as for oomb_moe_decode_fp8)
+    const void* xv = nullptr;
+    const void* ov = nullptr;
+    const void* unused = nullptr;
+    const Mem xk = mem_kind(x, &xv), okind = mem_kind(out, &ov);
+    if (xk == Mem::none || okind == Mem::none || mem_kind(workspace, &unused) != Mem::device ||
+        (ids && mem_kind(ids, &unused) != Mem::device) || (weights && mem_kind(weights, &unused) != Mem::device))
+        return OOMB_E_ARG;
+    out = const_cast<void*>(ov);
+    if (xk == Mem::host) {
+        // staged into the y region (unused by the expert-parallel step) once the previous kernel has completed
+        const int64_t n16 = static_cast<int64_t>(t) * L->hidden * (x_dtype == OOMB_BF16 ? 2 : 4) / 16;
+        const int64_t blocks = (n16 + 255) / 256;
+        const int rs = launch(stage_host_kernel, dim3(static_cast<unsigned>(blocks < d->sms ? blocks : d->sms)),
+                              dim3(256), 0, stream, reinterpret_cast<uint4*>(static_cast<uint8_t*>(workspace) + lay.y),
+                              static_cast<const uint4*>(xv), n16);
+        if (rs) return rs;
+        x = static_cast<uint8_t*>(workspace) + lay.y;
+    } else {
+        x = xv;
+    }
     FusedDecode f;
     if (!fused_decode_plan(d, L, t, x_dtype == OOMB_BF16, f, q->ranks)) return OOMB_E_SHAPE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);

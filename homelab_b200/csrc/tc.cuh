@@ -311,11 +311,40 @@ __device__ __forceinline__ void tc_fold(uint32_t taddr, const float* sx, int t0,
     const int base = t0 * TS;
     const int ncol = (nt * TS + 7) & ~7;
     const float* sxb = sx + base;
+    constexpr int NC = NT * TS;
+    constexpr int LG = NC % 32 == 0 ? 32 : 8;  // columns a tensor-memory load brings
+    if constexpr (NC % 8 == 0 && TS % 2 == 0) {
+        if (nt == NT) {
+            // every column present: all tensor-memory loads in flight before one
+            // wait, and each token's term pairs multiplied two at a time (each
+            // product rounded as alone, so the same sums as one at a time)
+            float d[NC / LG][LG];
+#pragma unroll
+            for (int g = 0; g < NC / LG; g++) {
+                if constexpr (LG == 32) tc_ld32(taddr + static_cast<uint32_t>(base + LG * g), d[g]);
+                else tc_ld8(taddr + static_cast<uint32_t>(base + LG * g), d[g]);
+            }
+            tc_wait_ld();
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                float u = 0.0f;
+#pragma unroll
+                for (int q = 0; q < TS; q += 2) {
+                    const int c = t * TS + q;  // even: the pair (c, c + 1) shares token t and a load group
+                    const float2 sp = *reinterpret_cast<const float2*>(sxb + c);
+                    const float2 pr = fmul2(sp, make_float2(d[c / LG][c % LG], d[c / LG][c % LG + 1]));
+                    u = q == 0 ? __fadd_rn(pr.x, pr.y) : __fadd_rn(__fadd_rn(u, pr.x), pr.y);
+                }
+                acc[t] = fmaf(ws, u, acc[t]);
+            }
+            return;
+        }
+    }
     float u = 0.0f;
     auto fold = [&](int c, float d) {
         const int t = c / TS, term = c - (c / TS) * TS;
         if (t < NT) {
-            const float v = sxb[c] * d;
+            const float v = __fmul_rn(sxb[c], d);
             u = term == 0 ? v : __fadd_rn(u, v);
             if (term == TS - 1) acc[t] = fmaf(ws, u, acc[t]);
         }

@@ -364,7 +364,7 @@ class EpDecodeLayer:
         """out[t, hidden] = the routed experts' combined output for this rank's t tokens."""
         xd = BF16 if x.dtype == torch.bfloat16 else F32
         od = BF16 if out.dtype == torch.bfloat16 else F32
-        s = torch.cuda.current_stream(x.device).cuda_stream
+        s = torch.cuda.current_stream(self.ws.device).cuda_stream  # x and out may be pinned host tensors
         check(self.L.oomb_moe_decode_ep_fp8(C.byref(self.layer), C.byref(self.q), x.data_ptr(), xd, t, out.data_ptr(),
                                             od, self.ids.data_ptr(), self.weights.data_ptr(), self.ws.data_ptr(),
                                             self.ws.numel(), s), "moe_decode_ep")

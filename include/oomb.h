@@ -435,8 +435,9 @@ typedef struct oomb_ep_peer {
  * gate/up and down over the local experts (every received slot a group of its
  * own) with each output value stored into its source rank's mailbox as an
  * (epoch, value) 64-bit word, and the slot-order combine polling those words,
- * in one kernel per rank; every rank runs the step with the same t.
- * Bit-identical to one GPU. */
+ * in one kernel per rank; every rank runs the step with the same t.  x and out
+ * may be pinned host memory, as for oomb_moe_decode_fp8.  Bit-identical to one
+ * GPU. */
 size_t oomb_moe_decode_ep_workspace_bytes(int t, int ranks, const oomb_moe_layer* layer);
 int oomb_moe_decode_ep_fp8(const oomb_moe_layer* layer, const oomb_ep_peer* peer, const void* x, int x_dtype, int t,
                            void* out, int out_dtype, int32_t* ids, float* weights, void* workspace,

@@ -178,3 +178,23 @@ def test_one_launch_expert_parallel_single_rank_equals_single_gpu(layer):
             torch.cuda.synchronize()
             assert torch.equal(out, want), f"t={t} step {step}"
         mb.close()
+
+
+def test_one_launch_expert_parallel_takes_pinned_host_buffers(layer):
+    """x and out in pinned host memory: the step stages x itself and stores out
+    straight to the host, with the same bits as on device buffers."""
+    from homelab_b200.ep import EpDecodeLayer, EpPeerMailboxes
+    bank, router = layer["bank"], layer["router"]
+    t = 2
+    mb = EpPeerMailboxes(None, H, K, t, torch.bfloat16, DEV, ranks=1)
+    ep = EpDecodeLayer(mb, 0, H, E, K, router, bank.addrs, bank.geo, t)
+    for step in range(3):
+        x = torch.from_numpy(O.normal_bf16(700 + step, t * H).view(np.int16)).to(DEV).view(torch.bfloat16).view(t, H)
+        want = torch.full((t, H), float("nan"), dtype=torch.float32, device=DEV)
+        ep.forward(x, t, want)
+        xh = x.cpu().pin_memory()
+        oh = torch.full((t, H), float("nan"), dtype=torch.float32).pin_memory()
+        ep.forward(xh, t, oh)
+        torch.cuda.synchronize()
+        assert torch.equal(oh, want.cpu()), f"step {step}"
+    mb.close()
