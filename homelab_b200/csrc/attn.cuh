@@ -35,7 +35,7 @@ namespace oomb {
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
-constexpr int kAttnMaxSplits = 32;  // CTAs per (sequence, kv head): the last one merges at most this many
+constexpr int kAttnMaxSplits = 32;  // CTAs per (sequence, kv head): the last one merges at most this many (64 measured slower at batch 1: 17.5 -> 24.0 us)
 
 enum : unsigned {
     ERR_ATTN_LEN = 0x800,  // a kv_len entry was outside [0, kv_max] (clamped)
@@ -67,14 +67,14 @@ __device__ __forceinline__ void bf16x4_to_f32(uint2 w, float (&f)[4]) {
 }
 
 template <int G, int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, G <= 4 ? 4 : 3) attn_decode_kernel(const AttnParams p) {
     static_assert(D == 128, "lanes own four elements of a row");
     static_assert(G >= 1 && G <= 32 && (32 % G) == 0, "G must divide 32");
     constexpr int E = D / 32;
     constexpr int CP = 32 / G < 8 ? 32 / G : 8;  // positions per chunk: CP * G <= 32 scores, one per lane
     constexpr int PS = D + 4;                      // floats per partial row: acc[D], m, l, padding
-    __shared__ float ebuf[kAttnWarps][32];
-    __shared__ float cbuf[kAttnWarps][32];
+    __shared__ float2 ebuf[kAttnWarps][32];
+    __shared__ float2 cbuf[kAttnWarps][32];
     __shared__ bool last;
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -90,29 +90,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     const int j0 = static_cast<int>(static_cast<int64_t>(L) * wi / W);
     const int j1 = static_cast<int>(static_cast<int64_t>(L) * (wi + 1) / W);
 
-    // this lane's elements of the G query heads, scaled
-    float qv[G][E];
+    // this lane's elements of the G query heads, scaled, as pairs (elements 0,1 and 2,3)
+    float2 qp[G][2];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         const int64_t qi = (static_cast<int64_t>(b) * p.H + kvh * G + g) * D + lane * E;
+        float f[4];
         if (p.q_bf16) {
-            float f[4];
             bf16x4_to_f32(__ldcg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.q) + qi)), f);
-#pragma unroll
-            for (int e = 0; e < E; e++) qv[g][e] = f[e] * p.scale;
         } else {
-            const float4 f = __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + qi));
-            qv[g][0] = f.x * p.scale;
-            qv[g][1] = f.y * p.scale;
-            qv[g][2] = f.z * p.scale;
-            qv[g][3] = f.w * p.scale;
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + qi));
+            f[0] = v.x;
+            f[1] = v.y;
+            f[2] = v.z;
+            f[3] = v.w;
         }
+        qp[g][0] = make_float2(f[0] * p.scale, f[1] * p.scale);
+        qp[g][1] = make_float2(f[2] * p.scale, f[3] * p.scale);
     }
-    float acc[G][E];
+    // unnormalised accumulators of the lane's four elements, per head, as pairs
+    float2 acc[G][2];
 #pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-        for (int e = 0; e < E; e++) acc[g][e] = 0.0f;
+    for (int g = 0; g < G; g++) acc[g][0] = acc[g][1] = make_float2(0.0f, 0.0f);
     // running max and sum of the lane's head (lane % G); the same in every lane of that head
     float m_run = -INFINITY, l_run = 0.0f;
     const int64_t row_stride = static_cast<int64_t>(p.Hkv) * D;
@@ -132,20 +131,19 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
 #pragma unroll
         for (int c = 0; c < CP; c++)
             vr[c] = c < n ? __ldcs(reinterpret_cast<const uint2*>(vb + (j + c) * row_stride)) : make_uint2(0u, 0u);
-        // partial scores: value c * G + g = this lane's share of q_g . k_c
+        // partial scores: value c * G + g = this lane's share of q_g . k_c (two
+        // element pairs at once, then the pair's halves added)
         float s[32];
 #pragma unroll
         for (int i = CP * G; i < 32; i++) s[i] = 0.0f;
 #pragma unroll
         for (int c = 0; c < CP; c++) {
-            float kf[4];
-            bf16x4_to_f32(kr[c], kf);
+            const float2 k01 = make_float2(__uint_as_float(kr[c].x << 16), __uint_as_float(kr[c].x & 0xffff0000u));
+            const float2 k23 = make_float2(__uint_as_float(kr[c].y << 16), __uint_as_float(kr[c].y & 0xffff0000u));
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                float d = qv[g][0] * kf[0];
-#pragma unroll
-                for (int e = 1; e < E; e++) d = fmaf(qv[g][e], kf[e], d);
-                s[c * G + g] = d;
+                const float2 d2 = ffma2(qp[g][1], k23, fmul2(qp[g][0], k01));
+                s[c * G + g] = __fadd_rn(d2.x, d2.y);
             }
         }
         if (j + CP < j1) load_k(j + CP);  // the next chunk's keys load under this chunk's math
@@ -163,24 +161,24 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         for (int o = G; o < 32; o <<= 1) esum += __shfl_xor_sync(0xffffffffu, esum, o);
         l_run = fmaf(l_run, corr, esum);
         m_run = m_new;
-        ebuf[warp][lane] = e;
-        cbuf[warp][lane] = corr;
+        ebuf[warp][lane] = make_float2(e, e);  // as pairs: one load gives both lanes of a packed FMA
+        cbuf[warp][lane] = make_float2(corr, corr);
         __syncwarp();
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            const float cg = cbuf[warp][g];
-#pragma unroll
-            for (int e2 = 0; e2 < E; e2++) acc[g][e2] *= cg;
+            const float2 cg = cbuf[warp][g];
+            acc[g][0] = fmul2(acc[g][0], cg);
+            acc[g][1] = fmul2(acc[g][1], cg);
         }
 #pragma unroll
         for (int c = 0; c < CP; c++) {
-            float vf[4];
-            bf16x4_to_f32(vr[c], vf);
+            const float2 v01 = make_float2(__uint_as_float(vr[c].x << 16), __uint_as_float(vr[c].x & 0xffff0000u));
+            const float2 v23 = make_float2(__uint_as_float(vr[c].y << 16), __uint_as_float(vr[c].y & 0xffff0000u));
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                const float w = ebuf[warp][c * G + g];
-#pragma unroll
-                for (int e2 = 0; e2 < E; e2++) acc[g][e2] = fmaf(w, vf[e2], acc[g][e2]);
+                const float2 w = ebuf[warp][c * G + g];
+                acc[g][0] = ffma2(w, v01, acc[g][0]);
+                acc[g][1] = ffma2(w, v23, acc[g][1]);
             }
         }
         __syncwarp();
@@ -195,7 +193,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     }
 #pragma unroll
     for (int g = 0; g < G; g++)
-        *reinterpret_cast<float4*>(&wacc[warp][g][lane * E]) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+        *reinterpret_cast<float4*>(&wacc[warp][g][lane * E]) =
+            make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
     __syncthreads();
     const int64_t pbase = (static_cast<int64_t>(b) * p.Hkv + kvh) * p.splits;
     float* mine = p.part + (pbase + split) * G * PS;

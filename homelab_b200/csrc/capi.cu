@@ -989,8 +989,12 @@ bool attn_plan(const DeviceState* d, int batch, int heads, int kv_heads, int hea
     if (G != 1 && G != 2 && G != 4 && G != 8) return false;
     const int64_t pairs = static_cast<int64_t>(batch) * kv_heads;
     if (pairs > 65535LL * 65535LL) return false;
-    // about four CTAs of four warps per SM, each warp at least one chunk of positions
-    const int64_t want = (static_cast<int64_t>(d->sms) * 4 + pairs - 1) / pairs;
+    // as many CTAs as are resident at once (four per SM by registers, three at
+    // G = 8), rounded down to whole splits so the grid is one wave: a grid just
+    // past one wave runs a second wave as long as the first; each warp at least
+    // one chunk of positions
+    const int resident = G <= 4 ? 4 : 3;
+    const int64_t want = static_cast<int64_t>(d->sms) * resident / pairs;
     const int cp = 32 / G < 8 ? 32 / G : 8;
     const int64_t most = (static_cast<int64_t>(kv_max) + cp * kAttnWarps - 1) / (cp * kAttnWarps);
     pl.splits = static_cast<int>(want < most ? want : (most > 0 ? most : 1));
