@@ -46,7 +46,10 @@
 namespace oomb {
 
 constexpr int kTgMaxExperts = 4096;  // groups per launch (their chunk prefix sits in shared memory)
-constexpr int kTgLag = 3;            // weight tiles in flight before the oldest is released (< stages)
+#ifndef OOMB_TG_LAG
+#define OOMB_TG_LAG 3
+#endif
+constexpr int kTgLag = OOMB_TG_LAG;  // weight tiles in flight before the oldest is released (< stages)
 
 enum : unsigned {
     ERR_TG_WAIT = 0x580,  // a grouped tensor-core pipeline wait ran out (+ the waiting role)
