@@ -163,10 +163,17 @@ __device__ __forceinline__ void bar_arrive(unsigned* ctr) {
 
 // One thread per CTA: polls the arrival count at ctr (acquire) until it reaches
 // n.  False when the wait ran out (the error code is recorded).
+// Pause between polls of a grid barrier's count: one thread of every CTA polls
+// the same line that every CTA's arrival updates.  Measured on B200, config 2
+// batch 1: 23.50 us a step polling back to back, 23.15 with 64 or 200 ns.
+#ifndef OOMB_BAR_BACKOFF_NS
+#define OOMB_BAR_BACKOFF_NS 64
+#endif
 __device__ __forceinline__ bool bar_wait(const unsigned* ctr, unsigned n, unsigned* err, unsigned code) {
     if (ld_acquire_u32(ctr) >= n) return true;
     const unsigned long long t0 = global_ns(), limit = wait_limit();
     while (ld_acquire_u32(ctr) < n) {
+        if (OOMB_BAR_BACKOFF_NS > 0) __nanosleep(OOMB_BAR_BACKOFF_NS);
         if (global_ns() - t0 > limit) {
             record_error(err, code);
             return false;
