@@ -473,8 +473,8 @@ def run_ours(args, rank, world, local_rank):
     # the stand-alone gate/up kernel is timed beside it ----
     step_bytes = E * H * 2 + 8 * B * weight_bytes(layers[0][0].geo) + 2 * B * H * 2
     chain_env = os.environ.get("OOMB_DECODE_CHAIN") == "1"
-    fused = world == 1 and B < 12 and not chain_env     # one decode_kernel launch a step
-    tiled = world == 1 and B >= 12 and not chain_env     # route, 2 splits, 3 grouped GEMMs, SwiGLU, combine
+    fused = world == 1 and B <= 16 and not chain_env     # one decode_kernel launch a step
+    tiled = world == 1 and B > 16 and not chain_env      # route, 2 splits, 3 grouped GEMMs, SwiGLU, combine
     roof = measure_gate_up(gpu, layers, dev, s, B, LAYERS)
     gemv1 = measure_gemv_config1(gpu, dev, s)
     del layers
@@ -528,7 +528,7 @@ def run_ours(args, rank, world, local_rank):
             "ep_config5": ep5,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
-            # per step: one decode_kernel below 12 tokens; from 12 tokens the grouped
+            # per step: one decode_kernel up to 16 tokens; from 17 tokens the grouped
             # tensor-core path (route, split x, gate, up, SwiGLU, split h, down, combine);
             # the chain route, gate/up, down, combine with OOMB_DECODE_CHAIN=1;
             # expert-parallel over peer memory: one launch per rank (fused), or router

@@ -38,6 +38,11 @@
 // correct: an expert kernel lets its dependent launch only after its own
 // dependency wait, so a kernel reading tables two launches back finds them
 // complete whatever the occupancy.
+// Single-GPU one-launch steps of 2 .. OOMB_DECODE_SINGLES_MAX_T tokens group every
+// slot on its own (see fused_decode_plan).
+#ifndef OOMB_DECODE_SINGLES_MAX_T
+#define OOMB_DECODE_SINGLES_MAX_T 16
+#endif
 #ifndef OOMB_MOE_CTAS_PER_SM
 #define OOMB_MOE_CTAS_PER_SM 2
 #endif
@@ -520,14 +525,16 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     if (t < 1 || t > kDecodeMaxT || E > kRouteSmallE || H > kRouteMaxH) return false;
     const int TA = ranks > 0 ? ranks * t : t;  // tokens whose slots this rank groups
     if (ranks > 0 && (E % ranks || E / ranks > kThreads)) return false;
-    // expert parallelism groups every received slot on its own: one assignment per group
-    const TbP tp = ranks > 0 ? TbP{1, false} : tb_p(TA);
+    // expert parallelism groups every received slot on its own, and so does a
+    // single-GPU step of up to OOMB_DECODE_SINGLES_MAX_T tokens: one assignment per group
+    const bool singles = ranks == 0 && t > 1 && t <= OOMB_DECODE_SINGLES_MAX_T;
+    const TbP tp = ranks > 0 || singles ? TbP{1, false} : tb_p(TA);
     f.tb = tp.chunked ? 2 : tp.tb;
     f.p = f.tb == 1 ? pass_len<1>() : 1;
     const StreamPlan pg = stream_plan(H, 2, f.p, layout), pd = stream_plan(I, 1, f.p, layout);
     if (pg.stage_bytes > kStageBytes || pd.stage_bytes > kStageBytes) return false;
     const int gpe_g = (I + pg.rpp - 1) / pg.rpp, gpe_d = (H + pd.rpp - 1) / pd.rpp;
-    const int64_t groups_max = ranks > 0 && static_cast<int64_t>(TA) * K > E ? static_cast<int64_t>(TA) * K : E;
+    const int64_t groups_max = static_cast<int64_t>(TA) * K > E ? static_cast<int64_t>(TA) * K : E;
     if (gpe_d > kDecodeMaxGroups || groups_max * (gpe_g > gpe_d ? gpe_g : gpe_d) * 1025 >= (int64_t{1} << 32))
         return false;
     const int slot = pg.slot_bytes > pd.slot_bytes ? pg.slot_bytes : pd.slot_bytes;
@@ -595,7 +602,8 @@ bool fused_decode_plan(const DeviceState* d, const oomb_moe_layer* L, int t, boo
     // at most four 512-column slabs; a slot's 8 rows fit a ring slot; a group's
     // stages fit the ring at once, since its consumers release them together)
     const Down1 d1 = down1_plan(K, I, slot);
-    q.dn1 = OOMB_DECODE_DOWN1 && ranks == 0 && f.tb == 1 && I <= 2048 && d1.spp >= 1 && d1.nst <= stages;
+    q.dn1 = OOMB_DECODE_DOWN1 && ranks == 0 && t == 1 && I <= 2048 && d1.spp >= 1 && d1.nst <= stages;
+    q.singles = singles ? 1 : 0;
     return true;
 }
 
@@ -1106,7 +1114,10 @@ struct DecodeLayout {
 // (route, split x once, gate and up, SwiGLU, split h, down, combine) when the
 // layer's shapes allow it; below it the one-launch kernel (or the CUDA-core chain).
 // The environment variable OOMB_DECODE_TILED_MIN_T overrides it (>= 2).
-constexpr int kDecodeTiledMinT = 12;  // measured crossover: configs 2 and 4 at 8 tokens tie, at 16 the tensor cores win 1.2-1.9x
+// Measured on B200 with the one-launch kernel grouping every slot on its own: config 2
+// at 16 tokens 205 us one launch vs 265 us tensor cores, config 4 401 vs 430 us at 14 and
+// a tie at 16; so the tensor cores from 17 tokens, where the one-launch kernel ends.
+constexpr int kDecodeTiledMinT = 17;
 
 int decode_tiled_min_t() {
     const char* env = getenv("OOMB_DECODE_TILED_MIN_T");

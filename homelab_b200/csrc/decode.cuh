@@ -17,7 +17,10 @@
 //      CTA loads all T x E logits into shared memory;
 //   3. softmax top-k and grouping of all tokens from the logits, the same in
 //      every CTA (deterministic), into shared-memory routing tables: no
-//      second hand-off through global memory;
+//      second hand-off through global memory.  From two tokens (p.singles) every
+//      slot is a group of its own, so the streaming phases keep their one-token
+//      form (an expert picked twice streams twice; measured on B200 at config 2,
+//      8 tokens: 95 us a step against 158 grouped by expert with two-token units);
 //   4. the streaming engine over the CTA's slice of gate/up units, then of down
 //      units, through one weight ring: the copy producer runs straight on from
 //      gate/up into down, so the down weights stream in while gate/up finishes
@@ -91,6 +94,7 @@ struct DecodeParams {
     EpPeer ep;
     int epr;
     int dn1;  // one token: the down phase and the combine run per row group in one CTA (down1_*)
+    int singles;  // every slot a group of its own (the one-token streaming form for a few tokens)
 };
 
 // Routing tables in shared memory (byte offsets from the table area).
@@ -207,6 +211,37 @@ __device__ void group_singletons(const RouteParams& p, const GroupOut& g, const 
             g.assign_ret[idx] = i;
             g.recs_active[idx] = recs_sm[e];
         }
+        run += __popc(vm);
+    }
+    if (lane == 0) {
+        g.off[run] = run;
+        *g.n_active = run;
+    }
+}
+
+// Every slot of the step a group of its own, in slot order (one warp; all its
+// lanes call this): group i = slot i, so each group holds one assignment and the
+// streaming phases run their one-token form; an expert picked by two slots
+// streams twice.  A slot with an invalid expert id is recorded as an error and
+// left out.
+__device__ void group_slots(const RouteParams& p, const GroupOut& g, const int32_t* ids_sm, const uint64_t* recs_sm) {
+    const int lane = threadIdx.x & 31;
+    const int n = p.T * p.K;
+    int run = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const int e = i < n ? ids_sm[i] : -1;
+        const bool valid = i < n && e >= 0 && e < p.E;
+        if (i < n && !valid) record_error(p.err, ERR_BAD_TABLE);
+        const unsigned vm = __ballot_sync(0xffffffffu, valid);
+        const int idx = run + __popc(vm & ((1u << lane) - 1u));
+        if (valid) {
+            g.active[idx] = e;
+            g.off[idx] = idx;
+            g.assign_tok[idx] = i / p.K;
+            g.recs_active[idx] = recs_sm[e];
+        }
+        if (i < n) g.slot_assign[i] = valid ? idx : 0;
         run += __popc(vm);
     }
     if (lane == 0) {
@@ -631,7 +666,9 @@ __global__ void __launch_bounds__(kThreads, OOMB_STREAM_CTAS_PER_SM) decode_kern
         } else {
             const GroupOut go{n_active, reinterpret_cast<int32_t*>(tabs + dt.active), off_sm, assign_tok, slot_sm,
                               recs_active, nullptr};
-            if (A <= 32) {
+            if (p.singles) {
+                if (warp == 0) group_slots(p.r, go, ids_sm, recs_sm);
+            } else if (A <= 32) {
                 if (warp == 0) group_warp(p.r, go, ids_sm, recs_sm);
             } else {
                 group_assignments<kThreads>(p.r, go, ids_sm, reinterpret_cast<int32_t*>(tabs + dt.counts),

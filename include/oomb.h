@@ -283,8 +283,9 @@ int oomb_kv_append(const void* src, int src_dtype, int64_t src_row_stride, uint1
  * The workspace must hold oomb_moe_decode_workspace_bytes(t, layer) bytes and
  * be zeroed once before first use (oomb_workspace_clear), and again after a
  * device error (oomb_device_error); calls that share a workspace must be
- * ordered on one stream.  Paths: below 12 tokens (up to 256 experts) the step
- * is one persistent launch on the CUDA cores; from 12 tokens, when hidden and
+ * ordered on one stream.  Paths: up to 16 tokens (up to 256 experts) the step
+ * is one persistent launch on the CUDA cores (from 2 tokens every slot streams
+ * as a group of its own); from 17 tokens, when hidden and
  * intermediate are multiples of 128 and hidden >= 2 * intermediate, it is the
  * grouped tensor-core path (route, the token rows split once into e4m3 terms,
  * gate and up, SwiGLU, down, combine: the same bits as oomb_moe_tiled_fp8 for

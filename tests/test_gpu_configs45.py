@@ -5,8 +5,8 @@ Config 4: hidden 4096, 64 experts, top-6, intermediate 1408.  Config 5: hidden
 128x128 block scales, bf16 activations ~N(0, 1), router ~N(0, 0.02).  Bars:
 top-k ids and weights bit-exact with the oracle; outputs within 1e-4 of the
 float64 experts (relative to the largest) and within BASELINE's max relative
-error 1e-3; below 12 tokens the one-launch step and the chain of kernels give
-the same bits, from 12 tokens the grouped tensor-core path agrees with the chain
+error 1e-3; up to 16 tokens the one-launch step and the chain of kernels give
+the same bits, from 17 tokens the grouped tensor-core path agrees with the chain
 to 1e-5; every expert-parallel rank (virtual ranks on one GPU, G = 2, 4, 8)
 gives the bits of the single-GPU decode on the same CUDA-core kernels.
 """
@@ -83,7 +83,7 @@ def decode(gpu, lay, xd, t, chain=False, out_dtype=torch.float32):
 
 
 @pytest.mark.parametrize("config", [4, 5])
-@pytest.mark.parametrize("t", [1, 4, 16])
+@pytest.mark.parametrize("t", [1, 4, 16, 32])
 def test_decode_matches_oracle(gpu, layers, config, t):
     lay = layers[config]
     H, E, K, I = lay["shape"]
@@ -96,7 +96,7 @@ def test_decode_matches_oracle(gpu, layers, config, t):
     assert np.array_equal(ids.cpu().numpy(), want_ids)
     assert np.array_equal(wts.cpu().numpy().view(np.uint32), want_w.view(np.uint32))
     assert torch.equal(ids, ids_c) and torch.equal(wts, wts_c)
-    if t < 12:
+    if t <= 16:
         assert torch.equal(out, out_c), "one launch and the kernel chain differ"
     else:  # the grouped tensor-core path sums in another order
         rel_c = ((out - out_c).abs().max() / out_c.abs().max()).item()

@@ -260,18 +260,23 @@ def test_pageable_host_memory_is_refused(gpu):
 
 @pytest.mark.parametrize("name,xbf16,t", [("small", True, 12), ("small", False, 16), ("wide", True, 12)])
 def test_tiled_decode_equals_tiled_calls_and_float64(gpu, name, xbf16, t):
-    """From 12 tokens the decode step runs the grouped tensor-core path: route, x
-    split once for gate and up, SwiGLU, down, combine.  Its bits equal the public
-    calls in that order (oomb_moe_tiled_fp8 for gate, up and down,
-    oomb_moe_swiglu_range, oomb_moe_combine_slots on the same routing), and it is
-    within 1e-4 of the float64 step."""
+    """From 17 tokens (here from 12, forced with OOMB_DECODE_TILED_MIN_T) the decode
+    step runs the grouped tensor-core path: route, x split once for gate and up,
+    SwiGLU, down, combine.  Its bits equal the public calls in that order
+    (oomb_moe_tiled_fp8 for gate, up and down, oomb_moe_swiglu_range,
+    oomb_moe_combine_slots on the same routing), and it is within 1e-4 of the
+    float64 step."""
     lay = get_layer(gpu, name)
     L = lay["L"]
     H, E, K, I = L.hidden, L.experts, L.top_k, L.geo.inter
     if H % 128 or I % 128 or H < 2 * I:
         pytest.skip("layer shape outside the grouped tensor-core path")
     x = make_x(H, t, xbf16, 1500 + t)
-    out, ids, wts = run(gpu, lay, x, t, torch.float32, chain=False)
+    os.environ["OOMB_DECODE_TILED_MIN_T"] = "12"
+    try:
+        out, ids, wts = run(gpu, lay, x, t, torch.float32, chain=False)
+    finally:
+        os.environ.pop("OOMB_DECODE_TILED_MIN_T", None)
     torch.cuda.synchronize()
     x32 = x.float().cpu().numpy()
     want_ids, want_w = O.router_topk(O.router_logits(x32, lay["router"].reshape(E, H)), K)

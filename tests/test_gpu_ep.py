@@ -3,7 +3,7 @@
 The virtual ranks share the device; their all-to-alls are tensor copies
 (exchange_local).  Every rank's output must equal, bit for bit, the rows of the
 single-GPU decode (oomb_moe_decode_fp8) of the whole batch on the same CUDA-core
-expert kernels (OOMB_DECODE_CHAIN=1: batches of 12 and more otherwise take the
+expert kernels (OOMB_DECODE_CHAIN=1: batches of 17 and more otherwise take the
 grouped tensor-core path, whose summation order differs), and an expert's
 output for an assignment must not depend on which other assignments share its
 launch.

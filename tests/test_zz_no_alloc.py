@@ -6,8 +6,8 @@ some hosts have no device allocator at the call site): it runs the fused
 decode step with its scratch in one fixed device array inside liboomb.so
 instead of a caller workspace.  The same kernels run on the same inputs, so
 two calls in a row must each reproduce the workspace entry point's ids,
-weights and outputs bit for bit, for one-launch batches (t < 12) and for the
-grouped tensor-core path (t >= 12, whose self-resetting route ticket and split
+weights and outputs bit for bit, for one-launch batches (t <= 16) and for the
+grouped tensor-core path (t >= 17, whose self-resetting route ticket and split
 activations live in the shared array).  A call that needs more than the array holds is refused before
 any launch, and after a bounded device wait has run out, clearing the error
 zeroes the array's sync words so the next calls are again exact.  This file is
