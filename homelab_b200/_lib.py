@@ -90,6 +90,8 @@ SIGNATURES = [
     ("oomb_pack_fp8_tiles", I, [P, I, I, P, S]),
     ("oomb_silu_mul_rows", I, [P, P, I, I, I, S]),
     ("oomb_moe_experts_fp8", I, [P, P, P, P, I, P, I, P, P, C.POINTER(Fp8Record), I, S]),
+    ("oomb_moe_experts_tiled_fp8_workspace_bytes", Z, [I, C.POINTER(Fp8Record), I]),
+    ("oomb_moe_experts_tiled_fp8", I, [P, P, P, P, I, I, P, I, P, P, C.POINTER(Fp8Record), I, P, Z, S]),
     ("oomb_ep_meta", I, [P, I, I, I, I, P, S]),
     ("oomb_ep_group", I, [P, I, I, I, I, P, P, P, P, P, P, S]),
     ("oomb_ep_scatter", I, [P, P, P, P, I, I, P, S]),

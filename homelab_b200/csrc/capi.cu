@@ -1619,6 +1619,85 @@ int oomb_moe_experts_fp8(const uint64_t* recs_active, const int32_t* off, const 
     return launch_down(d, recs_active, off, n_active, 0, max_active, h, y, geo, maxn, true, stream);
 }
 
+size_t oomb_moe_experts_tiled_fp8_workspace_bytes(int max_assignments, const oomb_fp8_record* geo, int x_dtype) {
+    if (max_assignments <= 0 || !geo || (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16)) return 0;
+    const int H = static_cast<int>(geo->hidden), I = static_cast<int>(geo->inter);
+    if (H <= 0 || I <= 0 || H % kTcTile || I % kTcTile || H < 2 * I) return 0;
+    // x split for gate and up, then h (fp32: six terms) for down, one after the other
+    const size_t a = xs_layout(0, max_assignments * tc_ts(x_dtype == OOMB_BF16), H).end;
+    const size_t b = xs_layout(0, max_assignments * tc_ts(false), I).end;
+    return a > b ? a : b;
+}
+
+int oomb_moe_experts_tiled_fp8(const uint64_t* recs_active, const int32_t* off, const int32_t* assign_tok,
+                               const int32_t* n_active, int max_active, int max_assignments, const void* x,
+                               int x_dtype, float* h, float* y, const oomb_fp8_record* geo, int max_per_expert,
+                               void* workspace, size_t workspace_bytes, oomb_stream stream) {
+    if (!recs_active || !off || !assign_tok || !n_active || !x || !h || !y || !geo || !workspace) return OOMB_E_ARG;
+    if (x_dtype != OOMB_F32 && x_dtype != OOMB_BF16) return OOMB_E_ARG;
+    if (geo->layout != OOMB_SCALE_1X128 && geo->layout != OOMB_SCALE_128X128) return OOMB_E_ARG;
+    const int H = static_cast<int>(geo->hidden), I = static_cast<int>(geo->inter);
+    if (max_active <= 0 || max_active > kTgMaxExperts || max_assignments <= 0 || max_per_expert <= 0 || H <= 0 ||
+        I <= 0 || H % kTcTile || I % kTcTile || H < 2 * I || H > 4096 || I > 4096)
+        return OOMB_E_SHAPE;
+    if (!aligned16(x) || !aligned16(h) || !aligned16(y) || !aligned16(workspace)) return OOMB_E_ALIGN;
+    const size_t need = oomb_moe_experts_tiled_fp8_workspace_bytes(max_assignments, geo, x_dtype);
+    if (need == 0) return OOMB_E_SHAPE;
+    if (workspace_bytes < need) return OOMB_E_WORKSPACE;
+    const DeviceState* d = device_state();
+    if (!d) return OOMB_E_DEVICE;
+    const bool xb = x_dtype == OOMB_BF16;
+    const int A = max_assignments;
+    uint8_t* xsr = static_cast<uint8_t*>(workspace);
+    // g and u in y (H >= 2I), whose rows down overwrites only after SwiGLU has read them;
+    // the assignment count is off[*n_active] on the device: the splits cover A rows and
+    // skip the ones past it
+    float* g = y;
+    float* u = y + static_cast<size_t>(A) * I;
+    const XsLayout xl1 = xs_layout(0, A * tc_ts(xb), H);
+    XsParams xp{};
+    xp.x = x;
+    xp.rows = assign_tok;
+    xp.count = off;
+    xp.count_idx = n_active;
+    xp.a_host = A;
+    xp.a_cover = A;
+    xp.K = H;
+    xp.kblocks = H / kTcTile;
+    xp.xs = xsr + xl1.xs_off;
+    xp.rows_alloc = xl1.rows_alloc;
+    xp.sx = reinterpret_cast<float*>(xsr + xl1.sx_off);
+    xp.sx_stride = xl1.sx_stride;
+    int rc = launch_xsplit(xb, xp, stream);
+    if (rc) return rc;
+    if ((rc = tiled_projection(d, recs_active, off, n_active, max_active, max_per_expert, A, xb, xsr, xl1, g, I, H,
+                               geo->gate_weight, geo->gate_scale, geo->layout, stream)))
+        return rc;
+    if ((rc = tiled_projection(d, recs_active, off, n_active, max_active, max_per_expert, A, xb, xsr, xl1, u, I, H,
+                               geo->up_weight, geo->up_scale, geo->layout, stream)))
+        return rc;
+    const int64_t n_h = static_cast<int64_t>(A) * I;
+    if ((rc = launch(swiglu_range_kernel, dim3(static_cast<unsigned>((n_h + 255) / 256)), dim3(256), 0, stream,
+                     static_cast<const float*>(g), static_cast<const float*>(u), h, int64_t{0}, n_h)))
+        return rc;
+    const XsLayout xl2 = xs_layout(0, A * tc_ts(false), I);
+    xp = XsParams{};
+    xp.x = h;
+    xp.count = off;
+    xp.count_idx = n_active;
+    xp.a_host = A;
+    xp.a_cover = A;
+    xp.K = I;
+    xp.kblocks = I / kTcTile;
+    xp.xs = xsr + xl2.xs_off;
+    xp.rows_alloc = xl2.rows_alloc;
+    xp.sx = reinterpret_cast<float*>(xsr + xl2.sx_off);
+    xp.sx_stride = xl2.sx_stride;
+    if ((rc = launch_xsplit(false, xp, stream))) return rc;
+    return tiled_projection(d, recs_active, off, n_active, max_active, max_per_expert, A, false, xsr, xl2, y, H, I,
+                            geo->down_weight, geo->down_scale, geo->layout, stream);
+}
+
 int oomb_ep_scatter(const float* y, const int32_t* n_active, const int32_t* off, const int32_t* assign_ret, int h,
                     int max_rows, float* ret, oomb_stream stream) {
     if (!y || !n_active || !off || !assign_ret || !ret) return OOMB_E_ARG;

@@ -228,6 +228,7 @@ struct XsParams {
     const int32_t* rows;   // [A] activation row of each assignment, or null (row = assignment)
     const int32_t* first;  // device word holding the first assignment to split (the first CSR offset), or null: 0
     const int32_t* count;  // device word holding A (the last CSR offset), or null: A = a_host
+    const int32_t* count_idx;  // with count: A = count[*count_idx] (a CSR whose group count is on the device)
     int a_host;
     int a_cover;           // assignments the grid covers (>= A)
     int zero_pad;          // rows of assignments in [A, a_cover) are written as zero terms
@@ -249,7 +250,7 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const XsParams p) {
     const int64_t w = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
     if (w >= static_cast<int64_t>(p.a_cover) * p.kblocks) return;
     const int a = static_cast<int>(w / p.kblocks), kb = static_cast<int>(w - static_cast<int64_t>(a) * p.kblocks);
-    const int A = p.count ? __ldcg(p.count) : p.a_host;
+    const int A = p.count ? __ldcg(p.count + (p.count_idx ? __ldcg(p.count_idx) : 0)) : p.a_host;
     if ((a >= A && !p.zero_pad) || (p.first && a < __ldcg(p.first))) return;
     float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (a < A) {

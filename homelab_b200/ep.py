@@ -35,6 +35,11 @@ import torch.distributed as dist
 from . import _lib
 from ._lib import BF16, F32, check
 
+# Tokens over all ranks (ranks x t) from which the peer chain runs its local
+# experts on the tensor cores (oomb_moe_experts_tiled_fp8), as the single-GPU
+# decode step does from 17 tokens.
+EP_TILED_MIN_TOKENS = 17
+
 
 class EpGpuOps:
     """The device steps of an expert-parallel layer on liboomb.so."""
@@ -66,6 +71,23 @@ class EpGpuOps:
         check(self.L.oomb_moe_experts_fp8(recs_active.data_ptr(), off.data_ptr(), assign_row.data_ptr(),
                                           n_active.data_ptr(), max_active, x.data_ptr(), xd, h.data_ptr(),
                                           y.data_ptr(), C.byref(geo), max_per_expert, self._s()), "moe_experts")
+
+    def experts_tiled(self, recs_active, off, assign_row, n_active, max_active, max_assignments, x, h, y, geo,
+                      max_per_expert, ws):
+        """The same step on the tensor cores (oomb_moe_experts_tiled_fp8); ws from
+        tiled_workspace."""
+        xd = BF16 if x.dtype == torch.bfloat16 else F32
+        check(self.L.oomb_moe_experts_tiled_fp8(recs_active.data_ptr(), off.data_ptr(), assign_row.data_ptr(),
+                                                n_active.data_ptr(), max_active, max_assignments, x.data_ptr(), xd,
+                                                h.data_ptr(), y.data_ptr(), C.byref(geo), max_per_expert,
+                                                ws.data_ptr(), ws.numel(), self._s()), "moe_experts_tiled")
+
+    def tiled_workspace(self, max_assignments, geo, x_dtype=torch.bfloat16):
+        """The workspace of experts_tiled, or None when the layer's shapes are
+        outside the tensor-core path."""
+        xd = BF16 if x_dtype == torch.bfloat16 else F32
+        n = self.L.oomb_moe_experts_tiled_fp8_workspace_bytes(max_assignments, C.byref(geo), xd)
+        return torch.empty(n, dtype=torch.uint8, device=self.device) if n else None
 
     def scatter(self, y, n_active, off, assign_ret, hidden, max_rows, ret):
         check(self.L.oomb_ep_scatter(y.data_ptr(), n_active.data_ptr(), off.data_ptr(), assign_ret.data_ptr(),
@@ -295,6 +317,8 @@ class EpPeerMoeLayer:
         self.recs_active = torch.zeros(self.epr, dtype=torch.int64, device=dev)
         self.h = torch.empty((A, inter), **f32)
         self.y = torch.empty((A, hidden), **f32)
+        # from EP_TILED_MIN_TOKENS tokens over the ranks the local experts run on the tensor cores
+        self.tiled_ws = ops.tiled_workspace(A, geo, mailboxes.x_dtype) if G * T >= EP_TILED_MIN_TOKENS else None
 
     def _s(self):
         return torch.cuda.current_stream(self.router_w.device).cuda_stream
@@ -315,8 +339,12 @@ class EpPeerMoeLayer:
               "ep_group_peer")
         G, K = self.G, self.K
         max_active = min(self.epr, G * t * K)
-        self.ops.experts(self.recs_active, self.off, self.assign_row, self.n_active, max_active,
-                         self.mb.recv_x(self.rank, t), self.h, self.y, self.geo, G * t)
+        if self.tiled_ws is not None and G * t >= EP_TILED_MIN_TOKENS:
+            self.ops.experts_tiled(self.recs_active, self.off, self.assign_row, self.n_active, max_active, G * t * K,
+                                   self.mb.recv_x(self.rank, t), self.h, self.y, self.geo, G * t, self.tiled_ws)
+        else:
+            self.ops.experts(self.recs_active, self.off, self.assign_row, self.n_active, max_active,
+                             self.mb.recv_x(self.rank, t), self.h, self.y, self.geo, G * t)
         check(self.L.oomb_ep_return_peer(C.byref(self.q), self.y.data_ptr(), self.n_active.data_ptr(),
                                          self.off.data_ptr(), self.assign_ret.data_ptr(), t, G * t * K, self._s()),
               "ep_return_peer")

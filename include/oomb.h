@@ -378,6 +378,22 @@ int oomb_moe_experts_fp8(const uint64_t* recs_active, const int32_t* off, const 
                          const int32_t* n_active, int max_active, const void* x, int x_dtype, float* h, float* y,
                          const oomb_fp8_record* geo, int max_per_expert, oomb_stream stream);
 
+/* The same step on the tensor cores, for many assignments per expert (the
+ * reference's Moe::run_group takes its tiled branch there, moe.rs:746-758): the
+ * activation rows split once into e4m3 terms, gate and up by oomb_moe_tiled_fp8's
+ * kernel (into y, which needs hidden >= 2 * intermediate), SwiGLU into h, h split,
+ * down into y.  The groups' count stays on the device (n_active); max_assignments
+ * bounds off[n_active] and sizes the workspace
+ * (oomb_moe_experts_tiled_fp8_workspace_bytes); max_per_expert bounds any group
+ * (> 0).  hidden and intermediate are multiples of 128.  Within the tensor-core
+ * path's tolerance of oomb_moe_experts_fp8 (another summation order); an output's
+ * bits do not depend on the other assignments of the launch. */
+size_t oomb_moe_experts_tiled_fp8_workspace_bytes(int max_assignments, const oomb_fp8_record* geo, int x_dtype);
+int oomb_moe_experts_tiled_fp8(const uint64_t* recs_active, const int32_t* off, const int32_t* assign_tok,
+                               const int32_t* n_active, int max_active, int max_assignments, const void* x,
+                               int x_dtype, float* h, float* y, const oomb_fp8_record* geo, int max_per_expert,
+                               void* workspace, size_t workspace_bytes, oomb_stream stream);
+
 /* ---- expert parallelism (experts sharded over ranks) --------------------- */
 /* No counterpart in the reference, which runs on one device (its experts are
  * tiered, not sharded).  Expert e lives on rank e / experts_per_rank.  A step:

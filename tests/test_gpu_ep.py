@@ -198,3 +198,30 @@ def test_one_launch_expert_parallel_takes_pinned_host_buffers(layer):
         torch.cuda.synchronize()
         assert torch.equal(oh, want.cpu()), f"step {step}"
     mb.close()
+
+
+@pytest.mark.parametrize("G,t", [(2, 16), (4, 8)])
+def test_peer_expert_parallel_on_tensor_cores_matches_single_gpu(layer, G, t):
+    """From 17 tokens over the ranks the chain over peer memory runs its local
+    experts on the tensor cores (oomb_moe_experts_tiled_fp8); the single-GPU decode
+    of the whole batch takes its tensor-core path too.  Routing and outputs
+    bit-exact: an output's bits depend neither on the chunking of its expert's
+    assignments nor on which other assignments share the launch."""
+    from homelab_b200.ep import EP_TILED_MIN_TOKENS
+    assert G * t >= EP_TILED_MIN_TOKENS
+    gpu, L = layer["gpu"], layer["L"]
+    T = G * t
+    xs = [torch.from_numpy(O.normal_bf16(900 + 7 * G + t + i, T * H).view(np.int16)).to(DEV).view(torch.bfloat16)
+          .view(T, H) for i in range(2)]
+    ws = gpu.moe_decode_workspace(L, T)
+    results = run_virtual_peer(layer, xs, G, t)
+    for x, (outs, routing) in zip(xs, results):
+        want = torch.empty((T, H), dtype=torch.float32, device=DEV)
+        ids = torch.empty((T, K), dtype=torch.int32, device=DEV)
+        wts = torch.empty((T, K), dtype=torch.float32, device=DEV)
+        gpu.moe_decode(L, x, T, want, ws, ids, wts)
+        torch.cuda.synchronize()
+        got = torch.cat(outs)
+        for g in range(G):
+            assert torch.equal(routing[g][0], ids[g * t:(g + 1) * t])
+        assert torch.equal(got, want), "expert-parallel tensor-core step differs from one GPU"
