@@ -175,3 +175,22 @@ def test_new_entry_points_check_arguments():
     assert L.oomb_moe_layer_workspace_bytes(1, C.byref(layer), C.byref(sh), _lib.BF16) == 0
     assert L.oomb_moe_layer_decode_fp8(C.byref(layer), C.byref(sh), fake, 1, 1, fake, 1, None, None, fake, 1 << 30,
                                        None) == _lib.E_SHAPE
+
+
+def test_tensor_core_expert_entry_checks_arguments():
+    L = hb.lib()
+    fake = 0x10000
+    from homelab_b200.records import record_layout
+    geo, _ = record_layout(2048, 768)
+    assert L.oomb_moe_experts_tiled_fp8_workspace_bytes(64, C.byref(geo), _lib.BF16) > 0
+    narrow, _ = record_layout(1024, 768)  # hidden < 2 * intermediate: g and u do not fit in y
+    assert L.oomb_moe_experts_tiled_fp8_workspace_bytes(64, C.byref(narrow), _lib.BF16) == 0
+    odd, _ = record_layout(2048, 720)  # intermediate not a multiple of 128
+    assert L.oomb_moe_experts_tiled_fp8_workspace_bytes(64, C.byref(odd), _lib.BF16) == 0
+    # a workspace is required, and must be large enough
+    assert L.oomb_moe_experts_tiled_fp8(fake, fake, fake, fake, 8, 64, fake, _lib.BF16, fake, fake, C.byref(geo), 8,
+                                        None, 0, None) == _lib.E_ARG
+    assert L.oomb_moe_experts_tiled_fp8(fake, fake, fake, fake, 8, 64, fake, _lib.BF16, fake, fake, C.byref(geo), 8,
+                                        fake, 16, None) == _lib.E_WORKSPACE
+    assert L.oomb_moe_experts_tiled_fp8(fake, fake, fake, fake, 8, 64, fake, _lib.BF16, fake, fake, C.byref(narrow),
+                                        8, fake, 1 << 30, None) == _lib.E_SHAPE

@@ -167,3 +167,35 @@ def test_silu_mul_rows_matches_float64(gpu, out_bf16):
     got = y.float().cpu().numpy()
     rel = np.abs(got - want).max() / np.abs(want).max()
     assert rel <= (2 ** -8 if out_bf16 else 1e-6), rel
+
+
+def test_gemm_fp8_entry_reaches_the_tensor_cores_with_a_workspace(gpu):
+    """The drop-in oomb_gemm_fp8 (Linear::gemm_fp8's counterpart, through ctypes)
+    at 4 tokens: given a workspace it launches the activation split and the
+    tcgen05 GEMM, without one the CUDA-core stream kernel (kernel names from the
+    CUDA activity trace), and both give the same y within the fp32 bound."""
+    from torch.profiler import ProfilerActivity, profile
+    t, n, k = 4, 1024, 2048
+    w = O.normal_bf16(71, n * k, 0.0, 0.02)
+    q, s = gpu.quantize_fp8(dev(w.view(np.int16)), n, k, SCALE_128X128)
+    x = dev(O.normal_bf16(72, t * k).view(np.int16)).view(torch.bfloat16).view(t, k)
+    ws = gpu.gemm_fp8_workspace(t, n, k)
+    y_tc = torch.empty((t, n), dtype=torch.float32, device=DEV)
+    y_cc = torch.empty_like(y_tc)
+    gpu.gemm_fp8(x, q, s, y_tc, t, n, k, SCALE_128X128, ws)  # first call outside the trace
+    torch.cuda.synchronize()
+
+    def kernels(fn):
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        return [e.key for e in prof.key_averages()]
+
+    with_ws = kernels(lambda: gpu.gemm_fp8(x, q, s, y_tc, t, n, k, SCALE_128X128, ws))
+    without = kernels(lambda: gpu.gemm_fp8(x, q, s, y_cc, t, n, k, SCALE_128X128))
+    assert any("tc_gemm_kernel" in nm for nm in with_ws), with_ws
+    assert any("xsplit_kernel" in nm for nm in with_ws), with_ws
+    assert not any("tc_gemm_kernel" in nm for nm in without), without
+    assert any("stream_kernel" in nm for nm in without), without
+    bound = FP32_BOUND * (x.float().abs() @ (torch.from_numpy(O.bf16_to_f32(w)).to(DEV).view(n, k).abs().t())).max()
+    assert (y_tc - y_cc).abs().max().item() <= 2 * bound.item()
